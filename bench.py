@@ -1,0 +1,369 @@
+"""Benchmark of the WKV-7 / quantised-GEMV hot paths on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0).  Under torchrun (N > 1) every rank runs its own
+replica of the workload (the paths shard with no exchange), timing is the max
+over ranks and `value` counts the units of all ranks.
+
+Workloads (synthetic, seeded 0x5EED2026):
+  wkv7     config 1 -- WKV-7 operator forward, B=1 T=1024 H=12 N=64 fp32,
+           tok/s = B*T per step.  Inputs (22 MB) are smaller than L2, so L2 is
+           flushed (a 256 MB write) before every timed step, outside the timed
+           interval.
+  gemv     config 2 -- 4-bit g64 GEMV over the four 1.5B projection shapes,
+           rows 1, fp16 activations; GB/s of the packed weight stream.
+`--impl reference` times the CPU oracle (the reference's Metal/MLX path
+cannot run here) on the same workload and metric, on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+SEED = 0x5EED2026
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ---------------------------------------------------------------- clock sampling
+
+class ClockSampler:
+    """nvidia-smi SM clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# -------------------------------------------------------------------- workloads
+
+def config1_inputs(rng, B=1, T=1024, H=12, N=64):
+    def n():
+        return rng.standard_normal((B, T, H, N)).astype(np.float32)
+    r, k, v = n(), n(), n()
+    u = -np.logaddexp(0, -n()) - 0.5
+    w = np.exp(-np.exp(u)).astype(np.float32)
+    kk = n()
+    kk /= np.sqrt((kk * kk).sum(-1, keepdims=True))
+    a = (-kk).astype(np.float32)
+    b = (kk / (1 + np.exp(-n()))).astype(np.float32)
+    return [r, w, k, v, a, b]
+
+
+class WKV7Prefill:
+    name = "wkv7"
+    metric = "WKV-7 prefill tok/s (config 1 operator forward, B=1 T=1024 H=12 N=64 fp32)"
+    unit = "tok/s"
+    B, T, H, N = 1, 1024, 12, 64
+
+    def setup(self, torch, dev):
+        from swiftrwkv_b200 import _lib
+        self.torch, self._lib = torch, _lib
+        rng = np.random.default_rng(SEED)
+        self.host = config1_inputs(rng, self.B, self.T, self.H, self.N)
+        self.x = [torch.from_numpy(a).to(dev) for a in self.host]
+        self.y = torch.empty_like(self.x[0])
+        self.h = torch.empty((self.B, self.H, self.N, self.N), device=dev)
+        self.pin = [torch.from_numpy(a).pin_memory() for a in self.host]
+        self.pin_y = torch.empty(self.y.shape, dtype=torch.float32).pin_memory()
+        self.units_per_step = self.B * self.T
+        self.launches_per_step = 1
+        # algorithmic bytes: 6 inputs + y (fp32) + h_out (h_in = 0 is not read)
+        BTHN = self.B * self.T * self.H * self.N
+        self.alg_bytes = 4 * (7 * BTHN + self.B * self.H * self.N * self.N)
+        self.kernel = "wkv7_seq_fwd_kernel"
+        self.h2d = sum(a.nbytes for a in self.host)
+        self.d2h = self.y.numel() * 4
+
+    def step(self):
+        _lib, P = self._lib, self._lib.P
+        st = P(self.torch.cuda.current_stream().cuda_stream)
+        _lib.call("rwkv_wkv7_forward", 0, *(P(t.data_ptr()) for t in self.x), None,
+                  P(self.y.data_ptr()), P(self.h.data_ptr()), self.B, self.T, self.H, self.N, st)
+
+    def step_e2e(self):
+        for d, p in zip(self.x, self.pin):
+            d.copy_(p, non_blocking=True)
+        self.step()
+        self.pin_y.copy_(self.y, non_blocking=True)
+
+    def cpu(self, seconds):
+        from oracle import oracle as O
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.wkv7_forward(*self.host)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * self.B * self.T / dt, f"{n} full config-1 forwards ({n * self.B * self.T} tokens)"
+
+
+class GemvSuite:
+    name = "gemv"
+    metric = "4-bit g64 GEMV GB/s (config 2, 1.5B projection shapes, rows 1, fp16 x)"
+    unit = "GB/s"
+    MATS = [(2048, 2048), (8192, 2048), (2048, 8192), (65536, 2048)]
+
+    def setup(self, torch, dev):
+        from swiftrwkv_b200 import _lib
+        self.torch, self._lib = torch, _lib
+        g = torch.Generator(device="cpu").manual_seed(SEED)
+        self.mats = []
+        from swiftrwkv_b200 import quant as Q
+        for OUT, IN in self.MATS:
+            W = (torch.randn((OUT, IN), generator=g) * 0.02).half().to(dev)
+            wq, sc, bi = Q.quantized(W)
+            x = torch.randn((1, IN), generator=g).half().to(dev)
+            y = torch.empty((1, OUT), device=dev, dtype=torch.float32)
+            self.mats.append((OUT, IN, wq, sc, bi, x, y))
+            del W
+        self.alg_bytes = sum(OUT * IN * 0.5 + OUT * IN // 64 * 4 + IN * 2 + OUT * 4
+                             for OUT, IN in self.MATS)
+        self.units_per_step = self.alg_bytes / 1e9
+        self.launches_per_step = len(self.MATS)
+        self.kernel = "q_gemv_quad_kernel"
+        self.h2d = sum(IN * 2 for _, IN in self.MATS)
+        self.d2h = sum(OUT * 4 for OUT, _ in self.MATS)
+        self.pin_x = [torch.empty((1, IN), dtype=torch.float16).pin_memory() for _, IN in self.MATS]
+        self.pin_y = [torch.empty((1, OUT), dtype=torch.float32).pin_memory() for OUT, _ in self.MATS]
+
+    def step(self):
+        _lib, P = self._lib, self._lib.P
+        st = P(self.torch.cuda.current_stream().cuda_stream)
+        for OUT, IN, wq, sc, bi, x, y in self.mats:
+            _lib.call("rwkv_q_gemm", 2, P(x.data_ptr()), P(wq.data_ptr()), P(sc.data_ptr()),
+                      P(bi.data_ptr()), 2, 0, P(y.data_ptr()), 1, OUT, IN, 64, 4, st)
+
+    def step_e2e(self):
+        for (OUT, IN, wq, sc, bi, x, y), px, py in zip(self.mats, self.pin_x, self.pin_y):
+            x.copy_(px, non_blocking=True)
+        self.step()
+        for (OUT, IN, wq, sc, bi, x, y), py in zip(self.mats, self.pin_y):
+            py.copy_(y, non_blocking=True)
+
+    def cpu(self, seconds):
+        from oracle import oracle as O
+        rng = np.random.default_rng(SEED)
+        OUT, IN = 2048, 2048
+        W = (rng.standard_normal((OUT, IN)) * 0.02).astype(np.float16).astype(np.float32)
+        wq, sc, bi = O.affine_quantize(W)
+        x = rng.standard_normal((1, IN)).astype(np.float16).astype(np.float32)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.affine_gemv(x, wq, sc, bi)
+            n += 1
+        dt = time.perf_counter() - t0
+        by = OUT * IN * 0.5 + OUT * IN // 64 * 4
+        return n * by / dt / 1e9, f"{n} GEMVs of 2048x2048 4-bit g64"
+
+
+WORKLOADS = {"wkv7": WKV7Prefill, "gemv": GemvSuite}
+
+
+# ----------------------------------------------------------------------- timing
+
+def timed(torch, fn, steps, warmup, flush, dist):
+    for _ in range(warmup):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        flush()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def max_over_ranks(torch, val, dist):
+    if not dist:
+        return val
+    t = torch.tensor([val], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_reference(args, rank):
+    """CPU arm: the oracle restatement on all host cores, same metric/config."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    O.build()
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    wl = WORKLOADS[args.workload]()
+    wl.host = config1_inputs(np.random.default_rng(SEED)) if wl.name == "wkv7" else None
+    if wl.name == "wkv7":
+        wl.B, wl.T, wl.H, wl.N = 1, 1024, 12, 64
+    per = []
+    for i in range(args.warmup + args.steps):
+        v, sample = wl.cpu(2.0)
+        if i >= args.warmup:
+            per.append(v)
+    value = statistics.median(per)
+    out = {"impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": wl.name},
+           "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cores, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="wkv7", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    dist = world > 1
+    torch.cuda.set_device(local)
+    if dist:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    from swiftrwkv_b200 import _lib
+    _lib.lib()
+
+    wl = WORKLOADS[args.workload]()
+    wl.setup(torch, dev)
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.zero_()
+
+    clk = ClockSampler(local)
+    clk.start()
+    times = timed(torch, wl.step, args.steps, args.warmup, flush, dist)
+    clocks = clk.stop()
+    e2e_times = timed(torch, wl.step_e2e, args.steps, args.warmup, flush, dist)
+
+    ms = max_over_ranks(torch, sum(times) / len(times), dist)
+    ms_e2e = max_over_ranks(torch, sum(e2e_times) / len(e2e_times), dist)
+    units = wl.units_per_step * world
+    value = units / (ms / 1e3)
+    e2e_value = units / (ms_e2e / 1e3)
+    peaks = load_peaks()
+    kernel_ms = sum(times) / len(times) / wl.launches_per_step
+    achieved = wl.alg_bytes / wl.launches_per_step / (kernel_ms / 1e3) / 1e9
+    result = {
+        "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if wl.name == "wkv7" else "u4/f16", "data": "synthetic",
+        "config": {"workload": wl.name, "l2": "flushed (256 MB write) before every timed step",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "peak_src": peaks["src"], "kernel": wl.kernel},
+        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
+                "d2h_bytes_per_step": wl.d2h},
+        "gpu_launches": wl.launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1:
+        from oracle import oracle as O
+        O.build()
+        cores = os.cpu_count() or 1
+        O.set_threads(cores)
+        v, sample = wl.cpu(args.cpu_seconds)
+        result["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": cores, "kind": "port",
+                                  "sample": sample}
+    if rank == 0:
+        print(json.dumps(result))
+    if dist:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,213 @@
+/*
+ * rwkv_cuda.h -- C ABI of the B200 (sm_100a) WKV-7 and quantised-GEMV library
+ * (librwkvcuda.so).
+ *
+ * Conventions (shared by every entry point):
+ *  - Every function returns an int status: RWKV_OK (0) or a negative
+ *    RWKV_E_* code.  Nothing traps; rwkv_last_error() gives a one-line reason
+ *    for the calling thread's last failure.
+ *  - Every buffer is a caller-owned DEVICE pointer unless stated otherwise.
+ *    Calls are asynchronous on the given stream (NULL = the legacy default
+ *    stream); argument checks happen on the host before anything launches.
+ *  - Element types are explicit (RWKV_F32 / RWKV_BF16 / RWKV_F16).  WKV state
+ *    is always fp32, laid out [.., H, N, N] with rows = value index dv and
+ *    columns = key index dk; sequence tensors are [B, T, H, N] row-major.
+ *  - Optional tensors may be NULL, mirroring the reference's Swift optionals
+ *    (h_in = NULL means a zero state; an output that is NULL is not written).
+ *  - Shapes a kernel does not take return RWKV_E_UNSUPPORTED (the reference's
+ *    `nil` fall-back); there is no CPU fallback behind any entry point.
+ *
+ * Each declaration cites the reference interface (RafaelUI/SwiftRWKV, file:line)
+ * it replaces.
+ */
+#ifndef RWKV_CUDA_H
+#define RWKV_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* rwkv_stream_t; /* == cudaStream_t */
+
+enum {
+    RWKV_OK = 0,
+    RWKV_E_NULL = -1,        /* a required pointer is NULL */
+    RWKV_E_SHAPE = -2,       /* inconsistent or out-of-range sizes */
+    RWKV_E_DTYPE = -3,       /* element type not accepted by this entry point */
+    RWKV_E_UNSUPPORTED = -4, /* valid shape the kernel does not take */
+    RWKV_E_CUDA = -5,        /* a CUDA runtime call failed */
+    RWKV_E_TIMEOUT = -6,     /* a bounded device-side wait gave up */
+    RWKV_E_WORKSPACE = -7    /* workspace missing or too small */
+};
+
+enum { RWKV_F32 = 0, RWKV_BF16 = 1, RWKV_F16 = 2 };
+
+#define RWKV_WKV7_HEAD_SIZE 64 /* WKV7_HEAD_SIZE, Sources/RWKVKernel/WKV7.swift:7 */
+#define RWKV_WKV7_CHUNK 16     /* WKV7_CHUNK, Sources/RWKVKernel/WKV7.swift:8 */
+
+/* ---------------------------------------------------------------- library */
+
+int rwkv_version(void);                  /* 100*major + minor */
+const char* rwkv_status_string(int status);
+const char* rwkv_last_error(void);       /* thread-local, "" when none */
+
+/* ------------------------------------------------------------------ WKV-7
+ * r, w, k, v, a, b, y: [B, T, H, N] in `dtype`; h_in/h_out: [B, H, N, N] fp32.
+ * N must be 64.  The recurrence per head, row dv (Sources/RWKVKernel/
+ * WKV7Reference.swift:47-74): sa = S a;  S <- S diag(w) + v k^T + sa b^T;
+ * y = S r (on the updated S).
+ */
+
+/* Frozen forward over the whole sequence, any T >= 1.
+ * Replaces wkv7SequenceForward (Sources/RWKVKernel/WKV7.swift:242-264), and
+ * with it wkv7ForwardWithState / wkv7ForwardChunked / wkv7Forward
+ * (WKV7.swift:96-148), which give the same result. */
+int rwkv_wkv7_forward(int dtype, const void* r, const void* w, const void* k, const void* v,
+                      const void* a, const void* b, const float* h_in, void* y, float* h_out,
+                      int B, int T, int H, int N, rwkv_stream_t stream);
+
+/* Differentiable forward of the training path: as rwkv_wkv7_forward, plus
+ * sa [B,T,H,N] fp32 (may be NULL) and h_ckpt [B, H, T/16, N, N] fp32, the state
+ * after every 16 steps (the last one equals h_out).  T % 16 == 0.
+ * Replaces wkv7TrainWithState's forward kernel (Sources/RWKVKernel/
+ * WKV7Train.swift:26-97, :375-468) and wkv7Train (:472-475). */
+int rwkv_wkv7_train_forward(int dtype, const void* r, const void* w, const void* k,
+                            const void* v, const void* a, const void* b, const float* h_in,
+                            void* y, float* h_out, float* sa, float* h_ckpt, int B, int T,
+                            int H, int N, rwkv_stream_t stream);
+
+/* Workspace bytes rwkv_wkv7_backward needs for these sizes. */
+int64_t rwkv_wkv7_backward_workspace_size(int B, int T, int H, int N);
+
+/* Gradients of (y, h_out) w.r.t. (r, w, k, v, a, b, h_in).  h_in (NULL = zero)
+ * and h_ckpt come from the forward; dh_out may be NULL (zero); dh_in may be
+ * NULL (not written).  States inside a chunk are recomputed from the chunk's
+ * starting checkpoint (no division by w).  Deterministic.  T % 16 == 0.
+ * `workspace` is device memory of rwkv_wkv7_backward_workspace_size bytes.
+ * Replaces the VJP of wkv7TrainWithState: ckptBwdKernelV2 / ckptBwdKernel
+ * (Sources/RWKVKernel/WKV7Train.swift:99-339, :410-420). */
+int rwkv_wkv7_backward(int dtype, const void* r, const void* w, const void* k, const void* v,
+                       const void* a, const void* b, const float* h_in, const float* h_ckpt,
+                       const void* dy, const float* dh_out, void* dr, void* dw, void* dk,
+                       void* dv, void* da, void* db, float* dh_in, int B, int T, int H, int N,
+                       void* workspace, int64_t workspace_bytes, rwkv_stream_t stream);
+
+/* One-token decode step for `rows` independent rows: r..b, y [rows, H, N];
+ * h [rows, H, N, N] fp32 updated in place.
+ * Replaces wkv7StepForward (Sources/RWKVKernel/WKV7DecodeKernels.swift:157-173). */
+int rwkv_wkv7_step(int dtype, const void* r, const void* w, const void* k, const void* v,
+                   const void* a, const void* b, float* h, void* y, int rows, int H, int N,
+                   rwkv_stream_t stream);
+
+/* Fused tmix tail: per (row, head) GroupNorm (two-pass, eps) of wkv, plus the
+ * bonus (sum r*k*r_k)*v, times the gate:
+ *   out = ((norm(wkv)*ln_w + ln_b) + (sum r*k*r_k) * v) * g.
+ * wkv, r, k, v, g, out: [rows, H*S] fp32; rk, ln_w, ln_b: [H*S] fp32.
+ * Replaces wkvTail (Sources/RWKVKernel/WKV7DecodeKernels.swift:190-262). */
+int rwkv_wkv_tail(const float* wkv, const float* r, const float* k, const float* v,
+                  const float* rk, const float* ln_w, const float* ln_b, const float* g,
+                  float* out, int rows, int H, int S, float eps, rwkv_stream_t stream);
+
+/* The decode step and the tail in one launch (the pair of calls at
+ * Sources/RWKVGen/X070Generation.swift:280-291): updates h, writes the tail
+ * output [rows, H*N] fp32.  Inputs fp32. */
+int rwkv_wkv7_step_tail(const float* r, const float* w, const float* k, const float* v,
+                        const float* a, const float* b, float* h, const float* rk,
+                        const float* ln_w, const float* ln_b, const float* g, float* out,
+                        int rows, int H, int N, float eps, rwkv_stream_t stream);
+
+/* ------------------------------------------- MLX affine container (QLoRA base)
+ * wq: uint32 [OUT, IN*bits/32], each row an LSB-first bit stream of `bits`-bit
+ * codes (Sources/RWKVQuant/RwkvqNative.swift:28-31,161-175); scales, biases:
+ * [OUT, IN/group] in `sdtype` (F16, BF16 or F32); w = scale*q + bias.
+ * bits in {2,3,4,5,6,8}; group in {32, 64, 128}; IN % group == 0.
+ */
+
+/* y[n, o] = sum_i x[n, i] * W[o, i]   (quantizedMM with transpose: true).
+ * x: [rows, IN] in xdtype; y: [rows, OUT] in ydtype; accumulation in fp32.
+ * Replaces the quantizedMM call of X070Backbone.baseProj
+ * (Sources/RWKVGen/X070Backbone.swift:678-681) and RwkvqNativeWeight
+ * (Sources/RWKVQuant/RwkvqNative.swift:48-51). */
+int rwkv_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* scales,
+                const void* biases, int sdtype, int ydtype, void* y, int rows, int OUT, int IN,
+                int group, int bits, rwkv_stream_t stream);
+
+/* Dense W [OUT, IN] in odtype: float(q)*float(scale) + float(bias), one
+ * rounding.  Replaces MLX `dequantized` as used at
+ * Sources/RWKVGen/X070Backbone.swift:759-766 and RwkvqModelTests. */
+int rwkv_q_dequant(const uint32_t* wq, const void* scales, const void* biases, int sdtype,
+                   int odtype, void* w_out, int OUT, int IN, int group, int bits,
+                   rwkv_stream_t stream);
+
+/* Embedding rows: out[n, :] = dequantised row ids[n] (int32, device), odtype.
+ * Replaces X070Backbone.embed's quantised branch (X070Backbone.swift:758-767). */
+int rwkv_q_rows(const int32_t* ids, int n_ids, const uint32_t* wq, const void* scales,
+                const void* biases, int sdtype, int odtype, void* out, int vocab, int IN,
+                int group, int bits, rwkv_stream_t stream);
+
+/* Affine quantiser writing the MLX container from W [OUT, IN] (wdtype);
+ * scales/biases written in wdtype (F16/BF16) or F32.  Replaces MLX `quantized`
+ * at Sources/RWKVGen/LoRA.swift:68 (quantizeWeight / quantizeBaseModel). */
+int rwkv_q_quantize(int wdtype, const void* W, uint32_t* wq, void* scales, void* biases,
+                    int OUT, int IN, int group, int bits, rwkv_stream_t stream);
+
+/* ------------------------------------------------------ .rwkvq sb6 (K3 layout)
+ * qblk: uint8 [OUT, (IN/32)*(16+4*xbits)]; qsqm: uint8 [OUT, (IN/32)*2];
+ * ddm: fp16 [OUT, (IN/256)*2]; superblock 8; xbits in {0,1,2}; IN % 256 == 0.
+ */
+
+/* Dense [OUT, IN] in odtype; combine in fp32, one rounding at store.
+ * Replaces rwkvqDequantDense (Sources/RWKVQuant/RwkvqDequant.swift:160-183). */
+int rwkv_sb6_dequant(const uint8_t* qblk, const uint8_t* qsqm, const uint16_t* ddm, int odtype,
+                     void* out, int OUT, int IN, int xbits, rwkv_stream_t stream);
+
+/* y [rows, OUT] fp32 = x [rows, IN] (xdtype) times W^T.  The reference takes
+ * one row; any rows >= 1 here.
+ * Replaces rwkvqSb6GEMV / RwkvqSidecar.sb6GEMV
+ * (Sources/RWKVQuant/RwkvqSb6GEMV.swift:170-208). */
+int rwkv_sb6_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_t* qsqm,
+                  const uint16_t* ddm, float* y, int rows, int OUT, int IN, int xbits,
+                  rwkv_stream_t stream);
+
+/* Lossless relayout into the MLX affine container (group 32, bits 4+xbits):
+ * wq [OUT, (IN/32)*bits] u32, scales/biases [OUT, IN/32] fp32 (scale clamped
+ * at 1e-8).  *fp16_ok_host (host int, written after a stream sync) is 1 when
+ * fp16 scales/biases would change no weight.
+ * Replaces RwkvqSidecar.nativeAffine (Sources/RWKVQuant/RwkvqNative.swift:78-196). */
+int rwkv_sb6_to_affine(const uint8_t* qblk, const uint8_t* qsqm, const uint16_t* ddm,
+                       uint32_t* wq, float* scales, float* biases, int* fp16_ok_host, int OUT,
+                       int IN, int xbits, rwkv_stream_t stream);
+
+/* --------------------------------------------------- .rwkvq sym (6 / 8 bit)
+ * qblk: 8-bit: int8 codes [OUT, IN]; 6-bit: [OUT, (IN/32)*24] (pairs of
+ * 16-blocks: 16 nibble bytes + 2 bit-planes, codes stored +32);
+ * qs: int8 [OUT, IN/16]; d: fp16 [OUT, ceil(IN/256)].
+ */
+
+/* Dense [OUT, IN]: F32 and BF16 multiply in float, F16 multiplies in half.
+ * Replaces rwkvqDequantSym (Sources/RWKVQuant/RwkvqDequant.swift:409-431). */
+int rwkv_sym_dequant(const uint8_t* qblk, const uint8_t* qs, const uint16_t* d, int odtype,
+                     void* out, int OUT, int IN, int bits, rwkv_stream_t stream);
+
+/* y [nn, OUT] fp32.  K = OUT/out_per matrices share one launch; matrix j
+ * (rows j*out_per ..) reads input row n*K + j of x [nn*K, IN].  out_per = OUT
+ * is a plain GEMV over nn input rows.  IN % 256 == 0, out_per % 4 == 0.
+ * Replaces rwkvqSymGEMV and symGEMVFused
+ * (Sources/RWKVQuant/RwkvqSymGEMV.swift:223-247, :343-358). */
+int rwkv_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_t* qs,
+                  const uint16_t* d, float* y, int nn, int OUT, int IN, int bits, int out_per,
+                  rwkv_stream_t stream);
+
+/* Embedding rows of an 8-bit sym table, fp16 out [n_ids, IN]:
+ * out = half(code * half(qs*d)).  Replaces RwkvqSymRowTable.rows
+ * (Sources/RWKVQuant/RwkvqSymRows.swift:402-411). */
+int rwkv_sym_rows(const int32_t* ids, int n_ids, const uint8_t* codes, const uint8_t* qs,
+                  const uint16_t* d, uint16_t* out, int vocab, int IN, rwkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RWKV_CUDA_H */
