@@ -19,9 +19,11 @@ namespace rwkv {
 
 __device__ __forceinline__ float rnd_half(float f) { return __half2float(__float2half_rn(f)); }
 
+// Blocks are 16 + 4*xbits bytes (20 or 24 at xbits 1/2), so only 4-byte
+// alignment holds: the block is read as u32 words, never as a 16-byte vector.
 __device__ __forceinline__ void sb6_block_codes(const uint8_t* blk, int xbits, uint8_t nib[32]) {
-    const uint4 q = *reinterpret_cast<const uint4*>(blk);
-    const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t* bw = reinterpret_cast<const uint32_t*>(blk);
+    const uint32_t wds[4] = {bw[0], bw[1], bw[2], bw[3]};
 #pragma unroll
     for (int j = 0; j < 16; j++) {
         const uint8_t byte = (uint8_t)(wds[j >> 2] >> (8 * (j & 3)));
@@ -139,9 +141,10 @@ __global__ void sb6_to_affine_kernel(const uint8_t* __restrict__ qblk, const uin
 
 // ------------------------------------------------------------------------ sym
 
+// Pairs are 24 bytes: read as u32 words (8-byte alignment at best).
 __device__ __forceinline__ void sym6_pair_codes(const uint8_t* pb, int code[32]) {
-    const uint4 q = *reinterpret_cast<const uint4*>(pb);
-    const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t* bw = reinterpret_cast<const uint32_t*>(pb);
+    const uint32_t wds[4] = {bw[0], bw[1], bw[2], bw[3]};
 #pragma unroll
     for (int blk = 0; blk < 2; blk++)
 #pragma unroll

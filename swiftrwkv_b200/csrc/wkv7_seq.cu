@@ -301,7 +301,8 @@ wkv7_bwd_seq_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* _
         // Recompute the chunk's states; thread i holds row i.
         {
             float row[HN];
-            const float* s0 = (c == 0) ? h_in : (h_ckpt + ((size_t)bh * NC + (c - 1)) * NN);
+            const float* s0 = (c == 0) ? (h_in ? h_in + hb : nullptr)
+                                       : (h_ckpt + ((size_t)bh * NC + (c - 1)) * NN);
 #pragma unroll
             for (int j = 0; j < HN; j++) row[j] = s0 ? s0[(size_t)i * HN + j] : 0.f;
             __syncthreads();
