@@ -206,6 +206,54 @@ int rwkv_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_t*
 int rwkv_sym_rows(const int32_t* ids, int n_ids, const uint8_t* codes, const uint8_t* qs,
                   const uint16_t* d, uint16_t* out, int vocab, int IN, rwkv_stream_t stream);
 
+
+/* --------------------------------------------- x070 recurrent decode runtime
+ * The host side of X070Backbone's decode over the kernels above, for a 4-bit
+ * group-64 QLoRA base: embedding -> per layer (ln1, token shift, r/k/v
+ * GEMVs, low-rank w/a/v/g branches, WKV step + tail, o GEMV, ln2, cmix
+ * key/value GEMVs) -> ln_out -> head GEMV -> greedy argmax.  Each row of a
+ * batch carries its own state; one step is captured into a CUDA graph per
+ * row count and replayed.  Replaces X070Backbone.step / stepEager
+ * (Sources/RWKVGen/X070Generation.swift:449-498), generate
+ * (Sources/RWKVGen/Generate.swift:112-202) and generateBatch's step loop
+ * (Sources/RWKVGen/BatchGenerate.swift:54-116), greedy sampling
+ * (Sources/RWKVGen/GPUSampler.swift:90).
+ */
+typedef struct rwkv_x070* rwkv_x070_t;
+
+typedef struct {
+    int n_layer, n_embd, head_size, vocab, ffn; /* X070Config (X070Backbone.swift:24-37) */
+    int rank_w, rank_a, rank_v, rank_g;         /* low-rank sizes (X070Init.swift:46-52) */
+    int quant_bits, quant_group;                /* 4, 64 (LoRA.swift:28-91) */
+    int act_dtype;  /* RWKV_F16: fp16 activations, tensor-core GEMVs; RWKV_F32: fp32 path */
+    int max_rows;   /* rows (batch) the state and workspace are sized for */
+} rwkv_x070_config;
+
+int rwkv_x070_create(const rwkv_x070_config* cfg, rwkv_x070_t* out);
+int rwkv_x070_destroy(rwkv_x070_t model);
+/* Parameter by its reference name ("emb.weight", "blocks.3.tmix.r_proj.weight",
+ * ...), from a HOST fp32 array of n elements; the big matrices are quantised
+ * on the device (rwkv_q_quantize), the low-rank matrices stored fp16. */
+int rwkv_x070_set_param(rwkv_x070_t model, const char* name, const float* host, int64_t n);
+/* Random init with the x070 recipe (Sources/RWKVGen/Training/X070Init.swift:79-206),
+ * drawn on the device from `seed`. */
+int rwkv_x070_init_random(rwkv_x070_t model, uint64_t seed);
+/* Zero the state of rows 0..rows-1 (RWKVState(cfg:), X070Generation.swift:34-41). */
+int rwkv_x070_reset_state(rwkv_x070_t model, int rows, rwkv_stream_t stream);
+/* One token per row.  ids: device int32 [rows] (NULL = the previous step's
+ * argmax, kept on the device); logits: device fp32 [rows, vocab] or NULL;
+ * next_ids: device int32 [rows] or NULL.  use_graph != 0 replays the
+ * captured step (the stream must not be the legacy default stream during
+ * the first, capturing call). */
+int rwkv_x070_step(rwkv_x070_t model, const int32_t* ids, int rows, float* logits,
+                   int32_t* next_ids, int use_graph, rwkv_stream_t stream);
+/* Greedy generation with HOST buffers: prompts [rows, prompt_len] fed
+ * recurrently, then n_new tokens per row into out [rows, n_new]. */
+int rwkv_x070_generate(rwkv_x070_t model, const int32_t* prompt_host, int rows, int prompt_len,
+                       int n_new, int32_t* out_host, rwkv_stream_t stream);
+int64_t rwkv_x070_weight_bytes(rwkv_x070_t model);
+int rwkv_x070_launches_per_step(rwkv_x070_t model);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,11 +53,21 @@ _SIGS = {
     "rwkv_sym_dequant": [P, P, P, I, P, I, I, I, P],
     "rwkv_sym_gemv": [I, P, P, P, P, P, I, I, I, I, I, P],
     "rwkv_sym_rows": [P, I, P, P, P, P, I, I, P],
+    "rwkv_x070_create": [P, P],
+    "rwkv_x070_destroy": [P],
+    "rwkv_x070_set_param": [P, ctypes.c_char_p, P, I64],
+    "rwkv_x070_init_random": [P, ctypes.c_uint64],
+    "rwkv_x070_reset_state": [P, I, P],
+    "rwkv_x070_step": [P, P, I, P, P, I, P],
+    "rwkv_x070_generate": [P, P, I, I, I, P, P],
+    "rwkv_x070_weight_bytes": [P],
+    "rwkv_x070_launches_per_step": [P],
 }
 _RESTYPES = {
     "rwkv_status_string": ctypes.c_char_p,
     "rwkv_last_error": ctypes.c_char_p,
     "rwkv_wkv7_backward_workspace_size": I64,
+    "rwkv_x070_weight_bytes": I64,
 }
 
 _lib = None

@@ -14,6 +14,7 @@
 // then reduced across the warp with shuffles.  Two output rows per warp share
 // the x loads and the x sums.
 #include "common.cuh"
+#include "gemv_mma.cuh"
 
 namespace rwkv {
 
@@ -276,6 +277,26 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
                   const void* biases, int sdtype, int ydtype, void* y, int rows, int OUT, int IN,
                   int group, int bits, cudaStream_t st) {
     const size_t xe = xdtype == RWKV_F32 ? 4 : 2, ye = ydtype == RWKV_F32 ? 4 : 2;
+    // fp16 activations on the 4-bit group-64 container: tensor-core path.
+    if (xdtype == RWKV_F16 && sdtype == RWKV_F16 && bits == 4 && group == 64 &&
+        (ydtype == RWKV_F32 || ydtype == RWKV_F16)) {
+        GemvJobs jobs{};
+        GemvJob& j = jobs.j[0];
+        j.w = wq;
+        j.scales = (const __half*)scales;
+        j.biases = (const __half*)biases;
+        j.x = (const __half*)x;
+        j.x_stride = IN;
+        j.OUT = OUT;
+        j.IN = IN;
+        j.act = ACT_NONE;
+        j.out = ydtype == RWKV_F32 ? OUT_F32 : OUT_F16;
+        j.y = y;
+        j.y_stride = OUT;
+        cudaError_t e = launch_gemv_mma<0>(jobs, 1, rows, st);
+        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemv_mma_kernel: %s", cudaGetErrorString(e));
+        return ok();
+    }
     return dispatch_dtype(xdtype, [&]<typename TX>() {
         return dispatch_sdtype(sdtype, [&]<typename TS>() {
             return dispatch_dtype(ydtype, [&]<typename TY>() {

@@ -1,0 +1,566 @@
+// x070 (RWKV-7 "Goose") recurrent decode runtime over the hot-path kernels:
+// the host side of X070Backbone.step / generate / generateBatch for a 4-bit
+// QLoRA base (Sources/RWKVGen/X070Generation.swift:449-498,
+// BatchGenerate.swift:54-116), in C++.
+//
+// Weights live on the device: the big matrices (r/k/v/o projections, cmix
+// key/value, head, embedding) in the MLX affine container (4-bit, group 64,
+// fp16 scale/bias), the low-rank branches in fp16, vectors in fp32.  Every
+// row has its own state: WKV [L, rows, H, 64, 64] fp32 and the two token-shift
+// rows per layer.  One decode step is a fixed sequence of launches on one
+// stream; it is captured once per row count into a CUDA graph and replayed.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv_mma.cuh"
+#include "x070_kernels.cuh"
+
+namespace rwkv {
+
+int launch_q_quantize(int, const void*, uint32_t*, void*, void*, int, int, int, int, cudaStream_t);
+
+// -------------------------------------------------------- device init helpers
+
+__device__ __forceinline__ uint64_t splitmix(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// mode 0: uniform(lo, hi); mode 1: normal(0, lo); counter-based, seeded.
+__global__ void fill_f16_kernel(__half* out, int64_t n, int mode, float lo, float hi, uint64_t seed) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint64_t z = splitmix(seed ^ splitmix((uint64_t)i));
+        const float u1 = ((z >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        float v;
+        if (mode == 0) {
+            v = lo + (hi - lo) * u1;
+        } else {
+            const float u2 = (((z >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
+            v = lo * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        }
+        out[i] = __float2half_rn(v);
+    }
+}
+
+__global__ void f32_to_f16_kernel(const float* in, __half* out, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = __float2half_rn(in[i]);
+}
+
+// ------------------------------------------------------------------- model
+
+struct QMat {
+    uint32_t* wq = nullptr;
+    __half* sc = nullptr;
+    __half* bi = nullptr;
+    int OUT = 0, IN = 0;
+};
+
+struct LayerW {
+    float *ln1w = nullptr, *ln1b = nullptr, *ln2w = nullptr, *ln2b = nullptr;
+    float* coef6 = nullptr;  // [6, C]: r, w, k, v, a, g
+    float *kkw = nullptr, *kaw = nullptr, *rkw = nullptr, *lnxw = nullptr, *lnxb = nullptr;
+    float* cxk = nullptr;
+    float *wbias = nullptr, *abias = nullptr, *vbias = nullptr;
+    __half *wA = nullptr, *wB = nullptr, *aA = nullptr, *aB = nullptr;
+    __half *gA = nullptr, *gB = nullptr, *vA = nullptr, *vB = nullptr;
+    QMat r, k, v, o, key, value;
+};
+
+struct X070 {
+    rwkv_x070_config cfg{};
+    int L, C, H, V, F, Rmax;
+    int rw, ra, rv, rg, hid;  // low-rank sizes and hidden width
+    bool f16act;
+    std::vector<void*> allocs;
+    std::vector<LayerW> lw;
+    QMat emb, head;
+    float *ln0w, *ln0b, *lnow, *lnob;
+    // state
+    float *wkv, *tshift, *cshift;
+    // workspace
+    float *x, *r, *k, *v, *wdec, *a, *vv, *g, *vfirst, *logits;
+    void *mix, *hidden, *tail, *xk, *ffn, *lnout;
+    int32_t* ids;
+    size_t act_bytes;
+    std::map<int, cudaGraphExec_t> graphs;
+    int64_t weight_bytes = 0;
+    // A capture cannot run on the legacy default stream: graph work requested
+    // there is forwarded to this stream, ordered by events on both sides.
+    cudaStream_t own = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+
+    bool alloc_failed = false;
+
+    // Device allocation owned by the model (freed by the destructor); a
+    // failure is recorded and reported by rwkv_x070_create.
+    template <typename T>
+    T* alloc(size_t n, bool zero = true) {
+        void* p = nullptr;
+        if (n == 0) n = 1;
+        if (alloc_failed || cudaMalloc(&p, n * sizeof(T)) != cudaSuccess) {
+            alloc_failed = true;
+            return nullptr;
+        }
+        if (zero) cudaMemset(p, 0, n * sizeof(T));
+        allocs.push_back(p);
+        return (T*)p;
+    }
+    QMat qmat(int OUT, int IN) {
+        QMat q;
+        q.OUT = OUT;
+        q.IN = IN;
+        q.wq = alloc<uint32_t>((size_t)OUT * IN / 8);
+        q.sc = alloc<__half>((size_t)OUT * IN / 64);
+        q.bi = alloc<__half>((size_t)OUT * IN / 64);
+        weight_bytes += (int64_t)OUT * IN / 2 + (int64_t)OUT * IN / 64 * 4;
+        return q;
+    }
+    __half* hmat(size_t n) {
+        weight_bytes += (int64_t)n * 2;
+        return alloc<__half>(n);
+    }
+
+    explicit X070(const rwkv_x070_config& c) : cfg(c) {
+        L = c.n_layer; C = c.n_embd; H = C / c.head_size; V = c.vocab; F = c.ffn; Rmax = c.max_rows;
+        rw = c.rank_w; ra = c.rank_a; rv = c.rank_v; rg = c.rank_g;
+        hid = rw + ra + rv + rg;
+        f16act = c.act_dtype == RWKV_F16;
+        act_bytes = f16act ? 2 : 4;
+        emb = qmat(V, C);
+        head = qmat(V, C);
+        ln0w = alloc<float>(C); ln0b = alloc<float>(C); lnow = alloc<float>(C); lnob = alloc<float>(C);
+        lw.resize(L);
+        for (int l = 0; l < L; l++) {
+            LayerW& w = lw[l];
+            w.ln1w = alloc<float>(C); w.ln1b = alloc<float>(C); w.ln2w = alloc<float>(C); w.ln2b = alloc<float>(C);
+            w.coef6 = alloc<float>(6 * (size_t)C);
+            w.kkw = alloc<float>(C); w.kaw = alloc<float>(C); w.rkw = alloc<float>(C);
+            w.lnxw = alloc<float>(C); w.lnxb = alloc<float>(C); w.cxk = alloc<float>(C);
+            w.wbias = alloc<float>(C); w.abias = alloc<float>(C); w.vbias = alloc<float>(C);
+            w.wA = hmat((size_t)rw * C); w.wB = hmat((size_t)C * rw);
+            w.aA = hmat((size_t)ra * C); w.aB = hmat((size_t)C * ra);
+            w.gA = hmat((size_t)rg * C); w.gB = hmat((size_t)C * rg);
+            if (l > 0) { w.vA = hmat((size_t)rv * C); w.vB = hmat((size_t)C * rv); }
+            w.r = qmat(C, C); w.k = qmat(C, C); w.v = qmat(C, C); w.o = qmat(C, C);
+            w.key = qmat(F, C); w.value = qmat(C, F);
+            weight_bytes += (int64_t)C * 4 * 20;
+        }
+        const size_t RC = (size_t)Rmax * C;
+        wkv = alloc<float>((size_t)L * Rmax * H * 64 * 64);
+        tshift = alloc<float>((size_t)L * RC);
+        cshift = alloc<float>((size_t)L * RC);
+        x = alloc<float>(RC); r = alloc<float>(RC); k = alloc<float>(RC); v = alloc<float>(RC);
+        wdec = alloc<float>(RC); a = alloc<float>(RC); vv = alloc<float>(RC); g = alloc<float>(RC);
+        vfirst = alloc<float>(RC);
+        logits = alloc<float>((size_t)Rmax * V);
+        mix = alloc<char>(6 * RC * act_bytes);
+        hidden = alloc<char>((size_t)Rmax * hid * act_bytes);
+        tail = alloc<char>(RC * act_bytes);
+        xk = alloc<char>(RC * act_bytes);
+        ffn = alloc<char>((size_t)Rmax * F * act_bytes);
+        lnout = alloc<char>(RC * act_bytes);
+        ids = alloc<int32_t>(Rmax);
+        // the widest tensor-core tiles use 64 KB of shared memory
+        cudaFuncSetAttribute(gemv_mma_kernel<0, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaFuncSetAttribute(gemv_mma_kernel<1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking);
+        cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+    }
+
+    ~X070() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        for (void* p : allocs) cudaFree(p);
+        if (own) cudaStreamDestroy(own);
+        if (ev_in) cudaEventDestroy(ev_in);
+        if (ev_out) cudaEventDestroy(ev_out);
+    }
+
+    // ----- parameters
+
+    int upload_q(QMat& q, const float* host, int64_t n) {
+        RWKV_REQUIRE(n == (int64_t)q.OUT * q.IN, RWKV_E_SHAPE, "matrix size %lld, expected %d x %d",
+                     (long long)n, q.OUT, q.IN);
+        float* tmp = nullptr;
+        __half* h16 = nullptr;
+        if (cudaMalloc(&tmp, n * 4) != cudaSuccess || cudaMalloc(&h16, n * 2) != cudaSuccess)
+            return fail(RWKV_E_CUDA, "set_param: staging allocation failed");
+        cudaMemcpy(tmp, host, n * 4, cudaMemcpyHostToDevice);
+        f32_to_f16_kernel<<<1024, 256>>>(tmp, h16, n);
+        int rc = launch_q_quantize(RWKV_F16, h16, q.wq, q.sc, q.bi, q.OUT, q.IN, 64, 4, 0);
+        cudaDeviceSynchronize();
+        cudaFree(tmp);
+        cudaFree(h16);
+        return rc;
+    }
+    int upload_h(__half* dst, int64_t expect, const float* host, int64_t n) {
+        RWKV_REQUIRE(dst != nullptr, RWKV_E_SHAPE, "set_param: this layer has no such matrix");
+        RWKV_REQUIRE(n == expect, RWKV_E_SHAPE, "matrix size %lld, expected %lld", (long long)n, (long long)expect);
+        float* tmp = nullptr;
+        if (cudaMalloc(&tmp, n * 4) != cudaSuccess) return fail(RWKV_E_CUDA, "set_param: staging allocation failed");
+        cudaMemcpy(tmp, host, n * 4, cudaMemcpyHostToDevice);
+        f32_to_f16_kernel<<<1024, 256>>>(tmp, dst, n);
+        cudaDeviceSynchronize();
+        cudaFree(tmp);
+        return check_launch("f32_to_f16_kernel");
+    }
+    int upload_f(float* dst, int64_t expect, const float* host, int64_t n) {
+        RWKV_REQUIRE(n == expect, RWKV_E_SHAPE, "vector size %lld, expected %lld", (long long)n, (long long)expect);
+        return cudaMemcpy(dst, host, n * 4, cudaMemcpyHostToDevice) == cudaSuccess
+                   ? ok() : fail(RWKV_E_CUDA, "set_param: copy failed");
+    }
+
+    int set_param(const std::string& name, const float* host, int64_t n) {
+        if (name == "emb.weight") return upload_q(emb, host, n);
+        if (name == "head.weight") return upload_q(head, host, n);
+        if (name == "ln0.weight") return upload_f(ln0w, C, host, n);
+        if (name == "ln0.bias") return upload_f(ln0b, C, host, n);
+        if (name == "ln_out.weight") return upload_f(lnow, C, host, n);
+        if (name == "ln_out.bias") return upload_f(lnob, C, host, n);
+        int l = -1, used = 0;
+        if (sscanf(name.c_str(), "blocks.%d.%n", &l, &used) != 1 || l < 0 || l >= L)
+            return fail(RWKV_E_SHAPE, "set_param: unknown parameter '%s'", name.c_str());
+        const std::string s = name.substr(used);
+        LayerW& w = lw[l];
+        static const char* mixn[6] = {"tmix.x_r", "tmix.x_w", "tmix.x_k", "tmix.x_v", "tmix.x_a", "tmix.x_g"};
+        for (int m = 0; m < 6; m++)
+            if (s == mixn[m]) return upload_f(w.coef6 + (size_t)m * C, C, host, n);
+        if (s == "ln1.weight") return upload_f(w.ln1w, C, host, n);
+        if (s == "ln1.bias") return upload_f(w.ln1b, C, host, n);
+        if (s == "ln2.weight") return upload_f(w.ln2w, C, host, n);
+        if (s == "ln2.bias") return upload_f(w.ln2b, C, host, n);
+        if (s == "tmix.k_k") return upload_f(w.kkw, C, host, n);
+        if (s == "tmix.k_a") return upload_f(w.kaw, C, host, n);
+        if (s == "tmix.r_k") return upload_f(w.rkw, C, host, n);
+        if (s == "tmix.ln_x.weight") return upload_f(w.lnxw, C, host, n);
+        if (s == "tmix.ln_x.bias") return upload_f(w.lnxb, C, host, n);
+        if (s == "cmix.x_k") return upload_f(w.cxk, C, host, n);
+        if (s == "tmix.w_lora_B.bias") return upload_f(w.wbias, C, host, n);
+        if (s == "tmix.a_lora_B.bias") return upload_f(w.abias, C, host, n);
+        if (s == "tmix.v_lora_B.bias") return upload_f(w.vbias, C, host, n);
+        if (s == "tmix.w_lora_A.weight") return upload_h(w.wA, (int64_t)rw * C, host, n);
+        if (s == "tmix.w_lora_B.weight") return upload_h(w.wB, (int64_t)C * rw, host, n);
+        if (s == "tmix.a_lora_A.weight") return upload_h(w.aA, (int64_t)ra * C, host, n);
+        if (s == "tmix.a_lora_B.weight") return upload_h(w.aB, (int64_t)C * ra, host, n);
+        if (s == "tmix.g_lora_A.weight") return upload_h(w.gA, (int64_t)rg * C, host, n);
+        if (s == "tmix.g_lora_B.weight") return upload_h(w.gB, (int64_t)C * rg, host, n);
+        if (s == "tmix.v_lora_A.weight") return upload_h(w.vA, (int64_t)rv * C, host, n);
+        if (s == "tmix.v_lora_B.weight") return upload_h(w.vB, (int64_t)C * rv, host, n);
+        if (s == "tmix.r_proj.weight") return upload_q(w.r, host, n);
+        if (s == "tmix.k_proj.weight") return upload_q(w.k, host, n);
+        if (s == "tmix.v_proj.weight") return upload_q(w.v, host, n);
+        if (s == "tmix.o_proj.weight") return upload_q(w.o, host, n);
+        if (s == "cmix.key.weight") return upload_q(w.key, host, n);
+        if (s == "cmix.value.weight") return upload_q(w.value, host, n);
+        return fail(RWKV_E_SHAPE, "set_param: unknown parameter '%s'", name.c_str());
+    }
+
+    // Random init on the device with the x070 recipe (X070Init.swift:79-206):
+    // orthogonal matrices are drawn as Gaussians of the same element scale.
+    int init_random(uint64_t seed) {
+        const size_t maxn = std::max((size_t)V * C, (size_t)F * C);
+        __half* h16 = nullptr;
+        if (cudaMalloc(&h16, maxn * 2) != cudaSuccess) return fail(RWKV_E_CUDA, "init: staging allocation failed");
+        uint64_t salt = 0;
+        auto fill = [&](__half* dst, int64_t n, int mode, float a, float b) {
+            fill_f16_kernel<<<2048, 256>>>(dst, n, mode, a, b, seed * 0x9E3779B97F4A7C15ull + (++salt));
+        };
+        auto qfill = [&](QMat& q, int mode, float a, float b) {
+            fill(h16, (int64_t)q.OUT * q.IN, mode, a, b);
+            return launch_q_quantize(RWKV_F16, h16, q.wq, q.sc, q.bi, q.OUT, q.IN, 64, 4, 0);
+        };
+        const float s = 0.5f / sqrtf((float)C);
+        int rc = qfill(emb, 0, -1e-4f, 1e-4f);
+        if (!rc) rc = qfill(head, 1, (V > C ? 0.5f * sqrtf((float)V / C) : 0.5f) / sqrtf((float)std::max(V, C)), 0);
+        std::vector<float> ones(C, 1.f), zeros(C, 0.f), tmp(C);
+        cudaMemcpy(ln0w, ones.data(), C * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(lnow, ones.data(), C * 4, cudaMemcpyHostToDevice);
+        const int N = cfg.head_size;
+        std::vector<float> lin(C), zz(C);
+        for (int i = 0; i < C; i++) {
+            lin[i] = (float)i / (C - 1) - 0.5f;
+            const float z = ((float)(i % N) - (N - 1) / 2.0f) / ((N - 1) / 2.0f);
+            zz[i] = z * fabsf(z);
+        }
+        auto curve = [&](double kk) {
+            for (int i = 0; i < C; i++) tmp[i] = (float)(1.0 - pow((double)i / C, kk));
+            return tmp.data();
+        };
+        for (int l = 0; l < L && !rc; l++) {
+            LayerW& w = lw[l];
+            const double r01 = L > 1 ? (double)l / (L - 1) : 0.0, r1a = 1.0 - (double)l / L;
+            cudaMemcpy(w.ln1w, ones.data(), C * 4, cudaMemcpyHostToDevice);
+            cudaMemcpy(w.ln2w, ones.data(), C * 4, cudaMemcpyHostToDevice);
+            const double ks[6] = {0.2, 0.9, 0.7, 0.7, 0.9, 0.2};
+            for (int m = 0; m < 6; m++)
+                cudaMemcpy(w.coef6 + (size_t)m * C, curve(ks[m] * r1a), C * 4, cudaMemcpyHostToDevice);
+            const double ex = 1.0 + pow(r01, 0.3);
+            for (int i = 0; i < C; i++)
+                tmp[i] = (float)(-6.0 + 6.0 * pow((double)i / (C - 1), ex)) + 0.5f + zz[i] * 2.5f;
+            cudaMemcpy(w.wbias, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            for (int i = 0; i < C; i++) tmp[i] = -0.19f + zz[i] * 0.3f + lin[i] * 0.4f;
+            cudaMemcpy(w.abias, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            for (int i = 0; i < C; i++) tmp[i] = 0.73f - lin[i] * 0.4f;
+            cudaMemcpy(w.vbias, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            for (int i = 0; i < C; i++) tmp[i] = 0.71f - lin[i] * 0.1f;
+            cudaMemcpy(w.kkw, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            std::fill(tmp.begin(), tmp.end(), 1.02f);
+            cudaMemcpy(w.kaw, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            std::fill(tmp.begin(), tmp.end(), -0.04f);
+            cudaMemcpy(w.rkw, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            std::fill(tmp.begin(), tmp.end(), (float)pow((double)(l + 1) / L, 0.7));
+            cudaMemcpy(w.lnxw, tmp.data(), C * 4, cudaMemcpyHostToDevice);
+            cudaMemcpy(w.cxk, curve(pow(r1a, 4)), C * 4, cudaMemcpyHostToDevice);
+            // low-rank: A = 0 (already zero), B ~ orthogonal * 0.1
+            fill(w.wB, (int64_t)C * rw, 1, 0.1f / sqrtf((float)C), 0);
+            fill(w.aB, (int64_t)C * ra, 1, 0.1f / sqrtf((float)C), 0);
+            fill(w.gB, (int64_t)C * rg, 1, 0.1f / sqrtf((float)C), 0);
+            if (l > 0) fill(w.vB, (int64_t)C * rv, 1, 0.1f / sqrtf((float)C), 0);
+            rc = qfill(w.r, 0, -s, s);
+            if (!rc) rc = qfill(w.k, 0, -0.1f * s, 0.1f * s);
+            if (!rc) rc = qfill(w.v, 0, -s, s);
+            if (!rc) rc = qfill(w.o, 0, 0.f, 0.f);
+            if (!rc) rc = qfill(w.key, 0, -s, s);
+            if (!rc) rc = qfill(w.value, 0, 0.f, 0.f);
+        }
+        cudaDeviceSynchronize();
+        cudaFree(h16);
+        if (rc) return rc;
+        return check_launch("init_random");
+    }
+
+    // ----- one decode step on `R` rows: ids -> logits, ids <- argmax
+
+    int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
+        if (f16act) {
+            cudaError_t e = fmt == 0 ? launch_gemv_mma<0>(jobs, nj, R, st) : launch_gemv_mma<1>(jobs, nj, R, st);
+            return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemv: %s", cudaGetErrorString(e));
+        }
+        int maxo = 0;
+        for (int i = 0; i < nj; i++) maxo = std::max(maxo, jobs.j[i].OUT);
+        dim3 grid((maxo + 7) / 8, nj, (R + 7) / 8);
+        if (fmt == 0) gemv_cc_kernel<0><<<grid, 256, 0, st>>>(jobs, R);
+        else gemv_cc_kernel<1><<<grid, 256, 0, st>>>(jobs, R);
+        return check_launch("gemv_cc_kernel");
+    }
+
+    static GemvJob qjob(const QMat& q, const void* x, int xs, int act, int out, void* y, int ys,
+                        const float* bias = nullptr) {
+        GemvJob j{};
+        j.w = q.wq; j.scales = q.sc; j.biases = q.bi; j.x = x; j.x_stride = xs;
+        j.OUT = q.OUT; j.IN = q.IN; j.act = act; j.out = out; j.y = y; j.y_stride = ys; j.bias = bias;
+        return j;
+    }
+    static GemvJob hjob(const __half* W, int OUT, int IN, const void* x, int xs, int act, int out,
+                        void* y, int ys, const float* bias = nullptr) {
+        GemvJob j{};
+        j.w = W; j.x = x; j.x_stride = xs; j.OUT = OUT; j.IN = IN; j.act = act; j.out = out;
+        j.y = y; j.y_stride = ys; j.bias = bias;
+        return j;
+    }
+
+    template <typename A>
+    int step_body(int R, cudaStream_t st) {
+        const size_t RC = (size_t)R * C;
+        const int aout = f16act ? OUT_F16 : OUT_F32;
+        A* mixp = (A*)mix;
+        A* hidp = (A*)hidden;
+        int rc;
+        x070_embed_kernel<<<R, GLUE_T, 0, st>>>(ids, emb.wq, emb.sc, emb.bi, nullptr, ln0w, ln0b, x, C, V);
+        if ((rc = check_launch("x070_embed_kernel"))) return rc;
+        for (int l = 0; l < L; l++) {
+            LayerW& w = lw[l];
+            float* ts = tshift + (size_t)l * Rmax * C;
+            float* cs = cshift + (size_t)l * Rmax * C;
+            float* st8 = wkv + (size_t)l * Rmax * H * 64 * 64;
+            x070_tmix_in_kernel<A><<<R, GLUE_T, 0, st>>>(x, w.ln1w, w.ln1b, ts, w.coef6, mixp, R, C);
+            if ((rc = check_launch("x070_tmix_in_kernel"))) return rc;
+            auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
+            GemvJobs J{};
+            J.j[0] = qjob(w.r, M(0), C, ACT_NONE, OUT_F32, r, C);
+            J.j[1] = qjob(w.k, M(2), C, ACT_NONE, OUT_F32, k, C);
+            J.j[2] = qjob(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
+            if ((rc = gemv(0, J, 3, R, st))) return rc;
+            // low-rank down: w (tanh), a, g (sigmoid), v
+            GemvJobs D{};
+            int nd = 0;
+            D.j[nd++] = hjob(w.wA, rw, C, M(1), C, ACT_TANH, aout, hidp, hid);
+            D.j[nd++] = hjob(w.aA, ra, C, M(4), C, ACT_NONE, aout, hidp + rw, hid);
+            D.j[nd++] = hjob(w.gA, rg, C, M(5), C, ACT_SIGMOID, aout, hidp + rw + ra, hid);
+            if (l > 0) D.j[nd++] = hjob(w.vA, rv, C, M(3), C, ACT_NONE, aout, hidp + rw + ra + rg, hid);
+            if ((rc = gemv(1, D, nd, R, st))) return rc;
+            GemvJobs U{};
+            int nu = 0;
+            U.j[nu++] = hjob(w.wB, C, rw, hidp, hid, ACT_DECAY, OUT_F32, wdec, C, w.wbias);
+            U.j[nu++] = hjob(w.aB, C, ra, hidp + rw, hid, ACT_SIGMOID_BIAS, OUT_F32, a, C, w.abias);
+            U.j[nu++] = hjob(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, g, C);
+            if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
+            if ((rc = gemv(1, U, nu, R, st))) return rc;
+            x070_wkv_kernel<A><<<R * H, 256, 0, st>>>(r, wdec, k, v, a, vv, vfirst, w.kkw, w.kaw, w.rkw,
+                                                      w.lnxw, w.lnxb, g, st8, (A*)tail, H, l == 0);
+            if ((rc = check_launch("x070_wkv_kernel"))) return rc;
+            GemvJobs O{};
+            O.j[0] = qjob(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C);
+            if ((rc = gemv(0, O, 1, R, st))) return rc;
+            x070_cmix_in_kernel<A><<<R, GLUE_T, 0, st>>>(x, w.ln2w, w.ln2b, cs, w.cxk, (A*)xk, C);
+            if ((rc = check_launch("x070_cmix_in_kernel"))) return rc;
+            GemvJobs K{};
+            K.j[0] = qjob(w.key, xk, C, ACT_RELU2, aout, ffn, F);
+            if ((rc = gemv(0, K, 1, R, st))) return rc;
+            GemvJobs Vv{};
+            Vv.j[0] = qjob(w.value, ffn, F, ACT_NONE, OUT_ADD_F32, x, C);
+            if ((rc = gemv(0, Vv, 1, R, st))) return rc;
+        }
+        x070_ln_out_kernel<A><<<R, GLUE_T, 0, st>>>(x, lnow, lnob, (A*)lnout, C);
+        if ((rc = check_launch("x070_ln_out_kernel"))) return rc;
+        GemvJobs Hd{};
+        Hd.j[0] = qjob(head, lnout, C, ACT_NONE, OUT_F32, logits, V);
+        if ((rc = gemv(0, Hd, 1, R, st))) return rc;
+        x070_argmax_kernel<<<R, GLUE_T, 0, st>>>(logits, V, ids);
+        return check_launch("x070_argmax_kernel");
+    }
+
+    int run_step(int R, cudaStream_t st) {
+        return f16act ? step_body<__half>(R, st) : step_body<float>(R, st);
+    }
+
+    int graph_step(int R, cudaStream_t st) {
+        auto it = graphs.find(R);
+        if (it == graphs.end()) {
+            cudaGraph_t gph;
+            if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+                return fail(RWKV_E_CUDA, "graph capture could not start (the stream must not be the legacy default stream)");
+            int rc = run_step(R, st);
+            cudaError_t e = cudaStreamEndCapture(st, &gph);
+            if (rc) return rc;
+            if (e != cudaSuccess) return fail(RWKV_E_CUDA, "graph capture: %s", cudaGetErrorString(e));
+            cudaGraphExec_t ex;
+            e = cudaGraphInstantiate(&ex, gph, 0);
+            cudaGraphDestroy(gph);
+            if (e != cudaSuccess) return fail(RWKV_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            it = graphs.emplace(R, ex).first;
+        }
+        cudaError_t e = cudaGraphLaunch(it->second, st);
+        return e == cudaSuccess ? ok() : fail(RWKV_E_CUDA, "graph launch: %s", cudaGetErrorString(e));
+    }
+
+    // graph_step on any stream, the legacy default stream included.
+    int graph_step_any(int R, cudaStream_t st) {
+        if (st != nullptr) return graph_step(R, st);
+        cudaEventRecord(ev_in, st);
+        cudaStreamWaitEvent(own, ev_in, 0);
+        int rc = graph_step(R, own);
+        cudaEventRecord(ev_out, own);
+        cudaStreamWaitEvent(st, ev_out, 0);
+        return rc;
+    }
+
+    int launches_per_step() const { return 2 + L * 10 + 2; }
+};
+
+}  // namespace rwkv
+
+using namespace rwkv;
+
+extern "C" {
+
+int rwkv_x070_create(const rwkv_x070_config* cfg, rwkv_x070_t* out) {
+    RWKV_REQUIRE(cfg && out, RWKV_E_NULL, "rwkv_x070_create: NULL argument");
+    const rwkv_x070_config& c = *cfg;
+    RWKV_REQUIRE(c.n_layer >= 1 && c.vocab >= 1 && c.max_rows >= 1, RWKV_E_SHAPE, "rwkv_x070_create: sizes");
+    RWKV_REQUIRE(c.head_size == 64 && c.n_embd % 64 == 0 && c.n_embd <= GLUE_T * GLUE_PER, RWKV_E_UNSUPPORTED,
+                 "rwkv_x070_create: n_embd %d must be a multiple of 64 up to 4096, head 64", c.n_embd);
+    RWKV_REQUIRE(c.ffn % 64 == 0, RWKV_E_UNSUPPORTED, "rwkv_x070_create: ffn %d must be a multiple of 64", c.ffn);
+    RWKV_REQUIRE(c.rank_w % 16 == 0 && c.rank_a % 16 == 0 && c.rank_v % 16 == 0 && c.rank_g % 16 == 0,
+                 RWKV_E_UNSUPPORTED, "rwkv_x070_create: low-rank sizes must be multiples of 16");
+    RWKV_REQUIRE(c.quant_bits == 4 && c.quant_group == 64, RWKV_E_UNSUPPORTED,
+                 "rwkv_x070_create: the base must be 4-bit group-64");
+    RWKV_REQUIRE(c.act_dtype == RWKV_F16 || c.act_dtype == RWKV_F32, RWKV_E_DTYPE, "rwkv_x070_create: act dtype");
+    X070* m = new X070(c);
+    if (m->alloc_failed) {
+        delete m;
+        return fail(RWKV_E_CUDA, "rwkv_x070_create: device allocation failed");
+    }
+    *out = reinterpret_cast<rwkv_x070_t>(m);
+    return ok();
+}
+
+int rwkv_x070_destroy(rwkv_x070_t h) {
+    delete reinterpret_cast<X070*>(h);
+    return ok();
+}
+
+int rwkv_x070_set_param(rwkv_x070_t h, const char* name, const float* host, int64_t n) {
+    RWKV_REQUIRE(h && name && host, RWKV_E_NULL, "rwkv_x070_set_param: NULL argument");
+    return reinterpret_cast<X070*>(h)->set_param(name, host, n);
+}
+
+int rwkv_x070_init_random(rwkv_x070_t h, uint64_t seed) {
+    RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_init_random: NULL handle");
+    return reinterpret_cast<X070*>(h)->init_random(seed);
+}
+
+int rwkv_x070_reset_state(rwkv_x070_t h, int rows, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_reset_state: NULL handle");
+    X070& m = *reinterpret_cast<X070*>(h);
+    RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax, RWKV_E_SHAPE, "rows %d not in 1..%d", rows, m.Rmax);
+    cudaStream_t st = (cudaStream_t)stream;
+    for (int l = 0; l < m.L; l++) {
+        cudaMemsetAsync(m.wkv + (size_t)l * m.Rmax * m.H * 4096, 0, (size_t)rows * m.H * 4096 * 4, st);
+        cudaMemsetAsync(m.tshift + (size_t)l * m.Rmax * m.C, 0, (size_t)rows * m.C * 4, st);
+        cudaMemsetAsync(m.cshift + (size_t)l * m.Rmax * m.C, 0, (size_t)rows * m.C * 4, st);
+    }
+    return check_launch("rwkv_x070_reset_state");
+}
+
+int rwkv_x070_step(rwkv_x070_t h, const int32_t* ids, int rows, float* logits, int32_t* next_ids,
+                   int use_graph, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_step: NULL handle");
+    X070& m = *reinterpret_cast<X070*>(h);
+    RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax, RWKV_E_SHAPE, "rows %d not in 1..%d", rows, m.Rmax);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (ids) cudaMemcpyAsync(m.ids, ids, rows * 4, cudaMemcpyDeviceToDevice, st);
+    int rc = use_graph ? m.graph_step_any(rows, st) : m.run_step(rows, st);
+    if (rc) return rc;
+    if (logits) cudaMemcpyAsync(logits, m.logits, (size_t)rows * m.V * 4, cudaMemcpyDeviceToDevice, st);
+    if (next_ids) cudaMemcpyAsync(next_ids, m.ids, rows * 4, cudaMemcpyDeviceToDevice, st);
+    return check_launch("rwkv_x070_step");
+}
+
+int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int prompt_len,
+                       int n_new, int32_t* out_host, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h && prompt_host && out_host, RWKV_E_NULL, "rwkv_x070_generate: NULL argument");
+    X070& m = *reinterpret_cast<X070*>(h);
+    RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax && prompt_len >= 1 && n_new >= 0, RWKV_E_SHAPE,
+                 "rwkv_x070_generate: rows %d prompt %d new %d", rows, prompt_len, n_new);
+    cudaStream_t st = (cudaStream_t)stream;
+    std::vector<int32_t> col(rows);
+    for (int t = 0; t < prompt_len; t++) {
+        for (int n = 0; n < rows; n++) col[n] = prompt_host[(size_t)n * prompt_len + t];
+        cudaMemcpyAsync(m.ids, col.data(), rows * 4, cudaMemcpyHostToDevice, st);
+        if (int rc = m.graph_step_any(rows, st)) return rc;
+    }
+    for (int s = 0; s < n_new; s++) {
+        cudaMemcpyAsync(col.data(), m.ids, rows * 4, cudaMemcpyDeviceToHost, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "generate: sync failed");
+        for (int n = 0; n < rows; n++) out_host[(size_t)n * n_new + s] = col[n];
+        if (s + 1 < n_new)
+            if (int rc = m.graph_step_any(rows, st)) return rc;
+    }
+    return check_launch("rwkv_x070_generate");
+}
+
+int64_t rwkv_x070_weight_bytes(rwkv_x070_t h) { return h ? reinterpret_cast<X070*>(h)->weight_bytes : 0; }
+
+int rwkv_x070_launches_per_step(rwkv_x070_t h) {
+    return h ? reinterpret_cast<X070*>(h)->launches_per_step() : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,342 @@
+// Glue kernels of the x070 recurrent decode step (one token per row), the
+// elementwise and reduction work between the projections:
+//   embedding row (4-bit) + LayerNorm ln0        (X070Generation.swift:483-486)
+//   ln1 + token shift + six lerps                (tmixStep, :201-230)
+//   kk / k / v prep + WKV step + tail            (:258-291, fused)
+//   ln2 + token shift + lerp                     (cmixStep, :310-316)
+//   ln_out and greedy argmax                     (:496-497, GPUSampler.swift:90)
+// One CTA per row (or per (row, head) for the WKV part); LayerNorm is the
+// reference's manual fp32 formula (two passes: mean, then mean of squares of
+// the deviations; eps 1e-5).
+#pragma once
+
+#include "common.cuh"
+
+namespace rwkv {
+
+constexpr int GLUE_T = 256;
+constexpr int GLUE_PER = 16;  // values per thread: C <= 4096
+
+__device__ __forceinline__ float block_sum256(float v, float* sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    v = (threadIdx.x < GLUE_T / 32) ? sh[threadIdx.x] : 0.f;
+    if (warp == 0) v = warp_sum(v);
+    if (threadIdx.x == 0) sh[32] = v;
+    __syncthreads();
+    v = sh[32];
+    __syncthreads();
+    return v;
+}
+
+template <typename A>
+__device__ __forceinline__ void st_act(A* p, float v) { *p = from_f<A>(v); }
+
+// Row LayerNorm of v[] (thread holds columns tid + 256*i), in place.
+__device__ __forceinline__ void ln_regs(float v[GLUE_PER], int C, const float* __restrict__ w,
+                                        const float* __restrict__ b, float* sh) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c < C) s += v[i];
+    }
+    const float mean = block_sum256(s, sh) / (float)C;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c < C) {
+            const float d = v[i] - mean;
+            q += d * d;
+        }
+    }
+    const float den = sqrtf(block_sum256(q, sh) / (float)C + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c < C) v[i] = (v[i] - mean) / den * w[c] + b[c];
+    }
+}
+
+// ids -> x = ln0(emb[id]).  Embedding in the 4-bit group-64 container
+// (emb_wq != NULL) or dense fp16.
+__global__ void __launch_bounds__(GLUE_T)
+x070_embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ emb_wq,
+                  const __half* __restrict__ emb_sc, const __half* __restrict__ emb_bi,
+                  const __half* __restrict__ emb_dense, const float* __restrict__ lnw,
+                  const float* __restrict__ lnb, float* __restrict__ x, int C, int vocab) {
+    __shared__ float sh[33];
+    const int n = blockIdx.x;
+    int id = ids[n];
+    id = min(max(id, 0), vocab - 1);
+    float v[GLUE_PER];
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        v[i] = 0.f;
+        if (c < C) {
+            if (emb_wq) {
+                const uint32_t word = emb_wq[(int64_t)id * (C / 8) + c / 8];
+                const float q = (float)((word >> (4 * (c & 7))) & 15u);
+                const int64_t gi = (int64_t)id * (C / 64) + c / 64;
+                v[i] = q * __half2float(emb_sc[gi]) + __half2float(emb_bi[gi]);
+            } else {
+                v[i] = __half2float(emb_dense[(int64_t)id * C + c]);
+            }
+        }
+    }
+    ln_regs(v, C, lnw, lnb, sh);
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c < C) x[(int64_t)n * C + c] = v[i];
+    }
+}
+
+// tmix input: xl = ln1(x); xx = shift - xl; shift = xl;
+// mix[m] = xl + xx * coef[m] for m = r, w, k, v, a, g  ([6][R][C], act type).
+template <typename A>
+__global__ void __launch_bounds__(GLUE_T)
+x070_tmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
+                    const float* __restrict__ lnb, float* __restrict__ shift,
+                    const float* __restrict__ coef, A* __restrict__ mix, int R, int C) {
+    __shared__ float sh[33];
+    const int n = blockIdx.x;
+    float v[GLUE_PER];
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
+    }
+    ln_regs(v, C, lnw, lnb, sh);
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c >= C) continue;
+        const int64_t o = (int64_t)n * C + c;
+        const float xx = shift[o] - v[i];
+        shift[o] = v[i];
+#pragma unroll
+        for (int m = 0; m < 6; m++) st_act(mix + (int64_t)m * R * C + o, v[i] + xx * coef[m * C + c]);
+    }
+}
+
+// cmix input: xl = ln2(x); xx = shift - xl; shift = xl; out = xl + xx * coef.
+template <typename A>
+__global__ void __launch_bounds__(GLUE_T)
+x070_cmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
+                    const float* __restrict__ lnb, float* __restrict__ shift,
+                    const float* __restrict__ coef, A* __restrict__ out, int C) {
+    __shared__ float sh[33];
+    const int n = blockIdx.x;
+    float v[GLUE_PER];
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
+    }
+    ln_regs(v, C, lnw, lnb, sh);
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c >= C) continue;
+        const int64_t o = (int64_t)n * C + c;
+        const float xx = shift[o] - v[i];
+        shift[o] = v[i];
+        st_act(out + o, v[i] + xx * coef[c]);
+    }
+}
+
+template <typename A>
+__global__ void __launch_bounds__(GLUE_T)
+x070_ln_out_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
+                   const float* __restrict__ lnb, A* __restrict__ out, int C) {
+    __shared__ float sh[33];
+    const int n = blockIdx.x;
+    float v[GLUE_PER];
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
+    }
+    ln_regs(v, C, lnw, lnb, sh);
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        if (c < C) st_act(out + (int64_t)n * C + c, v[i]);
+    }
+}
+
+// WKV part of tmixStep for one (row, head), 256 threads = 64 state rows x 4
+// lanes x 16 key columns:
+//   kk = l2norm(k * k_k);  k' = k * (1 + (a - 1) * k_a)
+//   v' = v (layer 0, also stored as v_first) or v + (v_first - v) * vv
+//   step with (r, w, k', v', -kk, kk * a); tail -> out (act type).
+template <typename A>
+__global__ void __launch_bounds__(256)
+x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
+                const float* __restrict__ kraw, const float* __restrict__ vraw,
+                const float* __restrict__ a, const float* __restrict__ vv,
+                float* __restrict__ vfirst, const float* __restrict__ kkw,
+                const float* __restrict__ kaw, const float* __restrict__ rkw,
+                const float* __restrict__ lnxw, const float* __restrict__ lnxb,
+                const float* __restrict__ g, float* __restrict__ state, A* __restrict__ out,
+                int H, int layer0) {
+    constexpr int N = 64, LPR = 4, CPL = 16;
+    __shared__ float ysh[N], vsh[N];
+    const int rh = blockIdx.x;
+    const int hi = rh % H;
+    const int dv = threadIdx.x / LPR, q = threadIdx.x % LPR, c0 = q * CPL;
+    const size_t vb = (size_t)rh * N;   // [R, H, N] element base of this (row, head)
+    const size_t hb = (size_t)hi * N;   // [H, N] parameter base
+    // per-column vectors for this lane
+    float kk[CPL], kp[CPL], aa[CPL];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPL; j++) {
+        const int c = c0 + j;
+        const float kr = kraw[vb + c];
+        kk[j] = kr * kkw[hb + c];
+        ss += kk[j] * kk[j];
+        aa[j] = a[vb + c];
+        kp[j] = kr * (1.0f + (aa[j] - 1.0f) * kaw[hb + c]);
+    }
+    ss = group_sum<LPR>(ss);
+    const float inv = 1.0f / sqrtf(ss + 1e-12f);
+#pragma unroll
+    for (int j = 0; j < CPL; j++) kk[j] *= inv;
+    // value row dv
+    float vd = vraw[vb + dv];
+    if (layer0) {
+        if (q == 0) vfirst[vb + dv] = vd;
+    } else {
+        const float f = vfirst[vb + dv];
+        vd = vd + (f - vd) * vv[vb + dv];
+    }
+    if (q == 0) vsh[dv] = vd;
+    float* hp = state + (size_t)rh * N * N + (size_t)dv * N + c0;
+    float s[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; j += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(hp + j);
+        s[j] = t4.x; s[j + 1] = t4.y; s[j + 2] = t4.z; s[j + 3] = t4.w;
+    }
+    // sa = S a_wkv with a_wkv = -kk
+    float sa0 = 0.f, sa1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPL; j += 2) {
+        sa0 = fmaf(s[j], -kk[j], sa0);
+        sa1 = fmaf(s[j + 1], -kk[j + 1], sa1);
+    }
+    const float sa = group_sum<LPR>(sa0 + sa1);
+    float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPL; j++) {
+        const int c = c0 + j;
+        const float bw = kk[j] * aa[j];
+        s[j] = fmaf(wdec[vb + c], s[j], fmaf(vd, kp[j], sa * bw));
+        if (j & 1) y1 = fmaf(s[j], r[vb + c], y1);
+        else y0 = fmaf(s[j], r[vb + c], y0);
+    }
+    const float yy = group_sum<LPR>(y0 + y1);
+#pragma unroll
+    for (int j = 0; j < CPL; j += 4)
+        *reinterpret_cast<float4*>(hp + j) = make_float4(s[j], s[j + 1], s[j + 2], s[j + 3]);
+    if (q == 0) ysh[dv] = yy;
+    // bonus partial: sum over this lane's columns of r * k' * r_k (row 0 lanes only)
+    float dpp = 0.f;
+    if (dv == 0) {
+#pragma unroll
+        for (int j = 0; j < CPL; j++) dpp += r[vb + c0 + j] * kp[j] * rkw[hb + c0 + j];
+    }
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int l = threadIdx.x;  // lanes 0..3 are row 0's four lanes
+    float dp = (l < LPR) ? dpp : 0.f;
+    dp = warp_sum(dp);
+    const float x0 = ysh[l], x1 = ysh[l + 32];
+    const float mean = warp_sum(x0 + x1) * (1.0f / N);
+    const float d0 = x0 - mean, d1 = x1 - mean;
+    const float var = warp_sum(d0 * d0 + d1 * d1) * (1.0f / N);
+    const float invs = 1.0f / sqrtf(var + 64e-5f);
+    const float o0 = (d0 * invs * lnxw[hb + l] + lnxb[hb + l] + dp * vsh[l]) * g[vb + l];
+    const float o1 = (d1 * invs * lnxw[hb + l + 32] + lnxb[hb + l + 32] + dp * vsh[l + 32]) * g[vb + l + 32];
+    st_act(out + vb + l, o0);
+    st_act(out + vb + l + 32, o1);
+}
+
+// Greedy sampler: first index of the maximum logit per row.
+__global__ void __launch_bounds__(GLUE_T)
+x070_argmax_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ ids) {
+    __shared__ float sv[GLUE_T / 32];
+    __shared__ int si[GLUE_T / 32];
+    const int n = blockIdx.x;
+    const float* p = logits + (int64_t)n * V;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = threadIdx.x; c < V; c += GLUE_T) {
+        const float v = p[c];
+        if (v > best || (v == best && c < bi)) { best = v; bi = c; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < GLUE_T / 32; w++)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+        ids[n] = bi;
+    }
+}
+
+// CUDA-core GEMV for fp32 activations (the fp32 parity mode): one warp per
+// output row, lanes strided over k, up to 8 input rows per launch tile.
+template <int FMT>
+__global__ void __launch_bounds__(256)
+gemv_cc_kernel(const GemvJobs jobs, int R) {
+    const GemvJob& jb = jobs.j[blockIdx.y];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int o = blockIdx.x * 8 + warp;
+    if (o >= jb.OUT) return;
+    const int n0 = blockIdx.z * 8;
+    const int Rz = min(R - n0, 8);
+    const float* x = (const float*)jb.x + (int64_t)n0 * jb.x_stride;
+    float acc[8];
+#pragma unroll
+    for (int n = 0; n < 8; n++) acc[n] = 0.f;
+    if (FMT == 0) {
+        const uint32_t* W = (const uint32_t*)jb.w + (int64_t)o * (jb.IN / 8);
+        const int NG = jb.IN / 64;
+        for (int c = lane; c < jb.IN; c += 32) {
+            const float q = (float)((W[c / 8] >> (4 * (c & 7))) & 15u);
+            const int gi = o * NG + c / 64;
+            const float wv = q * __half2float(jb.scales[gi]) + __half2float(jb.biases[gi]);
+#pragma unroll
+            for (int n = 0; n < 8; n++)
+                if (n < Rz) acc[n] = fmaf(wv, x[(int64_t)n * jb.x_stride + c], acc[n]);
+        }
+    } else {
+        const __half* W = (const __half*)jb.w + (int64_t)o * jb.IN;
+        for (int c = lane; c < jb.IN; c += 32) {
+            const float wv = __half2float(W[c]);
+#pragma unroll
+            for (int n = 0; n < 8; n++)
+                if (n < Rz) acc[n] = fmaf(wv, x[(int64_t)n * jb.x_stride + c], acc[n]);
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; n++) {
+        const float v = warp_sum(acc[n]);
+        if (lane == 0 && n < Rz) epilogue(jb, o, n0 + n, v);
+    }
+}
+
+}  // namespace rwkv

@@ -1,0 +1,141 @@
+"""Host mirror of X070Config / X070Backbone's decode API over the C runtime.
+
+`X070Backbone.step` / `generate` / `generateBatch` keep the reference's names
+(Sources/RWKVGen/X070Generation.swift:449-498, Generate.swift:112-202,
+BatchGenerate.swift:69-116); the model, its state and every kernel live in
+librwkvcuda (rwkv_x070_*).  torch only provides device buffers and the stream.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import F16, F32, call
+
+
+def lora_ranks(D: int):
+    """x070 low-rank sizes, rwkvMetal formula (X070Init.swift:46-52)."""
+    def f(c, p):
+        return max(32, int(np.floor(c * D ** p / 32 + 0.5)) * 32)
+    return {"w": f(1.8, 0.5), "a": f(1.8, 0.5), "v": f(1.3, 0.5), "g": f(0.6, 0.8)}
+
+
+@dataclass
+class X070Config:
+    """X070Backbone.swift:24-37."""
+    nLayer: int
+    nEmbd: int
+    vocab: int
+    headSize: int = 64
+    ffnMultiplier: float = 4.0
+
+    @property
+    def nHead(self):
+        return self.nEmbd // self.headSize
+
+    @property
+    def ffn(self):
+        return int(self.nEmbd * self.ffnMultiplier / 32) * 32
+
+
+class _Cfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "n_layer", "n_embd", "head_size", "vocab", "ffn", "rank_w", "rank_a", "rank_v", "rank_g",
+        "quant_bits", "quant_group", "act_dtype", "max_rows")]
+
+
+class X070Backbone:
+    """x070 model over a 4-bit group-64 QLoRA base, decoded recurrently.
+
+    act="f16" feeds the projections fp16 activations (tensor-core GEMVs);
+    act="f32" keeps activations fp32 end to end (the parity path)."""
+
+    def __init__(self, cfg: X070Config, max_rows: int = 1, act: str = "f16"):
+        self.cfg = cfg
+        r = lora_ranks(cfg.nEmbd)
+        c = _Cfg(cfg.nLayer, cfg.nEmbd, cfg.headSize, cfg.vocab, cfg.ffn, r["w"], r["a"], r["v"],
+                 r["g"], 4, 64, F16 if act == "f16" else F32, max_rows)
+        h = ctypes.c_void_p()
+        call("rwkv_x070_create", ctypes.byref(c), ctypes.byref(h))
+        self.h = h
+        self.max_rows = max_rows
+        self.ranks = r
+
+    def close(self):
+        if self.h:
+            _lib.lib().rwkv_x070_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---------------------------------------------------------------- weights
+    def load(self, weights: dict):
+        """Reference-named weights (numpy / torch, any float dtype)."""
+        for name, v in weights.items():
+            a = np.ascontiguousarray(np.asarray(v.cpu() if torch.is_tensor(v) else v, np.float32))
+            call("rwkv_x070_set_param", self.h, name.encode(), a.ctypes.data_as(ctypes.c_void_p),
+                 a.size)
+        return self
+
+    def init_random(self, seed: int = 0):
+        """Device-side random init with the x070 recipe (X070Init.weights)."""
+        call("rwkv_x070_init_random", self.h, ctypes.c_uint64(seed))
+        return self
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(_lib.lib().rwkv_x070_weight_bytes(self.h))
+
+    @property
+    def launches_per_step(self) -> int:
+        return int(_lib.lib().rwkv_x070_launches_per_step(self.h))
+
+    # ----------------------------------------------------------------- decode
+    @staticmethod
+    def _s():
+        return _lib.P(torch.cuda.current_stream().cuda_stream)
+
+    def reset(self, rows: int):
+        """Fresh (zero) state for rows 0..rows-1."""
+        call("rwkv_x070_reset_state", self.h, rows, self._s())
+
+    def step(self, ids, use_graph: bool = False):
+        """One token per row (ids: int tensor [rows]) -> logits [rows, vocab] fp32.
+        The state advances in place (X070Backbone.step(_:state:))."""
+        ids = torch.as_tensor(ids, dtype=torch.int32, device="cuda").reshape(-1).contiguous()
+        rows = ids.numel()
+        logits = torch.empty((rows, self.cfg.vocab), device="cuda", dtype=torch.float32)
+        call("rwkv_x070_step", self.h, _lib.P(ids.data_ptr()), rows, _lib.P(logits.data_ptr()),
+             None, int(use_graph), self._s())
+        return logits
+
+    def step_greedy(self, rows: int, ids=None, use_graph: bool = True):
+        """Device-resident greedy loop: feeds `ids` (or the previous argmax)."""
+        p = None
+        if ids is not None:
+            ids = torch.as_tensor(ids, dtype=torch.int32, device="cuda").reshape(-1).contiguous()
+            p = _lib.P(ids.data_ptr())
+        call("rwkv_x070_step", self.h, p, rows, None, None, int(use_graph), self._s())
+
+    def generateBatch(self, prompts, n_new: int):
+        """Greedy generation, host in / host out: prompts int [rows, T] (equal
+        lengths) -> new tokens int32 [rows, n_new].  State starts from zero."""
+        p = np.ascontiguousarray(np.asarray(prompts, np.int32))
+        rows, T = p.shape
+        self.reset(rows)
+        out = np.zeros((rows, n_new), np.int32)
+        call("rwkv_x070_generate", self.h, p.ctypes.data_as(ctypes.c_void_p), rows, T, n_new,
+             out.ctypes.data_as(ctypes.c_void_p), self._s())
+        return out
+
+    def generate(self, prompt, n_new: int):
+        """Single-row greedy generation (Generate.swift:112-202, argmax sampler)."""
+        return self.generateBatch(np.asarray(prompt, np.int32).reshape(1, -1), n_new)[0]
