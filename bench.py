@@ -233,8 +233,9 @@ class Decode15B:
     unit = "tok/s"
     L, C, V, PROMPT = 24, 2048, 65536, 128
 
-    def __init__(self, rows=64):
+    def __init__(self, rows=64, prompt=128):
         self.rows = rows
+        self.PROMPT = prompt
         self.metric = (f"x070 1.5B 4-bit decode tok/s (generateBatch greedy, {rows} rows/GPU, "
                        "fp16 activations)")
 
@@ -424,7 +425,7 @@ def run_reference(args, rank):
 
 def make_workload(args):
     if args.workload == "decode":
-        return Decode15B(args.rows)
+        return Decode15B(args.rows, args.prompt)
     return WORKLOADS[args.workload]()
 
 
@@ -435,6 +436,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
     ap.add_argument("--rows", type=int, default=64, help="decode rows per GPU")
+    ap.add_argument("--prompt", type=int, default=128, help="decode prompt tokens per row")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -251,6 +251,12 @@ int rwkv_x070_step(rwkv_x070_t model, const int32_t* ids, int rows, float* logit
  * recurrently, then n_new tokens per row into out [rows, n_new]. */
 int rwkv_x070_generate(rwkv_x070_t model, const int32_t* prompt_host, int rows, int prompt_len,
                        int n_new, int32_t* out_host, rwkv_stream_t stream);
+/* Step profiler (tracing): one eager step with a CUDA event after every
+ * launch; writes per-launch device milliseconds to ms_host[0..*count) and the
+ * launch names, '\n'-separated, to names_host.  Advances the state like a step.
+ * Stands in for DecodeBench's --step-profile (Sources/DecodeBench/main.swift:146-196). */
+int rwkv_x070_profile_step(rwkv_x070_t model, int rows, float* ms_host, int cap, char* names_host,
+                           int names_cap, int* count, rwkv_stream_t stream);
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t model);
 int rwkv_x070_launches_per_step(rwkv_x070_t model);
 

@@ -60,6 +60,7 @@ _SIGS = {
     "rwkv_x070_reset_state": [P, I, P],
     "rwkv_x070_step": [P, P, I, P, P, I, P],
     "rwkv_x070_generate": [P, P, I, I, I, P, P],
+    "rwkv_x070_profile_step": [P, I, P, I, P, I, P, P],
     "rwkv_x070_weight_bytes": [P],
     "rwkv_x070_launches_per_step": [P],
 }

@@ -14,7 +14,10 @@
 // then reduced across the warp with shuffles.  Two output rows per warp share
 // the x loads and the x sums.
 #include "common.cuh"
-#include "gemv_mma.cuh"
+#include <mutex>
+#include <unordered_map>
+
+#include "gemm_w4_wide.cuh"
 
 namespace rwkv {
 
@@ -255,6 +258,38 @@ static int dispatch_sdtype(int dt, F&& f) {
     }
 }
 
+// Library-owned split-K workspace of rwkv_q_gemm, one per device, allocated on
+// first use and kept until exit.
+struct GemmScratch {
+    float* ws = nullptr;
+    int* tickets = nullptr;
+    size_t floats = 0, tickets_n = 0;
+    int sm_count = 148;
+    std::mutex mu;
+};
+
+static GemmScratch* gemm_scratch() {
+    static std::mutex m;
+    static std::unordered_map<int, GemmScratch*> per_dev;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(m);
+    auto it = per_dev.find(dev);
+    if (it != per_dev.end()) return it->second;
+    GemmScratch* s = new GemmScratch();
+    cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, dev);
+    s->floats = (size_t)(4 * s->sm_count + 64) * GW_BM * 64;
+    s->tickets_n = 8192;
+    if (cudaMalloc(&s->ws, s->floats * 4) != cudaSuccess ||
+        cudaMalloc(&s->tickets, s->tickets_n * 4) != cudaSuccess ||
+        cudaMemset(s->tickets, 0, s->tickets_n * 4) != cudaSuccess) {
+        delete s;
+        return nullptr;
+    }
+    per_dev[dev] = s;
+    return s;
+}
+
 template <typename TX, typename TS, typename TY, int BITS>
 static void launch_quad(const void* x, const uint32_t* wq, const void* sc, const void* bi, void* y,
                         int r, int OUT, int IN, int group, int xs, int ys, cudaStream_t st) {
@@ -285,7 +320,7 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
         j.w = wq;
         j.scales = (const __half*)scales;
         j.biases = (const __half*)biases;
-        j.x = (const __half*)x;
+        j.x = x;
         j.x_stride = IN;
         j.OUT = OUT;
         j.IN = IN;
@@ -293,8 +328,24 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
         j.out = ydtype == RWKV_F32 ? OUT_F32 : OUT_F16;
         j.y = y;
         j.y_stride = OUT;
-        cudaError_t e = launch_gemv_mma<0>(jobs, 1, rows, st);
-        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemv_mma_kernel: %s", cudaGetErrorString(e));
+        GemmScratch* sc = gemm_scratch();
+        if (!sc) return fail(RWKV_E_CUDA, "rwkv_q_gemm: workspace allocation failed");
+        GemmPlan p = plan_any(jobs, 1, rows, sc->sm_count);
+        if (p.ws_floats > sc->floats || p.tickets > sc->tickets_n) {
+            p.S = 1;
+            p.ws_floats = p.tickets = 0;
+        }
+        GemmArgs ga{};
+        ga.jobs = jobs;
+        ga.njobs = 1;
+        ga.R = rows;
+        ga.ws = sc->ws;
+        ga.tickets = sc->tickets;
+        // the split-K workspace is shared by every call on the device: calls are
+        // serialised on the stream they are issued to
+        std::lock_guard<std::mutex> lk(sc->mu);
+        cudaError_t e = launch_any<0>(ga, p, st);
+        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemm_w4_kernel: %s", cudaGetErrorString(e));
         return ok();
     }
     return dispatch_dtype(xdtype, [&]<typename TX>() {

@@ -16,7 +16,7 @@
 #include <vector>
 
 #include "common.cuh"
-#include "gemv_mma.cuh"
+#include "gemm_w4_wide.cuh"
 #include "x070_kernels.cuh"
 
 namespace rwkv {
@@ -88,6 +88,7 @@ struct X070 {
     float *x, *r, *k, *v, *wdec, *a, *vv, *g, *vfirst, *logits;
     void *mix, *hidden, *tail, *xk, *ffn, *lnout;
     int32_t* ids;
+    unsigned long long* amax_keys;
     size_t act_bytes;
     std::map<int, cudaGraphExec_t> graphs;
     int64_t weight_bytes = 0;
@@ -95,6 +96,26 @@ struct X070 {
     // there is forwarded to this stream, ordered by events on both sides.
     cudaStream_t own = nullptr;
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    // split-K partials and tickets of the tensor-core GEMMs
+    float* gws = nullptr;
+    int* gtickets = nullptr;
+    size_t gws_floats = 0, gtickets_n = 0;
+    int sm_count = 148;
+    // step profiler: an event node after every launch of a captured step
+    bool profiling = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<std::string> prof_names;
+    cudaStream_t prof_stream = nullptr;
+    void mark(const char* name) {
+        if (!profiling) return;
+        if (prof_names.size() >= prof_ev.size()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            prof_ev.push_back(e);
+        }
+        cudaEventRecordWithFlags(prof_ev[prof_names.size()], prof_stream, cudaEventRecordExternal);
+        prof_names.push_back(name);
+    }
 
     bool alloc_failed = false;
 
@@ -167,9 +188,15 @@ struct X070 {
         ffn = alloc<char>((size_t)Rmax * F * act_bytes);
         lnout = alloc<char>(RC * act_bytes);
         ids = alloc<int32_t>(Rmax);
-        // the widest tensor-core tiles use 64 KB of shared memory
-        cudaFuncSetAttribute(gemv_mma_kernel<0, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-        cudaFuncSetAttribute(gemv_mma_kernel<1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        amax_keys = alloc<unsigned long long>(Rmax);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+        // split-K never exceeds ~2 waves of 64 x 64 tiles: (2*SMs + tiles) * 4096 floats
+        gws_floats = (size_t)(4 * sm_count + 64) * GW_BM * 64;
+        gtickets_n = 8192;
+        gws = alloc<float>(gws_floats);
+        gtickets = alloc<int>(gtickets_n);
         cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking);
         cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
@@ -177,6 +204,7 @@ struct X070 {
 
     ~X070() {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
         if (own) cudaStreamDestroy(own);
         if (ev_in) cudaEventDestroy(ev_in);
@@ -340,8 +368,13 @@ struct X070 {
 
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
         if (f16act) {
-            cudaError_t e = fmt == 0 ? launch_gemv_mma<0>(jobs, nj, R, st) : launch_gemv_mma<1>(jobs, nj, R, st);
-            return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemv: %s", cudaGetErrorString(e));
+            GemmPlan p = plan_any(jobs, nj, R, sm_count);
+            if (p.ws_floats > gws_floats || p.tickets > gtickets_n)
+                return fail(RWKV_E_WORKSPACE, "gemm: split-K plan exceeds the workspace");
+            GemmArgs ga{};
+            ga.jobs = jobs; ga.njobs = nj; ga.R = R; ga.ws = gws; ga.tickets = gtickets;
+            cudaError_t e = fmt == 0 ? launch_any<0>(ga, p, st) : launch_any<1>(ga, p, st);
+            return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm: %s", cudaGetErrorString(e));
         }
         int maxo = 0;
         for (int i = 0; i < nj; i++) maxo = std::max(maxo, jobs.j[i].OUT);
@@ -375,6 +408,7 @@ struct X070 {
         int rc;
         x070_embed_kernel<<<R, GLUE_T, 0, st>>>(ids, emb.wq, emb.sc, emb.bi, nullptr, ln0w, ln0b, x, C, V);
         if ((rc = check_launch("x070_embed_kernel"))) return rc;
+        mark("embed");
         for (int l = 0; l < L; l++) {
             LayerW& w = lw[l];
             float* ts = tshift + (size_t)l * Rmax * C;
@@ -382,12 +416,14 @@ struct X070 {
             float* st8 = wkv + (size_t)l * Rmax * H * 64 * 64;
             x070_tmix_in_kernel<A><<<R, GLUE_T, 0, st>>>(x, w.ln1w, w.ln1b, ts, w.coef6, mixp, R, C);
             if ((rc = check_launch("x070_tmix_in_kernel"))) return rc;
+            mark("tmix_in");
             auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
             GemvJobs J{};
             J.j[0] = qjob(w.r, M(0), C, ACT_NONE, OUT_F32, r, C);
             J.j[1] = qjob(w.k, M(2), C, ACT_NONE, OUT_F32, k, C);
             J.j[2] = qjob(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
             if ((rc = gemv(0, J, 3, R, st))) return rc;
+            mark("gemm_rkv");
             // low-rank down: w (tanh), a, g (sigmoid), v
             GemvJobs D{};
             int nd = 0;
@@ -396,6 +432,7 @@ struct X070 {
             D.j[nd++] = hjob(w.gA, rg, C, M(5), C, ACT_SIGMOID, aout, hidp + rw + ra, hid);
             if (l > 0) D.j[nd++] = hjob(w.vA, rv, C, M(3), C, ACT_NONE, aout, hidp + rw + ra + rg, hid);
             if ((rc = gemv(1, D, nd, R, st))) return rc;
+            mark("lora_down");
             GemvJobs U{};
             int nu = 0;
             U.j[nu++] = hjob(w.wB, C, rw, hidp, hid, ACT_DECAY, OUT_F32, wdec, C, w.wbias);
@@ -403,28 +440,41 @@ struct X070 {
             U.j[nu++] = hjob(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, g, C);
             if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
             if ((rc = gemv(1, U, nu, R, st))) return rc;
+            mark("lora_up");
             x070_wkv_kernel<A><<<R * H, 256, 0, st>>>(r, wdec, k, v, a, vv, vfirst, w.kkw, w.kaw, w.rkw,
                                                       w.lnxw, w.lnxb, g, st8, (A*)tail, H, l == 0);
             if ((rc = check_launch("x070_wkv_kernel"))) return rc;
+            mark("wkv_step_tail");
             GemvJobs O{};
             O.j[0] = qjob(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C);
             if ((rc = gemv(0, O, 1, R, st))) return rc;
+            mark("gemm_o");
             x070_cmix_in_kernel<A><<<R, GLUE_T, 0, st>>>(x, w.ln2w, w.ln2b, cs, w.cxk, (A*)xk, C);
             if ((rc = check_launch("x070_cmix_in_kernel"))) return rc;
+            mark("cmix_in");
             GemvJobs K{};
             K.j[0] = qjob(w.key, xk, C, ACT_RELU2, aout, ffn, F);
             if ((rc = gemv(0, K, 1, R, st))) return rc;
+            mark("gemm_key");
             GemvJobs Vv{};
             Vv.j[0] = qjob(w.value, ffn, F, ACT_NONE, OUT_ADD_F32, x, C);
             if ((rc = gemv(0, Vv, 1, R, st))) return rc;
+            mark("gemm_value");
         }
         x070_ln_out_kernel<A><<<R, GLUE_T, 0, st>>>(x, lnow, lnob, (A*)lnout, C);
         if ((rc = check_launch("x070_ln_out_kernel"))) return rc;
+        mark("ln_out");
         GemvJobs Hd{};
         Hd.j[0] = qjob(head, lnout, C, ACT_NONE, OUT_F32, logits, V);
         if ((rc = gemv(0, Hd, 1, R, st))) return rc;
-        x070_argmax_kernel<<<R, GLUE_T, 0, st>>>(logits, V, ids);
-        return check_launch("x070_argmax_kernel");
+        mark("gemm_head");
+        x070_argmax_kernel<<<dim3((V + ARGMAX_SLICE - 1) / ARGMAX_SLICE, R), GLUE_T, 0, st>>>(logits, V, amax_keys);
+        if ((rc = check_launch("x070_argmax_kernel"))) return rc;
+        mark("argmax");
+        x070_argmax_finish_kernel<<<(R + 127) / 128, 128, 0, st>>>(amax_keys, ids, R);
+        rc = check_launch("x070_argmax_finish_kernel");
+        mark("argmax_finish");
+        return rc;
     }
 
     int run_step(int R, cudaStream_t st) {
@@ -451,6 +501,67 @@ struct X070 {
         return e == cudaSuccess ? ok() : fail(RWKV_E_CUDA, "graph launch: %s", cudaGetErrorString(e));
     }
 
+    // One eager step with an event after every launch; per-launch device
+    // milliseconds into ms[] (up to cap) and their names, '\n'-separated.
+    // The step captured into a graph with an event node after every launch,
+    // replayed once: device-side per-launch milliseconds into ms[] (up to
+    // cap) and their names, '\n'-separated.
+    int profile_step(int R, cudaStream_t st, float* ms, int cap, char* names, int names_cap, int* count) {
+        cudaStream_t cs = st ? st : own;
+        if (!st) {
+            cudaEventRecord(ev_in, st);
+            cudaStreamWaitEvent(own, ev_in, 0);
+        }
+        cudaEvent_t e0;
+        cudaEventCreate(&e0);
+        prof_stream = cs;
+        prof_names.clear();
+        cudaGraph_t gph;
+        if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+            return fail(RWKV_E_CUDA, "profile: capture could not start");
+        cudaEventRecordWithFlags(e0, cs, cudaEventRecordExternal);
+        profiling = true;
+        int rc = run_step(R, cs);
+        profiling = false;
+        cudaError_t e = cudaStreamEndCapture(cs, &gph);
+        if (rc == RWKV_OK && e != cudaSuccess) rc = fail(RWKV_E_CUDA, "profile capture: %s", cudaGetErrorString(e));
+        if (rc == RWKV_OK) {
+            cudaGraphExec_t ex;
+            e = cudaGraphInstantiate(&ex, gph, 0);
+            if (e == cudaSuccess) {
+                cudaGraphLaunch(ex, cs);
+                if (cudaStreamSynchronize(cs) != cudaSuccess) rc = fail(RWKV_E_CUDA, "profile: replay failed");
+                cudaGraphExecDestroy(ex);
+            } else {
+                rc = fail(RWKV_E_CUDA, "profile instantiate: %s", cudaGetErrorString(e));
+            }
+        }
+        if (e == cudaSuccess || rc != RWKV_OK) cudaGraphDestroy(gph);
+        std::string all;
+        int n = 0;
+        cudaEvent_t prev = e0;
+        for (size_t i = 0; i < prof_names.size() && rc == RWKV_OK; i++) {
+            float t = 0.f;
+            cudaEventElapsedTime(&t, prev, prof_ev[i]);
+            if (n < cap) ms[n++] = t;
+            all += prof_names[i];
+            all += "\n";
+            prev = prof_ev[i];
+        }
+        cudaEventDestroy(e0);
+        prof_names.clear();
+        *count = n;
+        if (names && names_cap > 0) {
+            strncpy(names, all.c_str(), names_cap - 1);
+            names[names_cap - 1] = 0;
+        }
+        if (!st) {
+            cudaEventRecord(ev_out, own);
+            cudaStreamWaitEvent(st, ev_out, 0);
+        }
+        return rc;
+    }
+
     // graph_step on any stream, the legacy default stream included.
     int graph_step_any(int R, cudaStream_t st) {
         if (st != nullptr) return graph_step(R, st);
@@ -462,7 +573,7 @@ struct X070 {
         return rc;
     }
 
-    int launches_per_step() const { return 2 + L * 10 + 2; }
+    int launches_per_step() const { return 1 + L * 10 + 4; }
 };
 
 }  // namespace rwkv
@@ -555,6 +666,14 @@ int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int 
             if (int rc = m.graph_step_any(rows, st)) return rc;
     }
     return check_launch("rwkv_x070_generate");
+}
+
+int rwkv_x070_profile_step(rwkv_x070_t h, int rows, float* ms_host, int cap, char* names_host,
+                           int names_cap, int* count, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h && ms_host && count, RWKV_E_NULL, "rwkv_x070_profile_step: NULL argument");
+    X070& m = *reinterpret_cast<X070*>(h);
+    RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax, RWKV_E_SHAPE, "rows %d not in 1..%d", rows, m.Rmax);
+    return m.profile_step(rows, (cudaStream_t)stream, ms_host, cap, names_host, names_cap, count);
 }
 
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t h) { return h ? reinterpret_cast<X070*>(h)->weight_bytes : 0; }

@@ -111,16 +111,25 @@ x070_tmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
         const int c = threadIdx.x + GLUE_T * i;
         v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
     }
+    // all loads of the row before any store
+    float sv[GLUE_PER], cf[6][GLUE_PER];
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        sv[i] = (c < C) ? shift[(int64_t)n * C + c] : 0.f;
+#pragma unroll
+        for (int m = 0; m < 6; m++) cf[m][i] = (c < C) ? coef[m * C + c] : 0.f;
+    }
     ln_regs(v, C, lnw, lnb, sh);
 #pragma unroll
     for (int i = 0; i < GLUE_PER; i++) {
         const int c = threadIdx.x + GLUE_T * i;
         if (c >= C) continue;
         const int64_t o = (int64_t)n * C + c;
-        const float xx = shift[o] - v[i];
+        const float xx = sv[i] - v[i];
         shift[o] = v[i];
 #pragma unroll
-        for (int m = 0; m < 6; m++) st_act(mix + (int64_t)m * R * C + o, v[i] + xx * coef[m * C + c]);
+        for (int m = 0; m < 6; m++) st_act(mix + (int64_t)m * R * C + o, v[i] + xx * cf[m][i]);
     }
 }
 
@@ -138,15 +147,22 @@ x070_cmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
         const int c = threadIdx.x + GLUE_T * i;
         v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
     }
+    float sv[GLUE_PER], cf[GLUE_PER];
+#pragma unroll
+    for (int i = 0; i < GLUE_PER; i++) {
+        const int c = threadIdx.x + GLUE_T * i;
+        sv[i] = (c < C) ? shift[(int64_t)n * C + c] : 0.f;
+        cf[i] = (c < C) ? coef[c] : 0.f;
+    }
     ln_regs(v, C, lnw, lnb, sh);
 #pragma unroll
     for (int i = 0; i < GLUE_PER; i++) {
         const int c = threadIdx.x + GLUE_T * i;
         if (c >= C) continue;
         const int64_t o = (int64_t)n * C + c;
-        const float xx = shift[o] - v[i];
+        const float xx = sv[i] - v[i];
         shift[o] = v[i];
-        st_act(out + o, v[i] + xx * coef[c]);
+        st_act(out + o, v[i] + xx * cf[i]);
     }
 }
 
@@ -192,17 +208,35 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
     const int dv = threadIdx.x / LPR, q = threadIdx.x % LPR, c0 = q * CPL;
     const size_t vb = (size_t)rh * N;   // [R, H, N] element base of this (row, head)
     const size_t hb = (size_t)hi * N;   // [H, N] parameter base
+    // the state slice first: its loads are in flight while the vectors arrive
+    float* hp = state + (size_t)rh * N * N + (size_t)dv * N + c0;
+    float s[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; j += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(hp + j);
+        s[j] = t4.x; s[j + 1] = t4.y; s[j + 2] = t4.z; s[j + 3] = t4.w;
+    }
     // per-column vectors for this lane
-    float kk[CPL], kp[CPL], aa[CPL];
+    float kk[CPL], kp[CPL], aa[CPL], kr[CPL], kkv[CPL], kav[CPL], wv[CPL], rv[CPL];
+    auto ld16 = [&](const float* p, float* o) {
+#pragma unroll
+        for (int j = 0; j < CPL; j += 4) {
+            const float4 t4 = *reinterpret_cast<const float4*>(p + j);
+            o[j] = t4.x; o[j + 1] = t4.y; o[j + 2] = t4.z; o[j + 3] = t4.w;
+        }
+    };
+    ld16(kraw + vb + c0, kr);
+    ld16(kkw + hb + c0, kkv);
+    ld16(a + vb + c0, aa);
+    ld16(kaw + hb + c0, kav);
+    ld16(wdec + vb + c0, wv);
+    ld16(r + vb + c0, rv);
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < CPL; j++) {
-        const int c = c0 + j;
-        const float kr = kraw[vb + c];
-        kk[j] = kr * kkw[hb + c];
+        kk[j] = kr[j] * kkv[j];
         ss += kk[j] * kk[j];
-        aa[j] = a[vb + c];
-        kp[j] = kr * (1.0f + (aa[j] - 1.0f) * kaw[hb + c]);
+        kp[j] = kr[j] * (1.0f + (aa[j] - 1.0f) * kav[j]);
     }
     ss = group_sum<LPR>(ss);
     const float inv = 1.0f / sqrtf(ss + 1e-12f);
@@ -217,13 +251,6 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
         vd = vd + (f - vd) * vv[vb + dv];
     }
     if (q == 0) vsh[dv] = vd;
-    float* hp = state + (size_t)rh * N * N + (size_t)dv * N + c0;
-    float s[CPL];
-#pragma unroll
-    for (int j = 0; j < CPL; j += 4) {
-        const float4 t4 = *reinterpret_cast<const float4*>(hp + j);
-        s[j] = t4.x; s[j + 1] = t4.y; s[j + 2] = t4.z; s[j + 3] = t4.w;
-    }
     // sa = S a_wkv with a_wkv = -kk
     float sa0 = 0.f, sa1 = 0.f;
 #pragma unroll
@@ -235,11 +262,10 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
     float y0 = 0.f, y1 = 0.f;
 #pragma unroll
     for (int j = 0; j < CPL; j++) {
-        const int c = c0 + j;
         const float bw = kk[j] * aa[j];
-        s[j] = fmaf(wdec[vb + c], s[j], fmaf(vd, kp[j], sa * bw));
-        if (j & 1) y1 = fmaf(s[j], r[vb + c], y1);
-        else y0 = fmaf(s[j], r[vb + c], y0);
+        s[j] = fmaf(wv[j], s[j], fmaf(vd, kp[j], sa * bw));
+        if (j & 1) y1 = fmaf(s[j], rv[j], y1);
+        else y0 = fmaf(s[j], rv[j], y0);
     }
     const float yy = group_sum<LPR>(y0 + y1);
 #pragma unroll
@@ -250,7 +276,7 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
     float dpp = 0.f;
     if (dv == 0) {
 #pragma unroll
-        for (int j = 0; j < CPL; j++) dpp += r[vb + c0 + j] * kp[j] * rkw[hb + c0 + j];
+        for (int j = 0; j < CPL; j++) dpp += rv[j] * kp[j] * rkw[hb + c0 + j];
     }
     __syncthreads();
     if (threadIdx.x >= 32) return;
@@ -268,33 +294,56 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
     st_act(out + vb + l + 32, o1);
 }
 
-// Greedy sampler: first index of the maximum logit per row.
+// Greedy sampler: first index of the maximum logit per row.  Each CTA scans
+// a slice of one row and folds (value, index) into a 64-bit key with
+// atomicMax: the high word is the float mapped to an order-preserving
+// unsigned, the low word ~index, so the maximum key is the largest logit and,
+// among equal logits, the lowest index -- independent of CTA order.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    unsigned u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned)(0xFFFFFFFFu - (unsigned)idx);
+}
+
+constexpr int ARGMAX_SLICE = 4096;
+
 __global__ void __launch_bounds__(GLUE_T)
-x070_argmax_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ ids) {
-    __shared__ float sv[GLUE_T / 32];
-    __shared__ int si[GLUE_T / 32];
-    const int n = blockIdx.x;
+x070_argmax_kernel(const float* __restrict__ logits, int V, unsigned long long* __restrict__ keys) {
+    __shared__ unsigned long long sk[GLUE_T / 32];
+    const int n = blockIdx.y;
+    const int c0 = blockIdx.x * ARGMAX_SLICE;
     const float* p = logits + (int64_t)n * V;
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int c = threadIdx.x; c < V; c += GLUE_T) {
-        const float v = p[c];
-        if (v > best || (v == best && c < bi)) { best = v; bi = c; }
+    unsigned long long best = 0ull;
+    const int cend = min(V, c0 + ARGMAX_SLICE);
+    if ((V & 3) == 0) {
+#pragma unroll 4
+        for (int c = c0 + 4 * threadIdx.x; c < cend; c += 4 * GLUE_T) {
+            const float4 v4 = *reinterpret_cast<const float4*>(p + c);
+            best = max(best, argmax_key(v4.x, c));
+            best = max(best, argmax_key(v4.y, c + 1));
+            best = max(best, argmax_key(v4.z, c + 2));
+            best = max(best, argmax_key(v4.w, c + 3));
+        }
+    } else {
+        for (int c = c0 + threadIdx.x; c < cend; c += GLUE_T) best = max(best, argmax_key(p[c], c));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < GLUE_T / 32; w++)
-            if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
-        ids[n] = bi;
+        for (int w = 1; w < GLUE_T / 32; w++) best = max(best, sk[w]);
+        atomicMax(keys + n, best);
     }
+}
+
+// keys -> ids, and re-arm the keys for the next step.
+__global__ void x070_argmax_finish_kernel(unsigned long long* __restrict__ keys,
+                                          int32_t* __restrict__ ids, int R) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= R) return;
+    ids[n] = (int32_t)(0xFFFFFFFFu - (unsigned)(keys[n] & 0xFFFFFFFFull));
+    keys[n] = 0ull;
 }
 
 // CUDA-core GEMV for fp32 activations (the fp32 parity mode): one warp per

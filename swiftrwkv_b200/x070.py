@@ -125,6 +125,22 @@ class X070Backbone:
             p = _lib.P(ids.data_ptr())
         call("rwkv_x070_step", self.h, p, rows, None, None, int(use_graph), self._s())
 
+    def profile_step(self, rows: int):
+        """One eager step with per-launch device times: {kernel: (launches, ms)}
+        plus the ordered list [(name, ms)].  The state advances as in step()."""
+        cap = 4096
+        ms = (ctypes.c_float * cap)()
+        names = ctypes.create_string_buffer(cap * 24)
+        n = ctypes.c_int(0)
+        call("rwkv_x070_profile_step", self.h, rows, ctypes.cast(ms, ctypes.c_void_p), cap,
+             ctypes.cast(names, ctypes.c_void_p), len(names), ctypes.byref(n), self._s())
+        seq = list(zip(names.value.decode().split("\n"), ms[:n.value]))
+        agg = {}
+        for name, t in seq:
+            c, tot = agg.get(name, (0, 0.0))
+            agg[name] = (c + 1, tot + t)
+        return agg, seq
+
     def generateBatch(self, prompts, n_new: int):
         """Greedy generation, host in / host out: prompts int [rows, T] (equal
         lengths) -> new tokens int32 [rows, n_new].  State starts from zero."""

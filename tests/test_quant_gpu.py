@@ -31,6 +31,19 @@ def make_affine(oracle, rng, OUT, IN, group=64, bits=4):
     return W, wq, sc, bi
 
 
+def want_gemm(oracle, x, wq, sc, bi, group=64, bits=4):
+    """What rwkv_q_gemm computes for fp16 x: up to 8 rows the exact product of
+    the dequantised weight (MLX's quantized matrix-vector numerics); above 8
+    rows, on the 4-bit group-64 tensor-core path, the exact product of the
+    weight dequantised into fp16 (MLX's quantized matmul dequantises into the
+    activation type)."""
+    rows = x.shape[0]
+    if rows <= 8 or not (bits == 4 and group == 64):
+        return oracle.affine_gemv(x.astype(np.float32), wq, sc, bi, group, bits, exact=True)
+    w16 = oracle.affine_dequant(wq, sc, bi, group, bits).astype(np.float16).astype(np.float64)
+    return x.astype(np.float64) @ w16.T
+
+
 # BASELINE config 2 matrices (OUT x IN) and a small odd one
 MATS = [(2048, 2048), (8192, 2048), (2048, 8192), (65536, 2048), (48, 320)]
 
@@ -85,7 +98,7 @@ def test_gemm_rows_and_formats(cuda, oracle, rng, rows, bits, group):
     x = f16(rng.standard_normal((rows, IN)))
     y = Q.quantizedMM(dev(x), dev(wq.view(np.int32)), dev(sc.view(np.float16)),
                       dev(bi.view(np.float16)), True, group, bits, out_dtype=torch.float32)
-    want = oracle.affine_gemv(x.astype(np.float32), wq, sc, bi, group, bits, exact=True)
+    want = want_gemm(oracle, x, wq, sc, bi, group, bits)
     assert rel_err(host(y), want) < 2e-5
     y16 = Q.quantizedMM(dev(x), dev(wq.view(np.int32)), dev(sc.view(np.float16)),
                         dev(bi.view(np.float16)), True, group, bits)
@@ -206,3 +219,19 @@ def test_sym_kat_and_rows(cuda, oracle, golden, rng):
     assert np.array_equal(host(rows.view(torch.int16)).view(np.uint16),
                           oracle.sym_rows(ids, codes, qs, d, C))
     assert torch.equal(rows, table.dense()[dev(ids).long()])
+
+
+@pytest.mark.parametrize("OUT,IN", [(96, 64), (2048, 2048), (300, 8192), (8192, 2048)])
+@pytest.mark.parametrize("rows", [1, 5, 8, 16, 31, 64, 100, 256])
+def test_tensor_core_gemm_shapes(cuda, oracle, rng, OUT, IN, rows):
+    """The pipelined tensor-core GEMM behind fp16 rwkv_q_gemm: every tile width
+    (8/16/32/64 rows), split-K, OUT off the 64-row tile, a single K group."""
+    from swiftrwkv_b200 import quant as Q
+    W, wq, sc, bi = make_affine(oracle, rng, OUT, IN)
+    x = f16(rng.standard_normal((rows, IN)))
+    args = (dev(x), dev(wq.view(np.int32)), dev(sc.view(np.float16)), dev(bi.view(np.float16)))
+    y = Q.quantizedMM(*args, out_dtype=torch.float32)
+    want = want_gemm(oracle, x, wq, sc, bi)
+    assert rel_err(host(y), want) < 2e-5
+    y2 = Q.quantizedMM(*args, out_dtype=torch.float32)
+    assert torch.equal(y, y2), "split-K reduction must be deterministic"
