@@ -191,6 +191,9 @@ x070_ln_out_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
 //   kk = l2norm(k * k_k);  k' = k * (1 + (a - 1) * k_a)
 //   v' = v (layer 0, also stored as v_first) or v + (v_first - v) * vv
 //   step with (r, w, k', v', -kk, kk * a); tail -> out (act type).
+// Every thread issues its four 16-byte state loads first; meanwhile two warps
+// build the head's vectors in shared memory, so a thread keeps only its 16
+// state values in registers and many (row, head) CTAs fit on an SM.
 template <typename A>
 __global__ void __launch_bounds__(256)
 x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
@@ -202,13 +205,13 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
                 const float* __restrict__ g, float* __restrict__ state, A* __restrict__ out,
                 int H, int layer0) {
     constexpr int N = 64, LPR = 4, CPL = 16;
-    __shared__ float ysh[N], vsh[N];
+    __shared__ __align__(16) float r_s[N], w_s[N], kp_s[N], aw_s[N], bw_s[N], v_s[N], y_s[N];
+    __shared__ float red[2];
     const int rh = blockIdx.x;
     const int hi = rh % H;
     const int dv = threadIdx.x / LPR, q = threadIdx.x % LPR, c0 = q * CPL;
     const size_t vb = (size_t)rh * N;   // [R, H, N] element base of this (row, head)
     const size_t hb = (size_t)hi * N;   // [H, N] parameter base
-    // the state slice first: its loads are in flight while the vectors arrive
     float* hp = state + (size_t)rh * N * N + (size_t)dv * N + c0;
     float s[CPL];
 #pragma unroll
@@ -216,80 +219,66 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
         const float4 t4 = *reinterpret_cast<const float4*>(hp + j);
         s[j] = t4.x; s[j + 1] = t4.y; s[j + 2] = t4.z; s[j + 3] = t4.w;
     }
-    // per-column vectors for this lane
-    float kk[CPL], kp[CPL], aa[CPL], kr[CPL], kkv[CPL], kav[CPL], wv[CPL], rv[CPL];
-    auto ld16 = [&](const float* p, float* o) {
-#pragma unroll
-        for (int j = 0; j < CPL; j += 4) {
-            const float4 t4 = *reinterpret_cast<const float4*>(p + j);
-            o[j] = t4.x; o[j + 1] = t4.y; o[j + 2] = t4.z; o[j + 3] = t4.w;
+    if (threadIdx.x < N) {  // warps 0-1: per-column vectors; column c = threadIdx.x
+        const int c = threadIdx.x;
+        const float kr = kraw[vb + c], aa = a[vb + c];
+        const float kk = kr * kkw[hb + c];
+        float ss = warp_sum(kk * kk);
+        if ((c & 31) == 0) red[c >> 5] = ss;
+        r_s[c] = r[vb + c];
+        w_s[c] = wdec[vb + c];
+        const float kp = kr * (1.0f + (aa - 1.0f) * kaw[hb + c]);
+        kp_s[c] = kp;
+        // value row c
+        float vd = vraw[vb + c];
+        if (layer0) {
+            vfirst[vb + c] = vd;
+        } else {
+            const float f = vfirst[vb + c];
+            vd = vd + (f - vd) * vv[vb + c];
         }
-    };
-    ld16(kraw + vb + c0, kr);
-    ld16(kkw + hb + c0, kkv);
-    ld16(a + vb + c0, aa);
-    ld16(kaw + hb + c0, kav);
-    ld16(wdec + vb + c0, wv);
-    ld16(r + vb + c0, rv);
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < CPL; j++) {
-        kk[j] = kr[j] * kkv[j];
-        ss += kk[j] * kk[j];
-        kp[j] = kr[j] * (1.0f + (aa[j] - 1.0f) * kav[j]);
+        v_s[c] = vd;
+        asm volatile("bar.sync 1, 64;");  // the two warps: both halves of the norm are in red[]
+        const float inv = 1.0f / sqrtf(red[0] + red[1] + 1e-12f);
+        const float kn = kk * inv;
+        aw_s[c] = -kn;
+        bw_s[c] = kn * aa;
     }
-    ss = group_sum<LPR>(ss);
-    const float inv = 1.0f / sqrtf(ss + 1e-12f);
-#pragma unroll
-    for (int j = 0; j < CPL; j++) kk[j] *= inv;
-    // value row dv
-    float vd = vraw[vb + dv];
-    if (layer0) {
-        if (q == 0) vfirst[vb + dv] = vd;
-    } else {
-        const float f = vfirst[vb + dv];
-        vd = vd + (f - vd) * vv[vb + dv];
-    }
-    if (q == 0) vsh[dv] = vd;
-    // sa = S a_wkv with a_wkv = -kk
+    __syncthreads();
     float sa0 = 0.f, sa1 = 0.f;
 #pragma unroll
     for (int j = 0; j < CPL; j += 2) {
-        sa0 = fmaf(s[j], -kk[j], sa0);
-        sa1 = fmaf(s[j + 1], -kk[j + 1], sa1);
+        sa0 = fmaf(s[j], aw_s[c0 + j], sa0);
+        sa1 = fmaf(s[j + 1], aw_s[c0 + j + 1], sa1);
     }
     const float sa = group_sum<LPR>(sa0 + sa1);
+    const float vd = v_s[dv];
     float y0 = 0.f, y1 = 0.f;
 #pragma unroll
     for (int j = 0; j < CPL; j++) {
-        const float bw = kk[j] * aa[j];
-        s[j] = fmaf(wv[j], s[j], fmaf(vd, kp[j], sa * bw));
-        if (j & 1) y1 = fmaf(s[j], rv[j], y1);
-        else y0 = fmaf(s[j], rv[j], y0);
+        const int c = c0 + j;
+        s[j] = fmaf(w_s[c], s[j], fmaf(vd, kp_s[c], sa * bw_s[c]));
+        if (j & 1) y1 = fmaf(s[j], r_s[c], y1);
+        else y0 = fmaf(s[j], r_s[c], y0);
     }
     const float yy = group_sum<LPR>(y0 + y1);
 #pragma unroll
     for (int j = 0; j < CPL; j += 4)
         *reinterpret_cast<float4*>(hp + j) = make_float4(s[j], s[j + 1], s[j + 2], s[j + 3]);
-    if (q == 0) ysh[dv] = yy;
-    // bonus partial: sum over this lane's columns of r * k' * r_k (row 0 lanes only)
-    float dpp = 0.f;
-    if (dv == 0) {
-#pragma unroll
-        for (int j = 0; j < CPL; j++) dpp += rv[j] * kp[j] * rkw[hb + c0 + j];
-    }
+    if (q == 0) y_s[dv] = yy;
     __syncthreads();
     if (threadIdx.x >= 32) return;
-    const int l = threadIdx.x;  // lanes 0..3 are row 0's four lanes
-    float dp = (l < LPR) ? dpp : 0.f;
+    // tail on one warp: GroupNorm(64e-5) of y, bonus (sum r*k'*r_k) * v', gate
+    const int l = threadIdx.x;
+    float dp = r_s[l] * kp_s[l] * rkw[hb + l] + r_s[l + 32] * kp_s[l + 32] * rkw[hb + l + 32];
     dp = warp_sum(dp);
-    const float x0 = ysh[l], x1 = ysh[l + 32];
+    const float x0 = y_s[l], x1 = y_s[l + 32];
     const float mean = warp_sum(x0 + x1) * (1.0f / N);
     const float d0 = x0 - mean, d1 = x1 - mean;
     const float var = warp_sum(d0 * d0 + d1 * d1) * (1.0f / N);
     const float invs = 1.0f / sqrtf(var + 64e-5f);
-    const float o0 = (d0 * invs * lnxw[hb + l] + lnxb[hb + l] + dp * vsh[l]) * g[vb + l];
-    const float o1 = (d1 * invs * lnxw[hb + l + 32] + lnxb[hb + l + 32] + dp * vsh[l + 32]) * g[vb + l + 32];
+    const float o0 = (d0 * invs * lnxw[hb + l] + lnxb[hb + l] + dp * v_s[l]) * g[vb + l];
+    const float o1 = (d1 * invs * lnxw[hb + l + 32] + lnxb[hb + l + 32] + dp * v_s[l + 32]) * g[vb + l + 32];
     st_act(out + vb + l, o0);
     st_act(out + vb + l + 32, o1);
 }
