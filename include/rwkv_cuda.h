@@ -94,6 +94,25 @@ int rwkv_wkv7_backward(int dtype, const void* r, const void* w, const void* k, c
                        void* dv, void* da, void* db, float* dh_in, int B, int T, int H, int N,
                        void* workspace, int64_t workspace_bytes, rwkv_stream_t stream);
 
+/* rwkv_wkv7_backward without a workspace argument and without allocating.
+ * No counterpart in the reference: it exists for hosts that cannot allocate
+ * device memory for this library -- a framework bridge that passes the op only
+ * its own input and output tensors, or a process whose memory budget is
+ * reserved up front, where a cudaMalloc could fail and would synchronise the
+ * device.  The recompute scratch is a fixed array built into the library:
+ * RWKV_NOALLOC_MAX_HEADS (batch, head) pairs x 272 KiB = 63.75 MiB, held by
+ * every GPU that loads the library until the process exits; B*H above the
+ * limit returns RWKV_E_SHAPE.  The first call on a device looks the array up
+ * (do it before any stream capture).  All calls on a device share the array:
+ * calls that overlap on the GPU race, so order them on one stream.  Same
+ * arguments and results as rwkv_wkv7_backward otherwise. */
+#define RWKV_NOALLOC_MAX_HEADS 240
+int rwkv_wkv7_backward_noalloc(int dtype, const void* r, const void* w, const void* k,
+                               const void* v, const void* a, const void* b, const float* h_in,
+                               const float* h_ckpt, const void* dy, const float* dh_out, void* dr,
+                               void* dw, void* dk, void* dv, void* da, void* db, float* dh_in,
+                               int B, int T, int H, int N, rwkv_stream_t stream);
+
 /* One-token decode step for `rows` independent rows: r..b, y [rows, H, N];
  * h [rows, H, N, N] fp32 updated in place.
  * Replaces wkv7StepForward (Sources/RWKVKernel/WKV7DecodeKernels.swift:157-173). */

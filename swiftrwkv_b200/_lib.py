@@ -15,6 +15,7 @@ HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "rwkv_cuda.h")
 
 OK, E_NULL, E_SHAPE, E_DTYPE, E_UNSUPPORTED, E_CUDA, E_TIMEOUT, E_WORKSPACE = 0, -1, -2, -3, -4, -5, -6, -7
 F32, BF16, F16 = 0, 1, 2
+RWKV_NOALLOC_MAX_HEADS = 240  # rwkv_cuda.h: (batch, head) pairs of rwkv_wkv7_backward_noalloc
 
 
 class RWKVError(RuntimeError):
@@ -40,6 +41,7 @@ _SIGS = {
     "rwkv_wkv7_train_forward": [I, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P],
     "rwkv_wkv7_backward_workspace_size": [I, I, I, I],
     "rwkv_wkv7_backward": [I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P, I64, P],
+    "rwkv_wkv7_backward_noalloc": [I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P],
     "rwkv_wkv7_step": [I, P, P, P, P, P, P, P, P, I, I, I, P],
     "rwkv_wkv_tail": [P, P, P, P, P, P, P, P, P, I, I, I, F, P],
     "rwkv_wkv7_step_tail": [P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, F, P],
