@@ -1,0 +1,615 @@
+// Batched-decode GEMM on the 5th-generation tensor cores (tcgen05 + TMA +
+// TMEM):  y[n, o] = act( sum_k x[n, k] * W[o, k] )  with W in the MLX affine
+// 4-bit group-64 container (fp16 scale / bias), x fp16, for activation rows
+// R > 8 (BN = 16 .. 128 rows per n-block).
+//
+// CTA (320 threads) = one 128-row block of W x one BN-row block of x, K in
+// stages of GPS 64-column groups:
+//   warp 0      TMA producer: the stage's packed codes (128 rows x 32*GPS
+//               bytes, swizzled) and GPS activation boxes (BN rows x 64 fp16,
+//               128-byte swizzle, the K-major layout tcgen05.mma reads)
+//   warp 1      TMEM owner and MMA issuer: 4*GPS tcgen05.mma (M=128, N=BN,
+//               K=16) per stage, A read from TMEM, B from shared memory, D in
+//               TMEM; tcgen05.commit frees the stage
+//   warps 2-9   thread <-> weight row (its TMEM lane); warps w and w+4 share a
+//               lane quadrant and split each stage's groups.  They dequantise
+//               with one HFMA2 per two weights, w = half(scale*q + bias),
+//               exactly as the mma.sync wide path does, and store the fp16
+//               weights into the A stage in TMEM (tcgen05.st); after the last
+//               stage they drain the accumulator (tcgen05.ld) and run the
+//               epilogue
+// Keeping A in TMEM means the dequantised weights never touch shared memory:
+// per group the CTA moves 4 KB of codes and BN*128 bytes of x through it.
+//
+// mbarriers: full[s] (TMA bytes landed), sempty[s] (MMAs of smem stage s
+// done), afull[a] (256 dequant arrivals), aempty[a] (MMAs reading TMEM stage
+// a done), done (every MMA done).  Every mbarrier wait is bounded in time: on
+// expiry the waiter sets *err, all roles wind down, the producer waits
+// (bounded) for its copies in flight, and TMEM is freed after the final MMA
+// commit.
+//
+// Split-K (S > 1): the S CTAs of one output tile form a (1, 1, S) cluster.
+// After a cluster barrier each CTA stores rows [128z/S, 128(z+1)/S) of its
+// fp32 partial into CTA z's shared memory (distributed shared memory, posted
+// stores); after a second barrier CTA z sums its rows over the S partials in
+// split order (deterministic) and applies the epilogue.  No global
+// workspace, no atomics.
+#pragma once
+
+#include <cudaTypedefs.h>
+
+#include "gemm_w4.cuh"
+
+namespace rwkv {
+namespace tc {
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t gtime() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint64_t WAIT_LIMIT_NS = 200ull * 1000 * 1000;  // far beyond any healthy wait
+
+// Wait for the phase with parity `parity` to complete.  Returns false (with
+// *err set) when the wait expires or another role has already given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
+    if (mbar_try(b, parity)) return true;
+    const uint64_t t0 = gtime();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*(volatile int*)err) return false;
+            if (gtime() - t0 > WAIT_LIMIT_NS) {
+                atomicExch(err, 1);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(saddr(dst)), "l"(map), "r"(saddr(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory operand descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart, descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;            // leading offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;  // stride offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;            // version
+    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+    return d;
+}
+
+// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+          "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+          "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(saddr(dst)), "l"(src), "n"(BYTES) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// The 8 codes of packed word w (k = 8w .. 8w+7), dequantised to fp16 in
+// natural k order: out[q] = (w_{2q}, w_{2q+1}).
+__device__ __forceinline__ void dq_word(uint32_t w, __half2 s2, __half2 b2, uint32_t* out) {
+    uint32_t p[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {  // p[j] = (w_j, w_{j+4})
+        uint32_t h = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+        const __half2 q = __hsub2(*reinterpret_cast<__half2*>(&h),
+                                  __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
+        const __half2 v = __hfma2(q, s2, b2);
+        p[j] = *reinterpret_cast<const uint32_t*>(&v);
+    }
+    out[0] = __byte_perm(p[0], p[1], 0x5410);
+    out[1] = __byte_perm(p[2], p[3], 0x5410);
+    out[2] = __byte_perm(p[0], p[1], 0x7632);
+    out[3] = __byte_perm(p[2], p[3], 0x7632);
+}
+
+// 8 columns into raw registers; complete them with tmem_ld_wait()
+__device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// whole-cluster barrier (every thread of every CTA), release / acquire
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// shared::cluster address of the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_rank(uint32_t smem_addr, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+// posted store into a peer CTA's shared memory (ordered by the next cluster barrier)
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+}  // namespace tc
+
+constexpr int TC_JOBS = 4;
+constexpr int TC_BM = 128;
+constexpr int TC_DQW = 8;                          // dequant / epilogue warps
+constexpr int TC_THREADS = 64 + 32 * TC_DQW;       // + producer warp + MMA warp
+constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_A_COL = 256;  // A stages live in TMEM columns [256, 512)
+constexpr int TC_SRING = 4;    // scale / bias prefetch ring (stages)
+constexpr int TC_MAX_SPLIT = 8;  // split-K CTAs of one tile form one cluster
+
+struct alignas(64) TcJob {
+    CUtensorMap wmap;  // codes: dims {IN/8, OUT} u32, box {8*GPS, 128}, swizzled
+    CUtensorMap xmap;  // activations: dims {IN, R} fp16, box {64, BN}, 128-byte swizzle
+    GemvJob g;         // scales, biases, OUT, IN, epilogue
+};
+
+struct TcArgs {
+    TcJob j[TC_JOBS];
+    int njobs, R, S;
+    int* err;
+};
+
+template <int BN, int GPS, int ST>
+struct TcCfg {
+    static constexpr int CROW = 32 * GPS;                 // code bytes per row per stage
+    static constexpr int C_BYTES = TC_BM * CROW;
+    static constexpr int XBOX = BN * 128;                 // one x box (64 columns)
+    static constexpr int X_BYTES = GPS * XBOX;
+    static constexpr int STAGE = C_BYTES + X_BYTES;       // multiple of 1024
+    static constexpr int ST_A = (TC_TMEM_COLS - TC_A_COL) / (32 * GPS);
+    static constexpr int SLOT = 4 * GPS;                  // ring slot bytes: GPS scales + GPS biases
+    static constexpr int SR_OFF = ST * STAGE;             // ring: [TC_SRING][32*TC_DQW] slots
+    static constexpr int B_OFF = SR_OFF + TC_SRING * 32 * TC_DQW * SLOT;
+    static constexpr int NBAR = 2 * ST + 2 * ST_A + 1;
+    static constexpr int T_OFF = B_OFF + NBAR * 8;
+    static constexpr int TOTAL = T_OFF + 16 + 1024;       // + slack for 1024-byte alignment
+    static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 needs N % 16 == 0, 16..256");
+    static_assert(BN <= TC_A_COL, "accumulator columns");
+    static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * BN * 4, "split-K receive buffers reuse the stage buffers");
+    static_assert(TOTAL <= 227 * 1024, "shared memory per CTA");
+    static_assert(GPS % 2 == 0 && TC_DQW == 8, "two dequant warps per lane quadrant, GPS/2 groups each");
+};
+
+// Byte offset of 16-byte chunk c of row r in a TMA tile with `rb`-byte rows
+// written with the matching swizzle (128 B: Swizzle<3,4,3>; 64 B: Swizzle<2,4,3>).
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c, uint32_t rb) {
+    const uint32_t off = r * rb + 16 * c;
+    return off ^ (((off >> 7) & (rb / 16 - 1)) << 4);
+}
+
+template <int BN, int GPS, int ST>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ TcArgs args) {
+    using C = TcCfg<BN, GPS, ST>;
+    constexpr int ST_A = C::ST_A;
+    constexpr int HG = GPS / 2;  // groups per dequant warp per stage
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::B_OFF);
+    uint64_t* sempty = full + ST;
+    uint64_t* afull = sempty + ST;
+    uint64_t* aempty = afull + ST_A;
+    uint64_t* done = aempty + ST_A;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::T_OFF);
+
+    const TcJob& jb = args.j[blockIdx.y];
+    const int OUT = jb.g.OUT, IN = jb.g.IN;
+    const int m0 = blockIdx.x * TC_BM;
+    const int S = args.S;
+    const int nblk = blockIdx.z / S, kz = blockIdx.z % S;  // kz = rank in the (1, 1, S) cluster
+    const int n0 = nblk * BN;
+    // uniform over the cluster (same x, y, n-block), before any barrier or TMEM use
+    if (m0 >= OUT || n0 >= args.R) return;
+    const int NG = IN / 64, NS = NG / GPS;
+    const int s0 = (int)((int64_t)NS * kz / S), s1 = (int)((int64_t)NS * (kz + 1) / S);
+    const int nst = s1 - s0;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int* err = args.err;
+
+    if (tid == 0) {
+        for (int s = 0; s < ST; s++) {
+            tc::mbar_init(full + s, 1);
+            tc::mbar_init(sempty + s, 1);
+        }
+        for (int a = 0; a < ST_A; a++) {
+            tc::mbar_init(afull + a, 32 * TC_DQW);
+            tc::mbar_init(aempty + a, 1);
+        }
+        tc::mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(tc::saddr(tmem_slot)), "r"(TC_TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc::tc_before();
+    __syncthreads();
+    tc::tc_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+    constexpr int HALF = BN / 2;  // accumulator columns per dequant warp
+    uint32_t acc[HALF];
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            int issued = 0;
+            for (int i = 0; i < nst; i++) {
+                const int s = i % ST;
+                if (i >= ST && !tc::mbar_wait(sempty + s, ((i / ST) - 1) & 1, err)) break;
+                unsigned char* st = smem + s * C::STAGE;
+                const int g = (s0 + i) * GPS;
+                tc::mbar_expect_tx(full + s, C::STAGE);
+                tc::tma_2d(st, &jb.wmap, full + s, 8 * g, m0);
+#pragma unroll
+                for (int q = 0; q < GPS; q++)
+                    tc::tma_2d(st + C::C_BYTES + q * C::XBOX, &jb.xmap, full + s, 64 * (g + q), n0);
+                issued = i + 1;
+            }
+            // the copies this thread issued have landed before the CTA may exit
+            for (int i = max(0, issued - ST); i < issued; i++) tc::mbar_wait(full + (i % ST), (i / ST) & 1, err);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            constexpr uint32_t IDESC = tc::idesc_f16(TC_BM, BN);
+            for (int i = 0; i < nst; i++) {
+                const int s = i % ST, a = i % ST_A;
+                if (!tc::mbar_wait(full + s, (i / ST) & 1, err) || !tc::mbar_wait(afull + a, (i / ST_A) & 1, err))
+                    break;
+                tc::tc_after();
+                const uint32_t xs = tc::saddr(smem + s * C::STAGE + C::C_BYTES);
+                const uint32_t ta = tmem + TC_A_COL + a * (32 * GPS);
+#pragma unroll
+                for (int q = 0; q < GPS; q++) {
+                    const uint64_t bd = tc::sw128_desc(xs + q * C::XBOX);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        tc::umma_ts(tmem, ta + q * 32 + kk * 8, bd + 2 * kk, IDESC, (i | q | kk) ? 1u : 0u);
+                }
+                tc::umma_commit(aempty + a);
+                tc::umma_commit(sempty + s);
+            }
+            tc::umma_commit(done);  // after an early exit too: TMEM is freed only after the MMAs finish
+        }
+    } else {
+        // ---- dequant: row rl = the warp's TMEM lane quadrant; warps w and w+4
+        // split each stage's groups (half h takes groups [h*HG, (h+1)*HG))
+        const int dt = tid - 64;
+        const int q4 = warp & 3, h = (warp - 2) >> 2;
+        const int rl = 32 * q4 + lane;
+        const int orow = min(m0 + rl, OUT - 1);
+        const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+        const __half* sc = (const __half*)jb.g.scales + (int64_t)orow * NG;
+        const __half* bi = (const __half*)jb.g.biases + (int64_t)orow * NG;
+        // ring slot of stage i for this thread: GPS scale halves, then GPS bias halves
+        __half* ring = reinterpret_cast<__half*>(smem + C::SR_OFF);
+        auto slot = [&](int i) { return ring + ((i % TC_SRING) * (32 * TC_DQW) + dt) * (2 * GPS); };
+        auto fetch = [&](int i) {
+            if (i < nst) {
+                const int g = (s0 + i) * GPS;
+                tc::cp_async<2 * GPS>(slot(i), sc + g);
+                tc::cp_async<2 * GPS>(slot(i) + GPS, bi + g);
+            }
+            tc::cp_commit();
+        };
+#pragma unroll
+        for (int i = 0; i < TC_SRING - 1; i++) fetch(i);
+        for (int i = 0; i < nst; i++) {
+            const int s = i % ST, a = i % ST_A;
+            fetch(i + TC_SRING - 1);
+            if (!tc::mbar_wait(full + s, (i / ST) & 1, err)) { ok = false; break; }
+            if (i >= ST_A && !tc::mbar_wait(aempty + a, ((i / ST_A) - 1) & 1, err)) { ok = false; break; }
+            tc::tc_after();
+            tc::cp_wait<TC_SRING - 1>();
+            const __half* sh = slot(i);
+            const unsigned char* cs = smem + s * C::STAGE;
+#pragma unroll
+            for (int qq = 0; qq < HG; qq++) {
+                const int q = h * HG + qq;
+                const __half2 s2 = __half2half2(sh[q]), b2 = __half2half2(sh[GPS + q]);
+                const uint4 c0 = *reinterpret_cast<const uint4*>(cs + swz(rl, 2 * q, C::CROW));
+                const uint4 c1 = *reinterpret_cast<const uint4*>(cs + swz(rl, 2 * q + 1, C::CROW));
+                const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                uint32_t v[32];
+#pragma unroll
+                for (int w = 0; w < 8; w++) tc::dq_word(words[w], s2, b2, v + 4 * w);
+                tc::tmem_st32(tmem + lane_base + TC_A_COL + a * (32 * GPS) + q * 32, v);
+            }
+            tc::tmem_st_wait();
+            tc::tc_before();
+            tc::mbar_arrive(afull + a);
+        }
+        tc::cp_wait<0>();
+        ok = tc::mbar_wait(done, 0, err) && ok;
+        tc::tc_after();
+        // ---- accumulator: row rl, this warp's half of the BN columns
+        const GemvJob g = jb.g;  // a register copy: stores below cannot alias it
+        const uint32_t tacc = tmem + lane_base;
+        const int o = m0 + rl;
+        // this thread's HALF accumulator columns (row rl), all loads in flight at once
+#pragma unroll
+        for (int c = 0; c < HALF; c += 8) tc::tmem_ld8_async(tacc + h * HALF + c, acc + c);
+        tc::tmem_ld_wait();
+        if (S == 1 && ok && o < OUT) {
+            const int c0 = n0 + h * HALF;
+            if (g.act == ACT_NONE && g.out == OUT_F32) {
+                float* yo = (float*)g.y + (int64_t)c0 * g.y_stride + o;
+#pragma unroll
+                for (int c = 0; c < HALF; c++)
+                    if (c0 + c < args.R) yo[(int64_t)c * g.y_stride] = __uint_as_float(acc[c]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < HALF; c++)
+                    if (c0 + c < args.R) epilogue(g, o, c0 + c, __uint_as_float(acc[c]));
+            }
+        }
+    }
+    if (S > 1) {
+        // Split-K over the (1, 1, S) cluster.  CTA z owns rows [128z/S, 128(z+1)/S)
+        // of the tile and receives, from every split zs, those rows of its
+        // partial into rbuf[zs][BN][NRM] (its own stage buffers, idle once
+        // every CTA of the cluster has passed the first barrier).  Every thread
+        // of every CTA takes both barriers, on every path.
+        const int NRM = (TC_BM + S - 1) / S;
+        const uint32_t rbuf = tc::saddr(smem);
+        tc::cluster_sync();
+        if (warp >= 2) {
+            const int rl = 32 * (warp & 3) + lane, h = (warp - 2) >> 2;
+            const int zo = ((rl + 1) * S + TC_BM - 1) / TC_BM - 1;  // owner of row rl
+            const int lr = rl - TC_BM * zo / S;
+            const uint32_t dst = tc::map_rank(rbuf + (uint32_t)((kz * BN + h * HALF) * NRM + lr) * 4, zo);
+#pragma unroll
+            for (int c = 0; c < HALF; c++) tc::st_cluster_u32(dst + (uint32_t)(c * NRM) * 4, acc[c]);
+        }
+        tc::cluster_sync();
+        if (warp >= 2 && !*(volatile int*)err) {
+            const GemvJob g = jb.g;
+            const int r0 = TC_BM * kz / S, nr = TC_BM * (kz + 1) / S - r0;
+            const float* rb = reinterpret_cast<const float*>(smem);
+            const bool plain = g.act == ACT_NONE && g.out == OUT_F32;
+            for (int e = tid - 64; e < nr * BN; e += 32 * TC_DQW) {
+                const int c = e / nr, lr = e - c * nr;
+                const float* src = rb + c * NRM + lr;
+                float p[TC_MAX_SPLIT];
+#pragma unroll
+                for (int z = 0; z < TC_MAX_SPLIT; z++) p[z] = z < S ? src[z * BN * NRM] : 0.f;
+                float v = 0.f;
+#pragma unroll
+                for (int z = 0; z < TC_MAX_SPLIT; z++) v += p[z];  // split order; the zero tail is exact
+                const int o = m0 + r0 + lr, n = n0 + c;
+                if (o < OUT && n < args.R) {
+                    if (plain) ((float*)g.y)[(int64_t)n * g.y_stride + o] = v;
+                    else epilogue(g, o, n, v);
+                }
+            }
+        }
+    }
+    tc::tc_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+struct TcPlan {
+    int BN = 0, GPS = 0, S = 1, nnb = 0, mblocks = 0;
+    bool ok = false;
+};
+
+// Whether a job can take the tcgen05 path: fp16 activations with rows
+// 16-byte aligned, IN a multiple of 256 (whole stages), 16-byte aligned codes,
+// 8-byte aligned scales and biases.
+inline bool tc_job_ok(const GemvJob& j) {
+    return j.IN % 256 == 0 && j.IN >= 256 && j.OUT >= 1 && j.x_stride % 8 == 0 &&
+           ((uintptr_t)j.x & 15) == 0 && ((uintptr_t)j.w & 15) == 0 && j.scales && j.biases &&
+           ((uintptr_t)j.scales & 7) == 0 && ((uintptr_t)j.biases & 7) == 0;
+}
+
+inline TcPlan plan_tc(const GemvJobs& jobs, int njobs, int R, int sm_count) {
+    TcPlan p{};
+    if (R <= 8 || R > 256 || njobs < 1 || njobs > TC_JOBS) return p;
+    for (int i = 0; i < njobs; i++)
+        if (!tc_job_ok(jobs.j[i])) return p;
+    p.BN = R <= 16 ? 16 : R <= 32 ? 32 : R <= 64 ? 64 : 128;
+    p.GPS = p.BN <= 64 ? 4 : 2;
+    p.nnb = (R + p.BN - 1) / p.BN;
+    int maxo = 0, minst = 1 << 30;
+    for (int i = 0; i < njobs; i++) {
+        maxo = std::max(maxo, jobs.j[i].OUT);
+        minst = std::min(minst, jobs.j[i].IN / 64 / p.GPS);
+    }
+    p.mblocks = (maxo + TC_BM - 1) / TC_BM;
+    int ctas = 0;
+    for (int i = 0; i < njobs; i++) ctas += (jobs.j[i].OUT + TC_BM - 1) / TC_BM * p.nnb;
+    int S = (sm_count + ctas - 1) / ctas;
+    S = std::max(1, std::min(std::min(S, minst / 2), TC_MAX_SPLIT));  // at least two stages per split
+    p.S = S;
+    p.ok = true;
+    return p;
+}
+
+inline bool encode_tc_maps(TcJob& t, const GemvJob& j, int R, int BN, int GPS) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    t.g = j;
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)(j.IN / 8), (cuuint64_t)j.OUT};
+        cuuint64_t strides[1] = {(cuuint64_t)j.IN / 2};
+        cuuint32_t box[2] = {(cuuint32_t)(8 * GPS), (cuuint32_t)TC_BM};
+        cuuint32_t es[2] = {1, 1};
+        if (enc(&t.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, (void*)j.w, dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                GPS == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)j.IN, (cuuint64_t)R};
+        cuuint64_t strides[1] = {(cuuint64_t)j.x_stride * 2};
+        cuuint32_t box[2] = {64, (cuuint32_t)BN};
+        cuuint32_t es[2] = {1, 1};
+        if (enc(&t.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)j.x, dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
+}
+
+template <int BN, int GPS, int ST>
+inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, cudaStream_t st) {
+    using C = TcCfg<BN, GPS, ST>;
+    auto kern = gemm_tc_kernel<BN, GPS, ST>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p.mblocks, a.njobs, p.nnb * a.S);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = C::TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = a.S;
+    cfg.attrs = attr;
+    cfg.numAttrs = a.S > 1 ? 1 : 0;
+    if (a.S > 1) {
+        // a cluster of S one-CTA-per-SM blocks must fit in a GPC (checked once per S)
+        static int fits[TC_MAX_SPLIT + 1] = {};
+        if (!fits[a.S]) {
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+            if (e != cudaSuccess) return e;
+            fits[a.S] = n > 0 ? 1 : -1;
+        }
+        if (fits[a.S] < 0) return cudaErrorLaunchOutOfResources;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// jobs -> tensor maps -> launch.  err: device int that a wait which gives up
+// sets to 1.
+inline cudaError_t launch_tc(const GemvJobs& jobs, int njobs, int R, const TcPlan& p, int* err,
+                             cudaStream_t st) {
+    TcArgs a{};
+    for (int i = 0; i < njobs; i++)
+        if (!encode_tc_maps(a.j[i], jobs.j[i], R, p.BN, p.GPS)) return cudaErrorInvalidValue;
+    a.njobs = njobs;
+    a.R = R;
+    a.S = p.S;
+    a.err = err;
+    switch (p.BN) {
+        case 16: return launch_tc_t<16, 4, 6>(a, p, st);
+        case 32: return launch_tc_t<32, 4, 5>(a, p, st);
+        case 64: return launch_tc_t<64, 4, 4>(a, p, st);
+        default: return launch_tc_t<128, 2, 4>(a, p, st);
+    }
+}
+
+}  // namespace rwkv

@@ -17,6 +17,7 @@
 #include <mutex>
 #include <unordered_map>
 
+#include "gemm_tc.cuh"
 #include "gemm_w4_wide.cuh"
 
 namespace rwkv {
@@ -263,6 +264,7 @@ static int dispatch_sdtype(int dt, F&& f) {
 struct GemmScratch {
     float* ws = nullptr;
     int* tickets = nullptr;
+    int* err = nullptr;  // set by a tensor-core GEMM wait that gave up
     size_t floats = 0, tickets_n = 0;
     int sm_count = 148;
     std::mutex mu;
@@ -281,11 +283,12 @@ static GemmScratch* gemm_scratch() {
     s->floats = (size_t)(4 * s->sm_count + 64) * GW_BM * 64;
     s->tickets_n = 8192;
     if (cudaMalloc(&s->ws, s->floats * 4) != cudaSuccess ||
-        cudaMalloc(&s->tickets, s->tickets_n * 4) != cudaSuccess ||
-        cudaMemset(s->tickets, 0, s->tickets_n * 4) != cudaSuccess) {
+        cudaMalloc(&s->tickets, (s->tickets_n + 1) * 4) != cudaSuccess ||
+        cudaMemset(s->tickets, 0, (s->tickets_n + 1) * 4) != cudaSuccess) {
         delete s;
         return nullptr;
     }
+    s->err = s->tickets + s->tickets_n;
     per_dev[dev] = s;
     return s;
 }
@@ -330,6 +333,13 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
         j.y_stride = OUT;
         GemmScratch* sc = gemm_scratch();
         if (!sc) return fail(RWKV_E_CUDA, "rwkv_q_gemm: workspace allocation failed");
+        // more than 8 rows: tcgen05 (TMA + TMEM) when the shapes allow it
+        const TcPlan tp = plan_tc(jobs, 1, rows, sc->sm_count);
+        if (tp.ok) {
+            cudaError_t e = launch_tc(jobs, 1, rows, tp, sc->err, st);
+            if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemm_tc_kernel: %s", cudaGetErrorString(e));
+            return ok();
+        }
         GemmPlan p = plan_any(jobs, 1, rows, sc->sm_count);
         if (p.ws_floats > sc->floats || p.tickets > sc->tickets_n) {
             p.S = 1;

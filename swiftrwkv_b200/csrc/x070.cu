@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "gemm_w4_wide.cuh"
 #include "x070_kernels.cuh"
 
@@ -99,6 +100,7 @@ struct X070 {
     // split-K partials and tickets of the tensor-core GEMMs
     float* gws = nullptr;
     int* gtickets = nullptr;
+    int* gerr = nullptr;  // set by a tensor-core GEMM wait that gave up
     size_t gws_floats = 0, gtickets_n = 0;
     int sm_count = 148;
     // step profiler: an event node after every launch of a captured step
@@ -196,7 +198,8 @@ struct X070 {
         gws_floats = (size_t)(4 * sm_count + 64) * GW_BM * 64;
         gtickets_n = 8192;
         gws = alloc<float>(gws_floats);
-        gtickets = alloc<int>(gtickets_n);
+        gtickets = alloc<int>(gtickets_n + 1);
+        gerr = gtickets + gtickets_n;
         cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking);
         cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
@@ -368,6 +371,13 @@ struct X070 {
 
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
         if (f16act) {
+            if (fmt == 0) {
+                const TcPlan tp = plan_tc(jobs, nj, R, sm_count);
+                if (tp.ok) {
+                    cudaError_t e = launch_tc(jobs, nj, R, tp, gerr, st);
+                    return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm_tc: %s", cudaGetErrorString(e));
+                }
+            }
             GemmPlan p = plan_any(jobs, nj, R, sm_count);
             if (p.ws_floats > gws_floats || p.tickets > gtickets_n)
                 return fail(RWKV_E_WORKSPACE, "gemm: split-K plan exceeds the workspace");
@@ -665,6 +675,10 @@ int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int 
         if (s + 1 < n_new)
             if (int rc = m.graph_step_any(rows, st)) return rc;
     }
+    int gave_up = 0;
+    cudaMemcpyAsync(&gave_up, m.gerr, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "generate: sync failed");
+    if (gave_up) return fail(RWKV_E_TIMEOUT, "generate: a tensor-core GEMM pipeline wait timed out");
     return check_launch("rwkv_x070_generate");
 }
 
