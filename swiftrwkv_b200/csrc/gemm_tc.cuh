@@ -3,7 +3,7 @@
 // 4-bit group-64 container (fp16 scale / bias), x fp16, for activation rows
 // R > 8 (BN = 16 .. 128 rows per n-block).
 //
-// CTA (320 threads) = one 128-row block of W x one BN-row block of x, K in
+// CTA (576 threads) = one 128-row block of W x one BN-row block of x, K in
 // stages of GPS 64-column groups:
 //   warp 0      TMA producer: the stage's packed codes (128 rows x 32*GPS
 //               bytes, swizzled) and GPS activation boxes (BN rows x 64 fp16,
@@ -11,8 +11,8 @@
 //   warp 1      TMEM owner and MMA issuer: 4*GPS tcgen05.mma (M=128, N=BN,
 //               K=16) per stage, A read from TMEM, B from shared memory, D in
 //               TMEM; tcgen05.commit frees the stage
-//   warps 2-9   thread <-> weight row (its TMEM lane); warps w and w+4 share a
-//               lane quadrant and split each stage's groups.  They dequantise
+//   warps 2-17  thread <-> weight row (its TMEM lane); the four warps of a
+//               lane quadrant split each stage's code chunks.  They dequantise
 //               with one HFMA2 per two weights, w = half(scale*q + bias),
 //               exactly as the mma.sync wide path does, and store the fp16
 //               weights into the A stage in TMEM (tcgen05.st); after the last
@@ -22,7 +22,7 @@
 // per group the CTA moves 4 KB of codes and BN*128 bytes of x through it.
 //
 // mbarriers: full[s] (TMA bytes landed), sempty[s] (MMAs of smem stage s
-// done), afull[a] (256 dequant arrivals), aempty[a] (MMAs reading TMEM stage
+// done), afull[a] (512 dequant arrivals), aempty[a] (MMAs reading TMEM stage
 // a done), done (every MMA done).  Every mbarrier wait is bounded in time: on
 // expiry the waiter sets *err, all roles wind down, the producer waits
 // (bounded) for its copies in flight, and TMEM is freed after the final MMA
@@ -141,6 +141,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
           "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+          "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
@@ -181,7 +188,12 @@ __device__ __forceinline__ void dq_word(uint32_t w, __half2 s2, __half2 b2, uint
     out[3] = __byte_perm(p[2], p[3], 0x7632);
 }
 
-// 8 columns into raw registers; complete them with tmem_ld_wait()
+// 4 / 8 columns into raw registers; complete them with tmem_ld_wait()
+__device__ __forceinline__ void tmem_ld4_async(uint32_t taddr, uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -218,7 +230,8 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
 
 constexpr int TC_JOBS = 4;
 constexpr int TC_BM = 128;
-constexpr int TC_DQW = 8;                          // dequant / epilogue warps
+constexpr int TC_QW = 4;                           // dequant warps per TMEM lane quadrant
+constexpr int TC_DQW = 4 * TC_QW;                  // dequant / epilogue warps
 constexpr int TC_THREADS = 64 + 32 * TC_DQW;       // + producer warp + MMA warp
 constexpr int TC_TMEM_COLS = 512;
 constexpr int TC_A_COL = 256;  // A stages live in TMEM columns [256, 512)
@@ -245,7 +258,9 @@ struct TcCfg {
     static constexpr int X_BYTES = GPS * XBOX;
     static constexpr int STAGE = C_BYTES + X_BYTES;       // multiple of 1024
     static constexpr int ST_A = (TC_TMEM_COLS - TC_A_COL) / (32 * GPS);
-    static constexpr int SLOT = 4 * GPS;                  // ring slot bytes: GPS scales + GPS biases
+    static constexpr int CPR = 2 * GPS;                   // 16-byte code chunks per row per stage
+    static constexpr int CPW = CPR / TC_QW;               // chunks per dequant warp per stage
+    static constexpr int SLOT = 8;                        // ring slot: a 4-byte-aligned pair of scales + of biases
     static constexpr int SR_OFF = ST * STAGE;             // ring: [TC_SRING][32*TC_DQW] slots
     static constexpr int B_OFF = SR_OFF + TC_SRING * 32 * TC_DQW * SLOT;
     static constexpr int NBAR = 2 * ST + 2 * ST_A + 1;
@@ -256,7 +271,8 @@ struct TcCfg {
     static_assert(BN <= TC_A_COL, "accumulator columns");
     static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * BN * 4, "split-K receive buffers reuse the stage buffers");
     static_assert(TOTAL <= 227 * 1024, "shared memory per CTA");
-    static_assert(GPS % 2 == 0 && TC_DQW == 8, "two dequant warps per lane quadrant, GPS/2 groups each");
+    static_assert(CPR % TC_QW == 0 && CPW >= 1 && CPW <= 2, "a dequant warp's chunks lie in one group");
+    static_assert(BN % (4 * TC_QW) == 0, "accumulator columns per warp in units of 4");
 };
 
 // Byte offset of 16-byte chunk c of row r in a TMA tile with `rb`-byte rows
@@ -271,7 +287,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     using C = TcCfg<BN, GPS, ST>;
     constexpr int ST_A = C::ST_A;
-    constexpr int HG = GPS / 2;  // groups per dequant warp per stage
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::B_OFF);
@@ -317,8 +332,8 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     tc::tc_after();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
-    constexpr int HALF = BN / 2;  // accumulator columns per dequant warp
-    uint32_t acc[HALF];
+    constexpr int CW = BN / TC_QW;  // accumulator columns per dequant warp
+    uint32_t acc[CW];
 
     if (warp == 0) {
         if (lane == 0) {  // ---- TMA producer
@@ -361,23 +376,26 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             tc::umma_commit(done);  // after an early exit too: TMEM is freed only after the MMAs finish
         }
     } else {
-        // ---- dequant: row rl = the warp's TMEM lane quadrant; warps w and w+4
-        // split each stage's groups (half h takes groups [h*HG, (h+1)*HG))
+        // ---- dequant: row rl = the warp's TMEM lane quadrant; the TC_QW warps of
+        // a quadrant split each stage's code chunks (warp h: chunks [h*CPW, (h+1)*CPW),
+        // all inside group q0 = h*CPW/2)
+        constexpr int CPW = C::CPW;
         const int dt = tid - 64;
         const int q4 = warp & 3, h = (warp - 2) >> 2;
         const int rl = 32 * q4 + lane;
         const int orow = min(m0 + rl, OUT - 1);
         const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
-        const __half* sc = (const __half*)jb.g.scales + (int64_t)orow * NG;
-        const __half* bi = (const __half*)jb.g.biases + (int64_t)orow * NG;
-        // ring slot of stage i for this thread: GPS scale halves, then GPS bias halves
+        const int q0 = (h * CPW) >> 1, qpair = q0 & ~1;
+        const __half* sc = (const __half*)jb.g.scales + (int64_t)orow * NG + qpair;
+        const __half* bi = (const __half*)jb.g.biases + (int64_t)orow * NG + qpair;
+        // ring slot of stage i for this thread: scales of groups (qpair, qpair+1), then biases
         __half* ring = reinterpret_cast<__half*>(smem + C::SR_OFF);
-        auto slot = [&](int i) { return ring + ((i % TC_SRING) * (32 * TC_DQW) + dt) * (2 * GPS); };
+        auto slot = [&](int i) { return ring + ((i % TC_SRING) * (32 * TC_DQW) + dt) * 4; };
         auto fetch = [&](int i) {
             if (i < nst) {
                 const int g = (s0 + i) * GPS;
-                tc::cp_async<2 * GPS>(slot(i), sc + g);
-                tc::cp_async<2 * GPS>(slot(i) + GPS, bi + g);
+                tc::cp_async<4>(slot(i), sc + g);
+                tc::cp_async<4>(slot(i) + 2, bi + g);
             }
             tc::cp_commit();
         };
@@ -391,18 +409,18 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             tc::tc_after();
             tc::cp_wait<TC_SRING - 1>();
             const __half* sh = slot(i);
+            const __half2 s2 = __half2half2(sh[q0 & 1]), b2 = __half2half2(sh[2 + (q0 & 1)]);
             const unsigned char* cs = smem + s * C::STAGE;
 #pragma unroll
-            for (int qq = 0; qq < HG; qq++) {
-                const int q = h * HG + qq;
-                const __half2 s2 = __half2half2(sh[q]), b2 = __half2half2(sh[GPS + q]);
-                const uint4 c0 = *reinterpret_cast<const uint4*>(cs + swz(rl, 2 * q, C::CROW));
-                const uint4 c1 = *reinterpret_cast<const uint4*>(cs + swz(rl, 2 * q + 1, C::CROW));
-                const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                uint32_t v[32];
-#pragma unroll
-                for (int w = 0; w < 8; w++) tc::dq_word(words[w], s2, b2, v + 4 * w);
-                tc::tmem_st32(tmem + lane_base + TC_A_COL + a * (32 * GPS) + q * 32, v);
+            for (int cc = 0; cc < CPW; cc++) {
+                const int ch = h * CPW + cc;
+                const uint4 cw = *reinterpret_cast<const uint4*>(cs + swz(rl, ch, C::CROW));
+                uint32_t v[16];
+                tc::dq_word(cw.x, s2, b2, v);
+                tc::dq_word(cw.y, s2, b2, v + 4);
+                tc::dq_word(cw.z, s2, b2, v + 8);
+                tc::dq_word(cw.w, s2, b2, v + 12);
+                tc::tmem_st16(tmem + lane_base + TC_A_COL + a * (32 * GPS) + ch * 16, v);
             }
             tc::tmem_st_wait();
             tc::tc_before();
@@ -415,20 +433,20 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         const GemvJob g = jb.g;  // a register copy: stores below cannot alias it
         const uint32_t tacc = tmem + lane_base;
         const int o = m0 + rl;
-        // this thread's HALF accumulator columns (row rl), all loads in flight at once
+        // this thread's CW accumulator columns (row rl), all loads in flight at once
 #pragma unroll
-        for (int c = 0; c < HALF; c += 8) tc::tmem_ld8_async(tacc + h * HALF + c, acc + c);
+        for (int c = 0; c < CW; c += 4) tc::tmem_ld4_async(tacc + h * CW + c, acc + c);
         tc::tmem_ld_wait();
         if (S == 1 && ok && o < OUT) {
-            const int c0 = n0 + h * HALF;
+            const int c0 = n0 + h * CW;
             if (g.act == ACT_NONE && g.out == OUT_F32) {
                 float* yo = (float*)g.y + (int64_t)c0 * g.y_stride + o;
 #pragma unroll
-                for (int c = 0; c < HALF; c++)
+                for (int c = 0; c < CW; c++)
                     if (c0 + c < args.R) yo[(int64_t)c * g.y_stride] = __uint_as_float(acc[c]);
             } else {
 #pragma unroll
-                for (int c = 0; c < HALF; c++)
+                for (int c = 0; c < CW; c++)
                     if (c0 + c < args.R) epilogue(g, o, c0 + c, __uint_as_float(acc[c]));
             }
         }
@@ -446,9 +464,9 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             const int rl = 32 * (warp & 3) + lane, h = (warp - 2) >> 2;
             const int zo = ((rl + 1) * S + TC_BM - 1) / TC_BM - 1;  // owner of row rl
             const int lr = rl - TC_BM * zo / S;
-            const uint32_t dst = tc::map_rank(rbuf + (uint32_t)((kz * BN + h * HALF) * NRM + lr) * 4, zo);
+            const uint32_t dst = tc::map_rank(rbuf + (uint32_t)((kz * BN + h * CW) * NRM + lr) * 4, zo);
 #pragma unroll
-            for (int c = 0; c < HALF; c++) tc::st_cluster_u32(dst + (uint32_t)(c * NRM) * 4, acc[c]);
+            for (int c = 0; c < CW; c++) tc::st_cluster_u32(dst + (uint32_t)(c * NRM) * 4, acc[c]);
         }
         tc::cluster_sync();
         if (warp >= 2 && !*(volatile int*)err) {
@@ -510,6 +528,45 @@ inline bool tc_job_ok(const GemvJob& j) {
            ((uintptr_t)j.scales & 7) == 0 && ((uintptr_t)j.biases & 7) == 0;
 }
 
+// How many (1, 1, S) clusters of this configuration the GPU holds at once
+// (cached per configuration and S; 0 when the query fails).
+template <int BN, int GPS, int ST>
+inline int tc_max_clusters_t(int S) {
+    static int cache[TC_MAX_SPLIT + 1] = {};
+    if (S < 1 || S > TC_MAX_SPLIT) return 0;
+    if (cache[S]) return cache[S] > 0 ? cache[S] : 0;
+    using C = TcCfg<BN, GPS, ST>;
+    auto kern = gemm_tc_kernel<BN, GPS, ST>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL) == cudaSuccess) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, S);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = C::TOTAL;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = S;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    cache[S] = n > 0 ? n : -1;
+    return n;
+}
+
+// the kernel configuration (stages) used for each tile width
+inline int tc_max_clusters(int BN, int S) {
+    switch (BN) {
+        case 16: return tc_max_clusters_t<16, 4, 6>(S);
+        case 32: return tc_max_clusters_t<32, 4, 5>(S);
+        case 64: return tc_max_clusters_t<64, 4, 4>(S);
+        default: return tc_max_clusters_t<128, 2, 4>(S);
+    }
+}
+
 inline TcPlan plan_tc(const GemvJobs& jobs, int njobs, int R, int sm_count) {
     TcPlan p{};
     if (R <= 8 || R > 256 || njobs < 1 || njobs > TC_JOBS) return p;
@@ -526,8 +583,12 @@ inline TcPlan plan_tc(const GemvJobs& jobs, int njobs, int R, int sm_count) {
     p.mblocks = (maxo + TC_BM - 1) / TC_BM;
     int ctas = 0;
     for (int i = 0; i < njobs; i++) ctas += (jobs.j[i].OUT + TC_BM - 1) / TC_BM * p.nnb;
+    // split K until about one CTA per SM, with at least two stages per split,
+    // and only as far as every cluster of the launch is resident at once
     int S = (sm_count + ctas - 1) / ctas;
-    S = std::max(1, std::min(std::min(S, minst / 2), TC_MAX_SPLIT));  // at least two stages per split
+    S = std::max(1, std::min(std::min(S, minst / 2), TC_MAX_SPLIT));
+    const int clusters = p.mblocks * njobs * p.nnb;
+    while (S > 1 && tc_max_clusters(p.BN, S) < clusters) S--;
     p.S = S;
     p.ok = true;
     return p;
@@ -579,17 +640,7 @@ inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, cudaStream_t st
     attr[0].val.clusterDim.z = a.S;
     cfg.attrs = attr;
     cfg.numAttrs = a.S > 1 ? 1 : 0;
-    if (a.S > 1) {
-        // a cluster of S one-CTA-per-SM blocks must fit in a GPC (checked once per S)
-        static int fits[TC_MAX_SPLIT + 1] = {};
-        if (!fits[a.S]) {
-            int n = 0;
-            e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-            if (e != cudaSuccess) return e;
-            fits[a.S] = n > 0 ? 1 : -1;
-        }
-        if (fits[a.S] < 0) return cudaErrorLaunchOutOfResources;
-    }
+    if (a.S > 1 && tc_max_clusters_t<BN, GPS, ST>(a.S) < 1) return cudaErrorLaunchOutOfResources;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
