@@ -127,6 +127,15 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
         ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
+// D[tmem] (+)= A[smem] * B[smem]^T
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar)) : "memory");
 }
@@ -238,8 +247,13 @@ constexpr int TC_A_COL = 256;  // A stages live in TMEM columns [256, 512)
 constexpr int TC_SRING = 4;    // scale / bias prefetch ring (stages)
 constexpr int TC_MAX_SPLIT = 8;  // split-K CTAs of one tile form one cluster
 
+// Weight formats: TC_Q4 = MLX affine 4-bit group-64 codes (dequantised into
+// TMEM), TC_F16 = dense fp16 [OUT, IN] (read by the MMA straight from shared memory).
+enum : int { TC_Q4 = 0, TC_F16 = 1 };
+
 struct alignas(64) TcJob {
-    CUtensorMap wmap;  // codes: dims {IN/8, OUT} u32, box {8*GPS, 128}, swizzled
+    CUtensorMap wmap;  // TC_Q4: codes {IN/8, OUT} u32, box {8*GPS, 128}, swizzled;
+                       // TC_F16: weights {IN, OUT} fp16, box {64, 128}, 128-byte swizzle
     CUtensorMap xmap;  // activations: dims {IN, R} fp16, box {64, BN}, 128-byte swizzle
     GemvJob g;         // scales, biases, OUT, IN, epilogue
 };
@@ -250,9 +264,9 @@ struct TcArgs {
     int* err;
 };
 
-template <int BN, int GPS, int ST>
+template <int FMT, int BN, int GPS, int ST>
 struct TcCfg {
-    static constexpr int CROW = 32 * GPS;                 // code bytes per row per stage
+    static constexpr int CROW = FMT == TC_Q4 ? 32 * GPS : 128 * GPS;  // weight bytes per row per stage
     static constexpr int C_BYTES = TC_BM * CROW;
     static constexpr int XBOX = BN * 128;                 // one x box (64 columns)
     static constexpr int X_BYTES = GPS * XBOX;
@@ -262,7 +276,7 @@ struct TcCfg {
     static constexpr int CPW = CPR / TC_QW;               // chunks per dequant warp per stage
     static constexpr int SLOT = 8;                        // ring slot: a 4-byte-aligned pair of scales + of biases
     static constexpr int SR_OFF = ST * STAGE;             // ring: [TC_SRING][32*TC_DQW] slots
-    static constexpr int B_OFF = SR_OFF + TC_SRING * 32 * TC_DQW * SLOT;
+    static constexpr int B_OFF = SR_OFF + (FMT == TC_Q4 ? TC_SRING * 32 * TC_DQW * SLOT : 0);
     static constexpr int NBAR = 2 * ST + 2 * ST_A + 1;
     static constexpr int T_OFF = B_OFF + NBAR * 8;
     static constexpr int TOTAL = T_OFF + 16 + 1024;       // + slack for 1024-byte alignment
@@ -271,7 +285,8 @@ struct TcCfg {
     static_assert(BN <= TC_A_COL, "accumulator columns");
     static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * BN * 4, "split-K receive buffers reuse the stage buffers");
     static_assert(TOTAL <= 227 * 1024, "shared memory per CTA");
-    static_assert(CPR % TC_QW == 0 && CPW >= 1 && CPW <= 2, "a dequant warp's chunks lie in one group");
+    static_assert(FMT == TC_F16 || (CPR % TC_QW == 0 && CPW >= 1 && CPW <= 2),
+                  "a dequant warp's chunks lie in one group");
     static_assert(BN % (4 * TC_QW) == 0, "accumulator columns per warp in units of 4");
 };
 
@@ -282,10 +297,10 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c, uint32_t rb) {
     return off ^ (((off >> 7) & (rb / 16 - 1)) << 4);
 }
 
-template <int BN, int GPS, int ST>
+template <int FMT, int BN, int GPS, int ST>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ TcArgs args) {
-    using C = TcCfg<BN, GPS, ST>;
+    using C = TcCfg<FMT, BN, GPS, ST>;
     constexpr int ST_A = C::ST_A;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -304,7 +319,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     const int n0 = nblk * BN;
     // uniform over the cluster (same x, y, n-block), before any barrier or TMEM use
     if (m0 >= OUT || n0 >= args.R) return;
-    const int NG = IN / 64, NS = NG / GPS;
+    const int NG = (IN + 63) / 64, NS = NG / GPS;  // TC_Q4: IN % (64 GPS) == 0; TC_F16: GPS == 1
     const int s0 = (int)((int64_t)NS * kz / S), s1 = (int)((int64_t)NS * (kz + 1) / S);
     const int nst = s1 - s0;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -344,7 +359,12 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
                 unsigned char* st = smem + s * C::STAGE;
                 const int g = (s0 + i) * GPS;
                 tc::mbar_expect_tx(full + s, C::STAGE);
-                tc::tma_2d(st, &jb.wmap, full + s, 8 * g, m0);
+                if constexpr (FMT == TC_Q4) {
+                    tc::tma_2d(st, &jb.wmap, full + s, 8 * g, m0);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < GPS; q++) tc::tma_2d(st + q * TC_BM * 128, &jb.wmap, full + s, 64 * (g + q), m0);
+                }
 #pragma unroll
                 for (int q = 0; q < GPS; q++)
                     tc::tma_2d(st + C::C_BYTES + q * C::XBOX, &jb.xmap, full + s, 64 * (g + q), n0);
@@ -358,19 +378,27 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             constexpr uint32_t IDESC = tc::idesc_f16(TC_BM, BN);
             for (int i = 0; i < nst; i++) {
                 const int s = i % ST, a = i % ST_A;
-                if (!tc::mbar_wait(full + s, (i / ST) & 1, err) || !tc::mbar_wait(afull + a, (i / ST_A) & 1, err))
-                    break;
+                if (!tc::mbar_wait(full + s, (i / ST) & 1, err)) break;
+                if (FMT == TC_Q4 && !tc::mbar_wait(afull + a, (i / ST_A) & 1, err)) break;
                 tc::tc_after();
                 const uint32_t xs = tc::saddr(smem + s * C::STAGE + C::C_BYTES);
                 const uint32_t ta = tmem + TC_A_COL + a * (32 * GPS);
+                const uint32_t ws = tc::saddr(smem + s * C::STAGE);
 #pragma unroll
                 for (int q = 0; q < GPS; q++) {
                     const uint64_t bd = tc::sw128_desc(xs + q * C::XBOX);
+                    if constexpr (FMT == TC_Q4) {
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        tc::umma_ts(tmem, ta + q * 32 + kk * 8, bd + 2 * kk, IDESC, (i | q | kk) ? 1u : 0u);
+                        for (int kk = 0; kk < 4; kk++)
+                            tc::umma_ts(tmem, ta + q * 32 + kk * 8, bd + 2 * kk, IDESC, (i | q | kk) ? 1u : 0u);
+                    } else {
+                        const uint64_t ad = tc::sw128_desc(ws + q * TC_BM * 128);
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            tc::umma_ss(tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (i | q | kk) ? 1u : 0u);
+                    }
                 }
-                tc::umma_commit(aempty + a);
+                if constexpr (FMT == TC_Q4) tc::umma_commit(aempty + a);
                 tc::umma_commit(sempty + s);
             }
             tc::umma_commit(done);  // after an early exit too: TMEM is freed only after the MMAs finish
@@ -399,6 +427,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             }
             tc::cp_commit();
         };
+        if constexpr (FMT == TC_Q4) {
 #pragma unroll
         for (int i = 0; i < TC_SRING - 1; i++) fetch(i);
         for (int i = 0; i < nst; i++) {
@@ -427,6 +456,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             tc::mbar_arrive(afull + a);
         }
         tc::cp_wait<0>();
+        }
         ok = tc::mbar_wait(done, 0, err) && ok;
         tc::tc_after();
         // ---- accumulator: row rl, this warp's half of the BN columns
@@ -520,23 +550,35 @@ struct TcPlan {
 };
 
 // Whether a job can take the tcgen05 path: fp16 activations with rows
-// 16-byte aligned, IN a multiple of 256 (whole stages), 16-byte aligned codes,
-// 8-byte aligned scales and biases.
-inline bool tc_job_ok(const GemvJob& j) {
-    return j.IN % 256 == 0 && j.IN >= 256 && j.OUT >= 1 && j.x_stride % 8 == 0 &&
-           ((uintptr_t)j.x & 15) == 0 && ((uintptr_t)j.w & 15) == 0 && j.scales && j.biases &&
+// 16-byte aligned, 16-byte aligned weights; TC_Q4: IN a multiple of 256
+// (whole stages) and 8-byte aligned scales and biases; TC_F16: 16-byte rows.
+inline bool tc_job_ok(int FMT, const GemvJob& j) {
+    const bool common = j.OUT >= 1 && j.x_stride % 8 == 0 && ((uintptr_t)j.x & 15) == 0 &&
+                        ((uintptr_t)j.w & 15) == 0;
+    if (FMT == TC_F16) return common && j.IN >= 8 && j.IN % 8 == 0;
+    return common && j.IN % 256 == 0 && j.IN >= 256 && j.scales && j.biases &&
            ((uintptr_t)j.scales & 7) == 0 && ((uintptr_t)j.biases & 7) == 0;
 }
 
+// Kernel configurations (tile width BN, groups per stage GPS, stages ST) per
+// weight format; X(BN, GPS, ST) for TC_Q4 then TC_F16.
+#define RWKV_TC_CONFIGS(FMT, X)                                                      \
+    switch (BN) {                                                                   \
+        case 16: return FMT == TC_Q4 ? X(TC_Q4, 16, 4, 6) : X(TC_F16, 16, 1, 8);     \
+        case 32: return FMT == TC_Q4 ? X(TC_Q4, 32, 4, 5) : X(TC_F16, 32, 1, 8);     \
+        case 64: return FMT == TC_Q4 ? X(TC_Q4, 64, 4, 4) : X(TC_F16, 64, 1, 8);     \
+        default: return FMT == TC_Q4 ? X(TC_Q4, 128, 2, 4) : X(TC_F16, 128, 1, 6);   \
+    }
+
 // How many (1, 1, S) clusters of this configuration the GPU holds at once
 // (cached per configuration and S; 0 when the query fails).
-template <int BN, int GPS, int ST>
+template <int FMT, int BN, int GPS, int ST>
 inline int tc_max_clusters_t(int S) {
     static int cache[TC_MAX_SPLIT + 1] = {};
     if (S < 1 || S > TC_MAX_SPLIT) return 0;
     if (cache[S]) return cache[S] > 0 ? cache[S] : 0;
-    using C = TcCfg<BN, GPS, ST>;
-    auto kern = gemm_tc_kernel<BN, GPS, ST>;
+    using C = TcCfg<FMT, BN, GPS, ST>;
+    auto kern = gemm_tc_kernel<FMT, BN, GPS, ST>;
     int n = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL) == cudaSuccess) {
         cudaLaunchConfig_t cfg{};
@@ -557,28 +599,26 @@ inline int tc_max_clusters_t(int S) {
     return n;
 }
 
-// the kernel configuration (stages) used for each tile width
-inline int tc_max_clusters(int BN, int S) {
-    switch (BN) {
-        case 16: return tc_max_clusters_t<16, 4, 6>(S);
-        case 32: return tc_max_clusters_t<32, 4, 5>(S);
-        case 64: return tc_max_clusters_t<64, 4, 4>(S);
-        default: return tc_max_clusters_t<128, 2, 4>(S);
-    }
+inline int tc_max_clusters(int FMT, int BN, int S) {
+#define X_(F, B, G, T) tc_max_clusters_t<F, B, G, T>(S)
+    RWKV_TC_CONFIGS(FMT, X_)
+#undef X_
 }
 
-inline TcPlan plan_tc(const GemvJobs& jobs, int njobs, int R, int sm_count) {
+inline int tc_gps(int FMT, int BN) { return FMT == TC_F16 ? 1 : BN <= 64 ? 4 : 2; }
+
+inline TcPlan plan_tc(int FMT, const GemvJobs& jobs, int njobs, int R, int sm_count) {
     TcPlan p{};
     if (R <= 8 || R > 256 || njobs < 1 || njobs > TC_JOBS) return p;
     for (int i = 0; i < njobs; i++)
-        if (!tc_job_ok(jobs.j[i])) return p;
+        if (!tc_job_ok(FMT, jobs.j[i])) return p;
     p.BN = R <= 16 ? 16 : R <= 32 ? 32 : R <= 64 ? 64 : 128;
-    p.GPS = p.BN <= 64 ? 4 : 2;
+    p.GPS = tc_gps(FMT, p.BN);
     p.nnb = (R + p.BN - 1) / p.BN;
     int maxo = 0, minst = 1 << 30;
     for (int i = 0; i < njobs; i++) {
         maxo = std::max(maxo, jobs.j[i].OUT);
-        minst = std::min(minst, jobs.j[i].IN / 64 / p.GPS);
+        minst = std::min(minst, (jobs.j[i].IN + 63) / 64 / p.GPS);
     }
     p.mblocks = (maxo + TC_BM - 1) / TC_BM;
     int ctas = 0;
@@ -588,17 +628,17 @@ inline TcPlan plan_tc(const GemvJobs& jobs, int njobs, int R, int sm_count) {
     int S = (sm_count + ctas - 1) / ctas;
     S = std::max(1, std::min(std::min(S, minst / 2), TC_MAX_SPLIT));
     const int clusters = p.mblocks * njobs * p.nnb;
-    while (S > 1 && tc_max_clusters(p.BN, S) < clusters) S--;
+    while (S > 1 && tc_max_clusters(FMT, p.BN, S) < clusters) S--;
     p.S = S;
     p.ok = true;
     return p;
 }
 
-inline bool encode_tc_maps(TcJob& t, const GemvJob& j, int R, int BN, int GPS) {
+inline bool encode_tc_maps(int FMT, TcJob& t, const GemvJob& j, int R, int BN, int GPS) {
     auto enc = tensor_map_encoder();
     if (!enc) return false;
     t.g = j;
-    {
+    if (FMT == TC_Q4) {
         cuuint64_t dims[2] = {(cuuint64_t)(j.IN / 8), (cuuint64_t)j.OUT};
         cuuint64_t strides[1] = {(cuuint64_t)j.IN / 2};
         cuuint32_t box[2] = {(cuuint32_t)(8 * GPS), (cuuint32_t)TC_BM};
@@ -606,6 +646,15 @@ inline bool encode_tc_maps(TcJob& t, const GemvJob& j, int R, int BN, int GPS) {
         if (enc(&t.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, (void*)j.w, dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE,
                 GPS == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    } else {
+        cuuint64_t dims[2] = {(cuuint64_t)j.IN, (cuuint64_t)j.OUT};
+        cuuint64_t strides[1] = {(cuuint64_t)j.IN * 2};
+        cuuint32_t box[2] = {64, (cuuint32_t)TC_BM};
+        cuuint32_t es[2] = {1, 1};
+        if (enc(&t.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)j.w, dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
     }
@@ -622,10 +671,10 @@ inline bool encode_tc_maps(TcJob& t, const GemvJob& j, int R, int BN, int GPS) {
     return true;
 }
 
-template <int BN, int GPS, int ST>
+template <int FMT, int BN, int GPS, int ST>
 inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, cudaStream_t st) {
-    using C = TcCfg<BN, GPS, ST>;
-    auto kern = gemm_tc_kernel<BN, GPS, ST>;
+    using C = TcCfg<FMT, BN, GPS, ST>;
+    auto kern = gemm_tc_kernel<FMT, BN, GPS, ST>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
@@ -640,27 +689,27 @@ inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, cudaStream_t st
     attr[0].val.clusterDim.z = a.S;
     cfg.attrs = attr;
     cfg.numAttrs = a.S > 1 ? 1 : 0;
-    if (a.S > 1 && tc_max_clusters_t<BN, GPS, ST>(a.S) < 1) return cudaErrorLaunchOutOfResources;
+    if (a.S > 1 && tc_max_clusters_t<FMT, BN, GPS, ST>(a.S) < 1) return cudaErrorLaunchOutOfResources;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 // jobs -> tensor maps -> launch.  err: device int that a wait which gives up
 // sets to 1.
-inline cudaError_t launch_tc(const GemvJobs& jobs, int njobs, int R, const TcPlan& p, int* err,
-                             cudaStream_t st) {
+inline cudaError_t launch_tc(int FMT, const GemvJobs& jobs, int njobs, int R, const TcPlan& p,
+                             int* err, cudaStream_t st) {
     TcArgs a{};
     for (int i = 0; i < njobs; i++)
-        if (!encode_tc_maps(a.j[i], jobs.j[i], R, p.BN, p.GPS)) return cudaErrorInvalidValue;
+        if (!encode_tc_maps(FMT, a.j[i], jobs.j[i], R, p.BN, p.GPS)) return cudaErrorInvalidValue;
     a.njobs = njobs;
     a.R = R;
     a.S = p.S;
     a.err = err;
-    switch (p.BN) {
-        case 16: return launch_tc_t<16, 4, 6>(a, p, st);
-        case 32: return launch_tc_t<32, 4, 5>(a, p, st);
-        case 64: return launch_tc_t<64, 4, 4>(a, p, st);
-        default: return launch_tc_t<128, 2, 4>(a, p, st);
-    }
+    const int BN = p.BN;
+#define X_(F, B, G, T) launch_tc_t<F, B, G, T>(a, p, st)
+    RWKV_TC_CONFIGS(FMT, X_)
+#undef X_
 }
+
+#undef RWKV_TC_CONFIGS
 
 }  // namespace rwkv

@@ -334,9 +334,9 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
         GemmScratch* sc = gemm_scratch();
         if (!sc) return fail(RWKV_E_CUDA, "rwkv_q_gemm: workspace allocation failed");
         // more than 8 rows: tcgen05 (TMA + TMEM) when the shapes allow it
-        const TcPlan tp = plan_tc(jobs, 1, rows, sc->sm_count);
+        const TcPlan tp = plan_tc(TC_Q4, jobs, 1, rows, sc->sm_count);
         if (tp.ok) {
-            cudaError_t e = launch_tc(jobs, 1, rows, tp, sc->err, st);
+            cudaError_t e = launch_tc(TC_Q4, jobs, 1, rows, tp, sc->err, st);
             if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemm_tc_kernel: %s", cudaGetErrorString(e));
             return ok();
         }

@@ -371,12 +371,11 @@ struct X070 {
 
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
         if (f16act) {
-            if (fmt == 0) {
-                const TcPlan tp = plan_tc(jobs, nj, R, sm_count);
-                if (tp.ok) {
-                    cudaError_t e = launch_tc(jobs, nj, R, tp, gerr, st);
-                    return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm_tc: %s", cudaGetErrorString(e));
-                }
+            const int tfmt = fmt == 0 ? TC_Q4 : TC_F16;
+            const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
+            if (tp.ok) {
+                cudaError_t e = launch_tc(tfmt, jobs, nj, R, tp, gerr, st);
+                return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm_tc: %s", cudaGetErrorString(e));
             }
             GemmPlan p = plan_any(jobs, nj, R, sm_count);
             if (p.ws_floats > gws_floats || p.tickets > gtickets_n)

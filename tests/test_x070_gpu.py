@@ -35,6 +35,22 @@ def test_step_logits_match_oracle(cuda, act, tol):
         assert rel_err(got, want) < tol, (t, rel_err(got, want))
 
 
+def test_wide_batch_tensor_core_path_matches_oracle(cuda):
+    """More than 8 rows at D=256: every 4-bit projection, the fp16 low-rank
+    projections and the head run on the tcgen05 GEMM (TMA + TMEM), whose
+    weights are dequantised into fp16 as MLX's quantized matmul does."""
+    from oracle import x070_oracle as XO
+    rows = 20
+    m, ref = tiny("f16", rows=rows, n_embd=256, vocab=200, seed=7)
+    ids = XO.splitmix_ids(rows, 4, vocab=200)
+    m.reset(rows)
+    st = ref.new_state(rows)
+    for t in range(ids.shape[1]):
+        got = m.step(torch.from_numpy(ids[:, t]).cuda()).cpu().numpy()
+        want = ref.step(ids[:, t], st)
+        assert rel_err(got, want) < 2e-3, (t, rel_err(got, want))
+
+
 def test_greedy_tokens_identical_fp32(cuda):
     """north_star: greedy decode token ids identical for the fp32 path."""
     from oracle import x070_oracle as XO
