@@ -151,7 +151,14 @@ wkv7_seq_fwd_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* _
 }
 
 // One decode step for `rows` independent rows, optionally with the fused tmix
-// tail.  grid (rows*H), block 256: 4 lanes per state row, 64 rows.
+// tail.  grid (rows*H), block 256: 4 lanes per state row (16 key columns
+// each), 64 rows -- the lane layout and summation order of the sequence
+// kernel, so a step equals the forward at T = 1 bit for bit.  The head's
+// vectors are staged in shared memory with 4 floats of padding after every
+// 32, so the four 16-column segments of a row (q = 0..3) fall in distinct
+// bank groups and a lane reads its columns with 16-byte loads.
+__device__ __forceinline__ int vpad(int c) { return c + ((c >> 5) << 2); }
+
 template <typename T, bool TAIL>
 __global__ void __launch_bounds__(256)
 wkv7_step_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* __restrict__ k,
@@ -159,34 +166,61 @@ wkv7_step_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* __re
                  float* __restrict__ h, T* __restrict__ y, const float* __restrict__ rk,
                  const float* __restrict__ lnw, const float* __restrict__ lnb,
                  const float* __restrict__ g, float* __restrict__ out, int H, float eps) {
-    __shared__ float ysh[HN];
+    constexpr int VP = HN + 8;
+    __shared__ __align__(16) float r_s[VP], w_s[VP], k_s[VP], a_s[VP], b_s[VP];
+    __shared__ __align__(16) float v_s[HN], ysh[HN], rk_s[HN], lw_s[HN], lb_s[HN], g_s[HN];
     const int rh = blockIdx.x;  // row*H + head
     const int hi = rh % H;
     const int dv = threadIdx.x / LPR, q = threadIdx.x % LPR, c0 = q * CPL;
     float* hp = h + (size_t)rh * HN * HN + (size_t)dv * HN + c0;
-    const size_t vb = (size_t)rh * HN;
+    const size_t vb = (size_t)rh * HN, hb = (size_t)hi * HN;
 
+    // state loads first; meanwhile the head's vectors (and the tail's
+    // parameters) go to shared memory, one column per thread
     float s[CPL];
 #pragma unroll
     for (int j = 0; j < CPL; j += 4) {
-        float4 t4 = *reinterpret_cast<const float4*>(hp + j);
+        const float4 t4 = *reinterpret_cast<const float4*>(hp + j);
         s[j] = t4.x; s[j + 1] = t4.y; s[j + 2] = t4.z; s[j + 3] = t4.w;
     }
+    {
+        const int c = threadIdx.x & (HN - 1), cp = vpad(c);
+        switch (threadIdx.x >> 6) {
+            case 0: r_s[cp] = to_f(r[vb + c]); w_s[cp] = to_f(w[vb + c]); break;
+            case 1: k_s[cp] = to_f(k[vb + c]); v_s[c] = to_f(v[vb + c]); break;
+            case 2: a_s[cp] = to_f(a[vb + c]); b_s[cp] = to_f(b[vb + c]); break;
+            default:
+                if (TAIL) { rk_s[c] = rk[hb + c]; lw_s[c] = lnw[hb + c]; lb_s[c] = lnb[hb + c]; g_s[c] = g[vb + c]; }
+        }
+    }
+    __syncthreads();
+    const int cb = vpad(c0);  // a lane's 16 columns are contiguous after padding
     float sa0 = 0.f, sa1 = 0.f;
 #pragma unroll
-    for (int j = 0; j < CPL; j += 2) {
-        sa0 = fmaf(s[j], to_f(a[vb + c0 + j]), sa0);
-        sa1 = fmaf(s[j + 1], to_f(a[vb + c0 + j + 1]), sa1);
+    for (int j = 0; j < CPL; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(a_s + cb + j);
+        sa0 = fmaf(s[j], a4.x, sa0);
+        sa1 = fmaf(s[j + 1], a4.y, sa1);
+        sa0 = fmaf(s[j + 2], a4.z, sa0);
+        sa1 = fmaf(s[j + 3], a4.w, sa1);
     }
     const float sa = group_sum<LPR>(sa0 + sa1);
-    const float vv = to_f(v[vb + dv]);
+    const float vv = v_s[dv];
     float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-    for (int j = 0; j < CPL; j++) {
-        const int c = c0 + j;
-        s[j] = fmaf(to_f(w[vb + c]), s[j], fmaf(vv, to_f(k[vb + c]), sa * to_f(b[vb + c])));
-        if (j & 1) y1 = fmaf(s[j], to_f(r[vb + c]), y1);
-        else y0 = fmaf(s[j], to_f(r[vb + c]), y0);
+    for (int j = 0; j < CPL; j += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(w_s + cb + j);
+        const float4 k4 = *reinterpret_cast<const float4*>(k_s + cb + j);
+        const float4 b4 = *reinterpret_cast<const float4*>(b_s + cb + j);
+        const float4 r4 = *reinterpret_cast<const float4*>(r_s + cb + j);
+        s[j] = fmaf(w4.x, s[j], fmaf(vv, k4.x, sa * b4.x));
+        y0 = fmaf(s[j], r4.x, y0);
+        s[j + 1] = fmaf(w4.y, s[j + 1], fmaf(vv, k4.y, sa * b4.y));
+        y1 = fmaf(s[j + 1], r4.y, y1);
+        s[j + 2] = fmaf(w4.z, s[j + 2], fmaf(vv, k4.z, sa * b4.z));
+        y0 = fmaf(s[j + 2], r4.z, y0);
+        s[j + 3] = fmaf(w4.w, s[j + 3], fmaf(vv, k4.w, sa * b4.w));
+        y1 = fmaf(s[j + 3], r4.w, y1);
     }
     const float yy = group_sum<LPR>(y0 + y1);
 #pragma unroll
@@ -200,18 +234,15 @@ wkv7_step_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* __re
     __syncthreads();
     if (threadIdx.x >= 32) return;
     // Tail on one warp: two values per lane (WKV7DecodeKernels.swift:123-157).
-    const int l = threadIdx.x;
+    const int l = threadIdx.x, lp = vpad(l), lp2 = vpad(l + 32);
     const float x0 = ysh[l], x1 = ysh[l + 32];
     const float mean = warp_sum(x0 + x1) * (1.0f / HN);
     const float d0 = x0 - mean, d1 = x1 - mean;
     const float var = warp_sum(d0 * d0 + d1 * d1) * (1.0f / HN);
     const float inv = 1.0f / sqrtf(var + eps);
-    const size_t hb = (size_t)hi * HN;
-    const float dp = warp_sum(to_f(r[vb + l]) * to_f(k[vb + l]) * rk[hb + l] +
-                              to_f(r[vb + l + 32]) * to_f(k[vb + l + 32]) * rk[hb + l + 32]);
-    out[vb + l] = (d0 * inv * lnw[hb + l] + lnb[hb + l] + dp * to_f(v[vb + l])) * g[vb + l];
-    out[vb + l + 32] =
-        (d1 * inv * lnw[hb + l + 32] + lnb[hb + l + 32] + dp * to_f(v[vb + l + 32])) * g[vb + l + 32];
+    const float dp = warp_sum(r_s[lp] * k_s[lp] * rk_s[l] + r_s[lp2] * k_s[lp2] * rk_s[l + 32]);
+    out[vb + l] = (d0 * inv * lw_s[l] + lb_s[l] + dp * v_s[l]) * g_s[l];
+    out[vb + l + 32] = (d1 * inv * lw_s[l + 32] + lb_s[l + 32] + dp * v_s[l + 32]) * g_s[l + 32];
 }
 
 // Standalone tail: one warp per (row, head), S % 32 == 0, S <= 256.

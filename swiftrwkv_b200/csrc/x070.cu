@@ -450,7 +450,7 @@ struct X070 {
             if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
             if ((rc = gemv(1, U, nu, R, st))) return rc;
             mark("lora_up");
-            x070_wkv_kernel<A><<<R * H, 256, 0, st>>>(r, wdec, k, v, a, vv, vfirst, w.kkw, w.kaw, w.rkw,
+            x070_wkv_kernel<A><<<R * H, 128, 0, st>>>(r, wdec, k, v, a, vv, vfirst, w.kkw, w.kaw, w.rkw,
                                                       w.lnxw, w.lnxb, g, st8, (A*)tail, H, l == 0);
             if ((rc = check_launch("x070_wkv_kernel"))) return rc;
             mark("wkv_step_tail");

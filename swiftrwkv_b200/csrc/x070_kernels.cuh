@@ -186,16 +186,19 @@ x070_ln_out_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
     }
 }
 
-// WKV part of tmixStep for one (row, head), 256 threads = 64 state rows x 4
-// lanes x 16 key columns:
+// WKV part of tmixStep for one (row, head):
 //   kk = l2norm(k * k_k);  k' = k * (1 + (a - 1) * k_a)
 //   v' = v (layer 0, also stored as v_first) or v + (v_first - v) * vv
 //   step with (r, w, k', v', -kk, kk * a); tail -> out (act type).
-// Every thread issues its four 16-byte state loads first; meanwhile two warps
-// build the head's vectors in shared memory, so a thread keeps only its 16
-// state values in registers and many (row, head) CTAs fit on an SM.
+// 128 threads = 4 warps x 16 state rows.  A warp updates two rows per pass:
+// lanes 0-15 row dv, lanes 16-31 row dv+1, lane l holding key columns
+// 4(l%16) .. 4(l%16)+3 (one 16-byte load per row, a warp load covers 512
+// contiguous bytes).  Row reductions (S a, S r) are 16-lane shuffles.  All of
+// a warp's 16 rows are loaded before the first is used; two warps meanwhile
+// build the head's vectors, and the tail's per-head parameters are fetched
+// in the prologue, so a CTA waits on global memory about once.
 template <typename A>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(128)
 x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
                 const float* __restrict__ kraw, const float* __restrict__ vraw,
                 const float* __restrict__ a, const float* __restrict__ vv,
@@ -204,21 +207,20 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
                 const float* __restrict__ lnxw, const float* __restrict__ lnxb,
                 const float* __restrict__ g, float* __restrict__ state, A* __restrict__ out,
                 int H, int layer0) {
-    constexpr int N = 64, LPR = 4, CPL = 16;
+    constexpr int N = 64, RPW = 16;  // rows per warp
     __shared__ __align__(16) float r_s[N], w_s[N], kp_s[N], aw_s[N], bw_s[N], v_s[N], y_s[N];
+    __shared__ __align__(16) float rk_s[N], lw_s[N], lb_s[N], g_s[N];
     __shared__ float red[2];
     const int rh = blockIdx.x;
     const int hi = rh % H;
-    const int dv = threadIdx.x / LPR, q = threadIdx.x % LPR, c0 = q * CPL;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = lane >> 4, c0 = 4 * (lane & 15);
     const size_t vb = (size_t)rh * N;   // [R, H, N] element base of this (row, head)
     const size_t hb = (size_t)hi * N;   // [H, N] parameter base
-    float* hp = state + (size_t)rh * N * N + (size_t)dv * N + c0;
-    float s[CPL];
+    float* hp = state + (size_t)rh * N * N + (size_t)(RPW * warp + half) * N + c0;
+    float4 s[RPW / 2];
 #pragma unroll
-    for (int j = 0; j < CPL; j += 4) {
-        const float4 t4 = *reinterpret_cast<const float4*>(hp + j);
-        s[j] = t4.x; s[j + 1] = t4.y; s[j + 2] = t4.z; s[j + 3] = t4.w;
-    }
+    for (int p = 0; p < RPW / 2; p++) s[p] = *reinterpret_cast<const float4*>(hp + (size_t)2 * p * N);
     if (threadIdx.x < N) {  // warps 0-1: per-column vectors; column c = threadIdx.x
         const int c = threadIdx.x;
         const float kr = kraw[vb + c], aa = a[vb + c];
@@ -243,42 +245,46 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
         const float kn = kk * inv;
         aw_s[c] = -kn;
         bw_s[c] = kn * aa;
+    } else {  // warps 2-3: the tail's per-head parameters and the gate
+        const int c = threadIdx.x - N;
+        rk_s[c] = rkw[hb + c];
+        lw_s[c] = lnxw[hb + c];
+        lb_s[c] = lnxb[hb + c];
+        g_s[c] = g[vb + c];
     }
     __syncthreads();
-    float sa0 = 0.f, sa1 = 0.f;
+    const float4 aw = *reinterpret_cast<const float4*>(aw_s + c0);
+    const float4 bw = *reinterpret_cast<const float4*>(bw_s + c0);
+    const float4 ww = *reinterpret_cast<const float4*>(w_s + c0);
+    const float4 kp = *reinterpret_cast<const float4*>(kp_s + c0);
+    const float4 rr = *reinterpret_cast<const float4*>(r_s + c0);
 #pragma unroll
-    for (int j = 0; j < CPL; j += 2) {
-        sa0 = fmaf(s[j], aw_s[c0 + j], sa0);
-        sa1 = fmaf(s[j + 1], aw_s[c0 + j + 1], sa1);
+    for (int p = 0; p < RPW / 2; p++) {
+        const int dv = RPW * warp + 2 * p + half;
+        float4 t = s[p];
+        const float sa = group_sum<16>(fmaf(t.x, aw.x, fmaf(t.y, aw.y, fmaf(t.z, aw.z, t.w * aw.w))));
+        const float vd = v_s[dv];
+        t.x = fmaf(ww.x, t.x, fmaf(vd, kp.x, sa * bw.x));
+        t.y = fmaf(ww.y, t.y, fmaf(vd, kp.y, sa * bw.y));
+        t.z = fmaf(ww.z, t.z, fmaf(vd, kp.z, sa * bw.z));
+        t.w = fmaf(ww.w, t.w, fmaf(vd, kp.w, sa * bw.w));
+        *reinterpret_cast<float4*>(hp + (size_t)2 * p * N) = t;
+        const float yy = group_sum<16>(fmaf(t.x, rr.x, fmaf(t.y, rr.y, fmaf(t.z, rr.z, t.w * rr.w))));
+        if ((lane & 15) == 0) y_s[dv] = yy;
     }
-    const float sa = group_sum<LPR>(sa0 + sa1);
-    const float vd = v_s[dv];
-    float y0 = 0.f, y1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < CPL; j++) {
-        const int c = c0 + j;
-        s[j] = fmaf(w_s[c], s[j], fmaf(vd, kp_s[c], sa * bw_s[c]));
-        if (j & 1) y1 = fmaf(s[j], r_s[c], y1);
-        else y0 = fmaf(s[j], r_s[c], y0);
-    }
-    const float yy = group_sum<LPR>(y0 + y1);
-#pragma unroll
-    for (int j = 0; j < CPL; j += 4)
-        *reinterpret_cast<float4*>(hp + j) = make_float4(s[j], s[j + 1], s[j + 2], s[j + 3]);
-    if (q == 0) y_s[dv] = yy;
     __syncthreads();
     if (threadIdx.x >= 32) return;
     // tail on one warp: GroupNorm(64e-5) of y, bonus (sum r*k'*r_k) * v', gate
     const int l = threadIdx.x;
-    float dp = r_s[l] * kp_s[l] * rkw[hb + l] + r_s[l + 32] * kp_s[l + 32] * rkw[hb + l + 32];
+    float dp = r_s[l] * kp_s[l] * rk_s[l] + r_s[l + 32] * kp_s[l + 32] * rk_s[l + 32];
     dp = warp_sum(dp);
     const float x0 = y_s[l], x1 = y_s[l + 32];
     const float mean = warp_sum(x0 + x1) * (1.0f / N);
     const float d0 = x0 - mean, d1 = x1 - mean;
     const float var = warp_sum(d0 * d0 + d1 * d1) * (1.0f / N);
     const float invs = 1.0f / sqrtf(var + 64e-5f);
-    const float o0 = (d0 * invs * lnxw[hb + l] + lnxb[hb + l] + dp * v_s[l]) * g[vb + l];
-    const float o1 = (d1 * invs * lnxw[hb + l + 32] + lnxb[hb + l + 32] + dp * v_s[l + 32]) * g[vb + l + 32];
+    const float o0 = (d0 * invs * lw_s[l] + lb_s[l] + dp * v_s[l]) * g_s[l];
+    const float o1 = (d1 * invs * lw_s[l + 32] + lb_s[l + 32] + dp * v_s[l + 32]) * g_s[l + 32];
     st_act(out + vb + l, o0);
     st_act(out + vb + l + 32, o1);
 }
