@@ -21,8 +21,8 @@
 // Keeping A in TMEM means the dequantised weights never touch shared memory:
 // per group the CTA moves 4 KB of codes and BN*128 bytes of x through it.
 //
-// mbarriers: full[s] (TMA bytes landed), sempty[s] (MMAs of smem stage s
-// done), afull[a] (512 dequant arrivals), aempty[a] (MMAs reading TMEM stage
+// mbarriers: wfull[s] / xfull[s] (the stage's weight / activation bytes
+// landed), sempty[s] (MMAs of smem stage s done), afull[a] (512 dequant arrivals), aempty[a] (MMAs reading TMEM stage
 // a done), done (every MMA done).  Every mbarrier wait is bounded in time: on
 // expiry the waiter sets *err, all roles wind down, the producer waits
 // (bounded) for its copies in flight, and TMEM is freed after the final MMA
@@ -277,7 +277,7 @@ struct TcCfg {
     static constexpr int SLOT = 8;                        // ring slot: a 4-byte-aligned pair of scales + of biases
     static constexpr int SR_OFF = ST * STAGE;             // ring: [TC_SRING][32*TC_DQW] slots
     static constexpr int B_OFF = SR_OFF + (FMT == TC_Q4 ? TC_SRING * 32 * TC_DQW * SLOT : 0);
-    static constexpr int NBAR = 2 * ST + 2 * ST_A + 1;
+    static constexpr int NBAR = 3 * ST + 2 * ST_A + 1;
     static constexpr int T_OFF = B_OFF + NBAR * 8;
     static constexpr int TOTAL = T_OFF + 16 + 1024;       // + slack for 1024-byte alignment
     static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
@@ -304,8 +304,9 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     constexpr int ST_A = C::ST_A;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::B_OFF);
-    uint64_t* sempty = full + ST;
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::B_OFF);
+    uint64_t* xfull = wfull + ST;
+    uint64_t* sempty = xfull + ST;
     uint64_t* afull = sempty + ST;
     uint64_t* aempty = afull + ST_A;
     uint64_t* done = aempty + ST_A;
@@ -326,8 +327,10 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     int* err = args.err;
 
     if (tid == 0) {
+        pdl_trigger();
         for (int s = 0; s < ST; s++) {
-            tc::mbar_init(full + s, 1);
+            tc::mbar_init(wfull + s, 1);
+            tc::mbar_init(xfull + s, 1);
             tc::mbar_init(sempty + s, 1);
         }
         for (int a = 0; a < ST_A; a++) {
@@ -352,33 +355,52 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
 
     if (warp == 0) {
         if (lane == 0) {  // ---- TMA producer
-            int issued = 0;
-            for (int i = 0; i < nst; i++) {
-                const int s = i % ST;
-                if (i >= ST && !tc::mbar_wait(sempty + s, ((i / ST) - 1) & 1, err)) break;
+            // weights do not depend on the previous kernel: the first stages'
+            // weights stream (and are dequantised) before its activations are ready
+            auto load_w = [&](int i) {
+                const int s = i % ST, g = (s0 + i) * GPS;
                 unsigned char* st = smem + s * C::STAGE;
-                const int g = (s0 + i) * GPS;
-                tc::mbar_expect_tx(full + s, C::STAGE);
+                tc::mbar_expect_tx(wfull + s, C::C_BYTES);
                 if constexpr (FMT == TC_Q4) {
-                    tc::tma_2d(st, &jb.wmap, full + s, 8 * g, m0);
+                    tc::tma_2d(st, &jb.wmap, wfull + s, 8 * g, m0);
                 } else {
 #pragma unroll
-                    for (int q = 0; q < GPS; q++) tc::tma_2d(st + q * TC_BM * 128, &jb.wmap, full + s, 64 * (g + q), m0);
+                    for (int q = 0; q < GPS; q++) tc::tma_2d(st + q * TC_BM * 128, &jb.wmap, wfull + s, 64 * (g + q), m0);
                 }
+            };
+            auto load_x = [&](int i) {
+                const int s = i % ST, g = (s0 + i) * GPS;
+                unsigned char* st = smem + s * C::STAGE;
+                tc::mbar_expect_tx(xfull + s, C::X_BYTES);
 #pragma unroll
                 for (int q = 0; q < GPS; q++)
-                    tc::tma_2d(st + C::C_BYTES + q * C::XBOX, &jb.xmap, full + s, 64 * (g + q), n0);
+                    tc::tma_2d(st + C::C_BYTES + q * C::XBOX, &jb.xmap, xfull + s, 64 * (g + q), n0);
+            };
+            const int pre = min(ST, nst);
+            for (int i = 0; i < pre; i++) load_w(i);
+            pdl_wait();
+            for (int i = 0; i < pre; i++) load_x(i);
+            int issued = pre;
+            for (int i = pre; i < nst; i++) {
+                const int s = i % ST;
+                if (!tc::mbar_wait(sempty + s, ((i / ST) - 1) & 1, err)) break;
+                load_w(i);
+                load_x(i);
                 issued = i + 1;
             }
             // the copies this thread issued have landed before the CTA may exit
-            for (int i = max(0, issued - ST); i < issued; i++) tc::mbar_wait(full + (i % ST), (i / ST) & 1, err);
+            for (int i = max(0, issued - ST); i < issued; i++) {
+                tc::mbar_wait(wfull + (i % ST), (i / ST) & 1, err);
+                tc::mbar_wait(xfull + (i % ST), (i / ST) & 1, err);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
             constexpr uint32_t IDESC = tc::idesc_f16(TC_BM, BN);
             for (int i = 0; i < nst; i++) {
                 const int s = i % ST, a = i % ST_A;
-                if (!tc::mbar_wait(full + s, (i / ST) & 1, err)) break;
+                if (!tc::mbar_wait(wfull + s, (i / ST) & 1, err) || !tc::mbar_wait(xfull + s, (i / ST) & 1, err))
+                    break;
                 if (FMT == TC_Q4 && !tc::mbar_wait(afull + a, (i / ST_A) & 1, err)) break;
                 tc::tc_after();
                 const uint32_t xs = tc::saddr(smem + s * C::STAGE + C::C_BYTES);
@@ -433,7 +455,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         for (int i = 0; i < nst; i++) {
             const int s = i % ST, a = i % ST_A;
             fetch(i + TC_SRING - 1);
-            if (!tc::mbar_wait(full + s, (i / ST) & 1, err)) { ok = false; break; }
+            if (!tc::mbar_wait(wfull + s, (i / ST) & 1, err)) { ok = false; break; }
             if (i >= ST_A && !tc::mbar_wait(aempty + a, ((i / ST_A) - 1) & 1, err)) { ok = false; break; }
             tc::tc_after();
             tc::cp_wait<TC_SRING - 1>();
@@ -459,6 +481,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         }
         ok = tc::mbar_wait(done, 0, err) && ok;
         tc::tc_after();
+        pdl_wait();  // (returns at once: the producer's wait preceded every MMA)
         // ---- accumulator: row rl, this warp's half of the BN columns
         const GemvJob g = jb.g;  // a register copy: stores below cannot alias it
         const uint32_t tacc = tmem + lane_base;
@@ -672,7 +695,7 @@ inline bool encode_tc_maps(int FMT, TcJob& t, const GemvJob& j, int R, int BN, i
 }
 
 template <int FMT, int BN, int GPS, int ST>
-inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, cudaStream_t st) {
+inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, bool pdl, cudaStream_t st) {
     using C = TcCfg<FMT, BN, GPS, ST>;
     auto kern = gemm_tc_kernel<FMT, BN, GPS, ST>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
@@ -682,21 +705,31 @@ inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, cudaStream_t st
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = C::TOTAL;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = a.S;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (a.S > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = a.S;
+        na++;
+    }
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = a.S > 1 ? 1 : 0;
+    cfg.numAttrs = na;
     if (a.S > 1 && tc_max_clusters_t<FMT, BN, GPS, ST>(a.S) < 1) return cudaErrorLaunchOutOfResources;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 // jobs -> tensor maps -> launch.  err: device int that a wait which gives up
 // sets to 1.
+// pdl: launch as a programmatic dependent of the previous kernel in the stream.
 inline cudaError_t launch_tc(int FMT, const GemvJobs& jobs, int njobs, int R, const TcPlan& p,
-                             int* err, cudaStream_t st) {
+                             int* err, cudaStream_t st, bool pdl = false) {
     TcArgs a{};
     for (int i = 0; i < njobs; i++)
         if (!encode_tc_maps(FMT, a.j[i], jobs.j[i], R, p.BN, p.GPS)) return cudaErrorInvalidValue;
@@ -705,7 +738,7 @@ inline cudaError_t launch_tc(int FMT, const GemvJobs& jobs, int njobs, int R, co
     a.S = p.S;
     a.err = err;
     const int BN = p.BN;
-#define X_(F, B, G, T) launch_tc_t<F, B, G, T>(a, p, st)
+#define X_(F, B, G, T) launch_tc_t<F, B, G, T>(a, p, pdl, st)
     RWKV_TC_CONFIGS(FMT, X_)
 #undef X_
 }

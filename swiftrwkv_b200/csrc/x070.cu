@@ -369,12 +369,16 @@ struct X070 {
 
     // ----- one decode step on `R` rows: ids -> logits, ids <- argmax
 
+    static int pdl_check(cudaError_t e, const char* name) {
+        return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
+    }
+
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
         if (f16act) {
             const int tfmt = fmt == 0 ? TC_Q4 : TC_F16;
             const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
             if (tp.ok) {
-                cudaError_t e = launch_tc(tfmt, jobs, nj, R, tp, gerr, st);
+                cudaError_t e = launch_tc(tfmt, jobs, nj, R, tp, gerr, st, /*pdl=*/true);
                 return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm_tc: %s", cudaGetErrorString(e));
             }
             GemmPlan p = plan_any(jobs, nj, R, sm_count);
@@ -415,16 +419,20 @@ struct X070 {
         A* mixp = (A*)mix;
         A* hidp = (A*)hidden;
         int rc;
-        x070_embed_kernel<<<R, GLUE_T, 0, st>>>(ids, emb.wq, emb.sc, emb.bi, nullptr, ln0w, ln0b, x, C, V);
-        if ((rc = check_launch("x070_embed_kernel"))) return rc;
+        if ((rc = pdl_check(launch_pdl(x070_embed_kernel, R, GLUE_T, 0, st, (const int32_t*)ids, (const uint32_t*)emb.wq,
+                                       (const __half*)emb.sc, (const __half*)emb.bi, (const __half*)nullptr,
+                                       (const float*)ln0w, (const float*)ln0b, x, C, V), "x070_embed_kernel")))
+            return rc;
         mark("embed");
         for (int l = 0; l < L; l++) {
             LayerW& w = lw[l];
             float* ts = tshift + (size_t)l * Rmax * C;
             float* cs = cshift + (size_t)l * Rmax * C;
             float* st8 = wkv + (size_t)l * Rmax * H * 64 * 64;
-            x070_tmix_in_kernel<A><<<R, GLUE_T, 0, st>>>(x, w.ln1w, w.ln1b, ts, w.coef6, mixp, R, C);
-            if ((rc = check_launch("x070_tmix_in_kernel"))) return rc;
+            if ((rc = pdl_check(launch_pdl(x070_tmix_in_kernel<A>, R, GLUE_T, 0, st, (const float*)x,
+                                           (const float*)w.ln1w, (const float*)w.ln1b, ts,
+                                           (const float*)w.coef6, mixp, R, C), "x070_tmix_in_kernel")))
+                return rc;
             mark("tmix_in");
             auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
             GemvJobs J{};
@@ -450,16 +458,22 @@ struct X070 {
             if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
             if ((rc = gemv(1, U, nu, R, st))) return rc;
             mark("lora_up");
-            x070_wkv_kernel<A><<<R * H, 128, 0, st>>>(r, wdec, k, v, a, vv, vfirst, w.kkw, w.kaw, w.rkw,
-                                                      w.lnxw, w.lnxb, g, st8, (A*)tail, H, l == 0);
-            if ((rc = check_launch("x070_wkv_kernel"))) return rc;
+            if ((rc = pdl_check(launch_pdl(x070_wkv_kernel<A>, R * H, 128, 0, st, (const float*)r,
+                                           (const float*)wdec, (const float*)k, (const float*)v,
+                                           (const float*)a, (const float*)vv, vfirst, (const float*)w.kkw,
+                                           (const float*)w.kaw, (const float*)w.rkw, (const float*)w.lnxw,
+                                           (const float*)w.lnxb, (const float*)g, st8, (A*)tail, H,
+                                           (int)(l == 0)), "x070_wkv_kernel")))
+                return rc;
             mark("wkv_step_tail");
             GemvJobs O{};
             O.j[0] = qjob(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C);
             if ((rc = gemv(0, O, 1, R, st))) return rc;
             mark("gemm_o");
-            x070_cmix_in_kernel<A><<<R, GLUE_T, 0, st>>>(x, w.ln2w, w.ln2b, cs, w.cxk, (A*)xk, C);
-            if ((rc = check_launch("x070_cmix_in_kernel"))) return rc;
+            if ((rc = pdl_check(launch_pdl(x070_cmix_in_kernel<A>, R, GLUE_T, 0, st, (const float*)x,
+                                           (const float*)w.ln2w, (const float*)w.ln2b, cs,
+                                           (const float*)w.cxk, (A*)xk, C), "x070_cmix_in_kernel")))
+                return rc;
             mark("cmix_in");
             GemvJobs K{};
             K.j[0] = qjob(w.key, xk, C, ACT_RELU2, aout, ffn, F);
@@ -470,18 +484,20 @@ struct X070 {
             if ((rc = gemv(0, Vv, 1, R, st))) return rc;
             mark("gemm_value");
         }
-        x070_ln_out_kernel<A><<<R, GLUE_T, 0, st>>>(x, lnow, lnob, (A*)lnout, C);
-        if ((rc = check_launch("x070_ln_out_kernel"))) return rc;
+        if ((rc = pdl_check(launch_pdl(x070_ln_out_kernel<A>, R, GLUE_T, 0, st, (const float*)x,
+                                       (const float*)lnow, (const float*)lnob, (A*)lnout, C), "x070_ln_out_kernel")))
+            return rc;
         mark("ln_out");
         GemvJobs Hd{};
         Hd.j[0] = qjob(head, lnout, C, ACT_NONE, OUT_F32, logits, V);
         if ((rc = gemv(0, Hd, 1, R, st))) return rc;
         mark("gemm_head");
-        x070_argmax_kernel<<<dim3((V + ARGMAX_SLICE - 1) / ARGMAX_SLICE, R), GLUE_T, 0, st>>>(logits, V, amax_keys);
-        if ((rc = check_launch("x070_argmax_kernel"))) return rc;
+        if ((rc = pdl_check(launch_pdl(x070_argmax_kernel, dim3((V + ARGMAX_SLICE - 1) / ARGMAX_SLICE, R), GLUE_T, 0,
+                                       st, (const float*)logits, V, amax_keys), "x070_argmax_kernel")))
+            return rc;
         mark("argmax");
-        x070_argmax_finish_kernel<<<(R + 127) / 128, 128, 0, st>>>(amax_keys, ids, R);
-        rc = check_launch("x070_argmax_finish_kernel");
+        rc = pdl_check(launch_pdl(x070_argmax_finish_kernel, (R + 127) / 128, 128, 0, st, amax_keys, ids, R),
+                       "x070_argmax_finish_kernel");
         mark("argmax_finish");
         return rc;
     }

@@ -68,6 +68,8 @@ x070_embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ 
                   const __half* __restrict__ emb_sc, const __half* __restrict__ emb_bi,
                   const __half* __restrict__ emb_dense, const float* __restrict__ lnw,
                   const float* __restrict__ lnb, float* __restrict__ x, int C, int vocab) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
     int id = ids[n];
@@ -103,6 +105,8 @@ __global__ void __launch_bounds__(GLUE_T)
 x070_tmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
                     const float* __restrict__ lnb, float* __restrict__ shift,
                     const float* __restrict__ coef, A* __restrict__ mix, int R, int C) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
     float v[GLUE_PER];
@@ -139,6 +143,8 @@ __global__ void __launch_bounds__(GLUE_T)
 x070_cmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
                     const float* __restrict__ lnb, float* __restrict__ shift,
                     const float* __restrict__ coef, A* __restrict__ out, int C) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
     float v[GLUE_PER];
@@ -170,6 +176,8 @@ template <typename A>
 __global__ void __launch_bounds__(GLUE_T)
 x070_ln_out_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
                    const float* __restrict__ lnb, A* __restrict__ out, int C) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
     float v[GLUE_PER];
@@ -207,6 +215,8 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
                 const float* __restrict__ lnxw, const float* __restrict__ lnxb,
                 const float* __restrict__ g, float* __restrict__ state, A* __restrict__ out,
                 int H, int layer0) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     constexpr int N = 64, RPW = 16;  // rows per warp
     __shared__ __align__(16) float r_s[N], w_s[N], kp_s[N], aw_s[N], bw_s[N], v_s[N], y_s[N];
     __shared__ __align__(16) float rk_s[N], lw_s[N], lb_s[N], g_s[N];
@@ -304,6 +314,8 @@ constexpr int ARGMAX_SLICE = 4096;
 
 __global__ void __launch_bounds__(GLUE_T)
 x070_argmax_kernel(const float* __restrict__ logits, int V, unsigned long long* __restrict__ keys) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     __shared__ unsigned long long sk[GLUE_T / 32];
     const int n = blockIdx.y;
     const int c0 = blockIdx.x * ARGMAX_SLICE;
@@ -335,6 +347,8 @@ x070_argmax_kernel(const float* __restrict__ logits, int V, unsigned long long* 
 // keys -> ids, and re-arm the keys for the next step.
 __global__ void x070_argmax_finish_kernel(unsigned long long* __restrict__ keys,
                                           int32_t* __restrict__ ids, int R) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     if (n >= R) return;
     ids[n] = (int32_t)(0xFFFFFFFFu - (unsigned)(keys[n] & 0xFFFFFFFFull));
@@ -346,6 +360,8 @@ __global__ void x070_argmax_finish_kernel(unsigned long long* __restrict__ keys,
 template <int FMT>
 __global__ void __launch_bounds__(256)
 gemv_cc_kernel(const GemvJobs jobs, int R) {
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     const GemvJob& jb = jobs.j[blockIdx.y];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int o = blockIdx.x * 8 + warp;
