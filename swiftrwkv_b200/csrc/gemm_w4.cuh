@@ -90,7 +90,9 @@ gemm_w4_kernel(const GemmArgs args, int max_groups) {
 
     const int nst = (ngr + GPS - 1) / GPS;  // stages of this CTA
     auto stage_ptr = [&](int s) { return smem + s * SM::STAGE; };
-    auto issue = [&](int si, int s) {  // groups g0 + GPS*si .. into stage s
+    // weights and activations of groups g0 + GPS*si .. into stage s; the
+    // weights do not depend on the previous kernel, the activations do
+    auto issue_w = [&](int si, int s) {
         unsigned char* st = stage_ptr(s);
         const int G0 = g0 + GPS * si;
         if (FMT == 0) {
@@ -112,7 +114,10 @@ gemm_w4_kernel(const GemmArgs args, int max_groups) {
                 cp_async16_cg(st + (r * SM::WROW + 8 * c) * 2, src, valid);
             }
         }
-        unsigned char* xs = st + SM::W_BYTES;
+    };
+    auto issue_x = [&](int si, int s) {
+        const int G0 = g0 + GPS * si;
+        unsigned char* xs = stage_ptr(s) + SM::W_BYTES;
         for (int e = tid; e < BN * 8 * GPS; e += GW_THREADS) {
             const int r = e / (8 * GPS), c = e % (8 * GPS);
             const int n = n0 + r;
@@ -129,11 +134,13 @@ gemm_w4_kernel(const GemmArgs args, int max_groups) {
 #pragma unroll
         for (int j = 0; j < WNT; j++) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
 
+    // first stages' weights, then (under programmatic launch) wait for the
+    // previous kernel before its activations: cp.async group s still holds
+    // stage s's activations, so the per-stage waits below are unchanged
+    if (tid == 0) pdl_trigger();
 #pragma unroll
-    for (int s = 0; s < STAGES - 1; s++) {
-        if (s < nst) issue(s, s);
-        cp_commit();
-    }
+    for (int s = 0; s < STAGES - 1; s++)
+        if (s < nst) issue_w(s, s);
     // scales / biases of this CTA's rows and groups -> shared, while the
     // first stages are in flight
     if (FMT == 0) {
@@ -145,12 +152,21 @@ gemm_w4_kernel(const GemmArgs args, int max_groups) {
             bi_s[r * max_groups + gg] = jb.biases[(int64_t)o * NGT + g0 + gg];
         }
     }
+    pdl_wait();
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; s++) {
+        if (s < nst) issue_x(s, s);
+        cp_commit();
+    }
 
 
     for (int si = 0; si < nst; si++) {
         cp_wait<STAGES - 2>();
         __syncthreads();
-        if (si + STAGES - 1 < nst) issue(si + STAGES - 1, (si + STAGES - 1) % STAGES);
+        if (si + STAGES - 1 < nst) {
+            issue_w(si + STAGES - 1, (si + STAGES - 1) % STAGES);
+            issue_x(si + STAGES - 1, (si + STAGES - 1) % STAGES);
+        }
         cp_commit();
         const unsigned char* st = stage_ptr(si % STAGES);
 #pragma unroll
@@ -360,7 +376,7 @@ inline GemmPlan plan_gemm(const GemvJobs& jobs, int njobs, int R, int sm_count) 
 }
 
 template <int FMT, int BN, int MW, int STAGES, int GPS>
-inline cudaError_t launch_gemm_t(const GemmArgs& a, const GemmPlan& p, cudaStream_t st) {
+inline cudaError_t launch_gemm_t(const GemmArgs& a, const GemmPlan& p, cudaStream_t st, bool pdl) {
     int maxg = 0;
     for (int i = 0; i < a.njobs; i++) maxg = std::max(maxg, (a.jobs.j[i].IN + 63) / 64);
     const int max_groups = (maxg + a.S - 1) / a.S + 1;
@@ -371,18 +387,20 @@ inline cudaError_t launch_gemm_t(const GemmArgs& a, const GemmPlan& p, cudaStrea
         if (e != cudaSuccess) return e;
     }
     dim3 grid(p.mblocks, a.njobs, p.nnb * a.S);
+    if (pdl) return launch_pdl(kern, grid, dim3(GW_THREADS), smem, st, a, max_groups);
     kern<<<grid, GW_THREADS, smem, st>>>(a, max_groups);
     return cudaGetLastError();
 }
 
 template <int FMT>
-inline cudaError_t launch_gemm(GemmArgs& a, const GemmPlan& p, cudaStream_t st) {
+// pdl: launch as a programmatic dependent of the previous kernel in the stream
+inline cudaError_t launch_gemm(GemmArgs& a, const GemmPlan& p, cudaStream_t st, bool pdl = false) {
     a.S = p.S;
     switch (p.BN) {
-        case 8: return launch_gemm_t<FMT, 8, 4, 3, FMT == 0 ? 4 : 1>(a, p, st);
-        case 16: return launch_gemm_t<FMT, 16, 4, 3, FMT == 0 ? 4 : 1>(a, p, st);
-        case 32: return launch_gemm_t<FMT, 32, 2, 4, FMT == 0 ? 2 : 1>(a, p, st);
-        default: return launch_gemm_t<FMT, 64, 1, 3, FMT == 0 ? 2 : 1>(a, p, st);
+        case 8: return launch_gemm_t<FMT, 8, 4, 3, FMT == 0 ? 4 : 1>(a, p, st, pdl);
+        case 16: return launch_gemm_t<FMT, 16, 4, 3, FMT == 0 ? 4 : 1>(a, p, st, pdl);
+        case 32: return launch_gemm_t<FMT, 32, 2, 4, FMT == 0 ? 2 : 1>(a, p, st, pdl);
+        default: return launch_gemm_t<FMT, 64, 1, 3, FMT == 0 ? 2 : 1>(a, p, st, pdl);
     }
 }
 

@@ -314,8 +314,9 @@ inline GemmPlan plan_any(const GemvJobs& jobs, int njobs, int R, int sm_count) {
 }
 
 template <int FMT>
-inline cudaError_t launch_any(GemmArgs& a, const GemmPlan& p, cudaStream_t st) {
-    return a.R <= 8 ? launch_gemm<FMT>(a, p, st) : launch_wide<FMT>(a, p, st);
+inline cudaError_t launch_any(GemmArgs& a, const GemmPlan& p, cudaStream_t st, bool pdl = false) {
+    // (the R <= 8 kernel supports programmatic launch; the wide kernel is launched plainly)
+    return a.R <= 8 ? launch_gemm<FMT>(a, p, st, pdl) : launch_wide<FMT>(a, p, st);
 }
 
 }  // namespace rwkv

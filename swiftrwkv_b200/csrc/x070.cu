@@ -386,7 +386,7 @@ struct X070 {
                 return fail(RWKV_E_WORKSPACE, "gemm: split-K plan exceeds the workspace");
             GemmArgs ga{};
             ga.jobs = jobs; ga.njobs = nj; ga.R = R; ga.ws = gws; ga.tickets = gtickets;
-            cudaError_t e = fmt == 0 ? launch_any<0>(ga, p, st) : launch_any<1>(ga, p, st);
+            cudaError_t e = fmt == 0 ? launch_any<0>(ga, p, st, true) : launch_any<1>(ga, p, st, true);
             return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm: %s", cudaGetErrorString(e));
         }
         int maxo = 0;
