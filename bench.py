@@ -49,6 +49,19 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
+def measured_traffic(wl):
+    """DRAM bytes (read + write) per launch of the dominant kernel, from the
+    ncu capture summarised in profiles/traffic.json for this workload and row
+    count; None when no capture covers it."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    e = d.get(wl.name, {}).get(str(getattr(wl, "rows", "")))
+    return None if e is None else e["dram_bytes_per_launch"]
+
+
 # ---------------------------------------------------------------- clock sampling
 
 class ClockSampler:
@@ -170,9 +183,13 @@ class WKV7Prefill:
 
 class GemvSuite:
     name = "gemv"
-    metric = "4-bit g64 GEMV GB/s (config 2, 1.5B projection shapes, rows 1, fp16 x)"
     unit = "GB/s"
     MATS = [(2048, 2048), (8192, 2048), (2048, 8192), (65536, 2048)]
+
+    def __init__(self, rows=1):
+        self.rows = rows
+        self.metric = (f"4-bit g64 GEMV GB/s (config 2, 1.5B projection shapes, rows {rows}, "
+                       "fp16 x)")
 
     def setup(self, torch, dev):
         from swiftrwkv_b200 import _lib
@@ -183,26 +200,36 @@ class GemvSuite:
         for OUT, IN in self.MATS:
             W = (torch.randn((OUT, IN), generator=g) * 0.02).half().to(dev)
             wq, sc, bi = Q.quantized(W)
-            x = torch.randn((1, IN), generator=g).half().to(dev)
-            y = torch.empty((1, OUT), device=dev, dtype=torch.float32)
+            x = torch.randn((self.rows, IN), generator=g).half().to(dev)
+            y = torch.empty((self.rows, OUT), device=dev, dtype=torch.float32)
             self.mats.append((OUT, IN, wq, sc, bi, x, y))
             del W
-        self.alg_bytes = sum(OUT * IN * 0.5 + OUT * IN // 64 * 4 + IN * 2 + OUT * 4
-                             for OUT, IN in self.MATS)
+        R = self.rows
+        mat_bytes = lambda OUT, IN: OUT * IN * 0.5 + OUT * IN // 64 * 4 + R * IN * 2 + R * OUT * 4
+        self.alg_bytes = sum(mat_bytes(OUT, IN) for OUT, IN in self.MATS)
         self.units_per_step = self.alg_bytes / 1e9
         self.launches_per_step = len(self.MATS)
-        self.kernel = "q_gemv_quad_kernel"
-        self.h2d = sum(IN * 2 for _, IN in self.MATS)
-        self.d2h = sum(OUT * 4 for OUT, _ in self.MATS)
-        self.pin_x = [torch.empty((1, IN), dtype=torch.float16).pin_memory() for _, IN in self.MATS]
-        self.pin_y = [torch.empty((1, OUT), dtype=torch.float32).pin_memory() for OUT, _ in self.MATS]
+        # the dominant launch: the 65536 x 2048 head matrix
+        self.dom_bytes = mat_bytes(*self.MATS[-1])
+        self.kernel = ("gemm_w4_kernel (mma.sync GEMV mode, exact per-group scaling), 65536x2048"
+                       if R <= 8 else "gemm_tc_kernel (tcgen05, TMA + TMEM), 65536x2048")
+        self.h2d = sum(R * IN * 2 for _, IN in self.MATS)
+        self.d2h = sum(R * OUT * 4 for OUT, _ in self.MATS)
+        self.pin_x = [torch.empty((R, IN), dtype=torch.float16).pin_memory() for _, IN in self.MATS]
+        self.pin_y = [torch.empty((R, OUT), dtype=torch.float32).pin_memory() for OUT, _ in self.MATS]
 
-    def step(self):
+    def _gemm(self, OUT, IN, wq, sc, bi, x, y):
         _lib, P = self._lib, self._lib.P
         st = P(self.torch.cuda.current_stream().cuda_stream)
-        for OUT, IN, wq, sc, bi, x, y in self.mats:
-            _lib.call("rwkv_q_gemm", 2, P(x.data_ptr()), P(wq.data_ptr()), P(sc.data_ptr()),
-                      P(bi.data_ptr()), 2, 0, P(y.data_ptr()), 1, OUT, IN, 64, 4, st)
+        _lib.call("rwkv_q_gemm", 2, P(x.data_ptr()), P(wq.data_ptr()), P(sc.data_ptr()),
+                  P(bi.data_ptr()), 2, 0, P(y.data_ptr()), self.rows, OUT, IN, 64, 4, st)
+
+    def step(self):
+        for m in self.mats:
+            self._gemm(*m)
+
+    def dominant(self):
+        self._gemm(*self.mats[-1])
 
     def step_e2e(self):
         for (OUT, IN, wq, sc, bi, x, y), px, py in zip(self.mats, self.pin_x, self.pin_y):
@@ -225,7 +252,7 @@ class GemvSuite:
             n += 1
         dt = time.perf_counter() - t0
         by = OUT * IN * 0.5 + OUT * IN // 64 * 4
-        return n * by / dt / 1e9, f"{n} GEMVs of 2048x2048 4-bit g64"
+        return n * by / dt / 1e9, f"{n} GEMVs of 2048x2048 4-bit g64, 1 row"
 
 
 class Decode15B:
@@ -258,7 +285,8 @@ class Decode15B:
         self.alg_bytes = self.m.weight_bytes + self.state_bytes + shift_bytes
         self.units_per_step = self.rows
         self.launches_per_step = self.m.launches_per_step
-        self.kernel = "decode step (CUDA graph)"
+        self.kernel = ("wkv7_step_kernel<float,1> via rwkv_wkv7_step_tail (the step's WKV+tail over "
+                       "one layer's rows x heads)")
         self.pin_ids = torch.zeros(self.rows, dtype=torch.int32).pin_memory()
         self.pin_out = torch.zeros(self.rows, dtype=torch.int32).pin_memory()
         self.dev_ids = torch.zeros(self.rows, dtype=torch.int32, device=dev)
@@ -425,7 +453,9 @@ def run_reference(args, rank):
 
 def make_workload(args):
     if args.workload == "decode":
-        return Decode15B(args.rows, args.prompt)
+        return Decode15B(args.rows or 64, args.prompt)
+    if args.workload == "gemv":
+        return GemvSuite(args.rows or 1)
     return WORKLOADS[args.workload]()
 
 
@@ -435,7 +465,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
-    ap.add_argument("--rows", type=int, default=64, help="decode rows per GPU")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="decode rows per GPU (default 64) / GEMV activation rows (default 1)")
     ap.add_argument("--prompt", type=int, default=128, help="decode prompt tokens per row")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -486,7 +517,7 @@ def main():
         dt = timed(torch, wl.dominant, args.steps, args.warmup, flush_l2, False)
         dom_ms = sum(dt) / len(dt)
         achieved = wl.dom_bytes / (dom_ms / 1e3) / 1e9
-        kernel = "x070_wkv/wkv7_step_tail (one layer, all rows x heads)"
+        kernel = wl.kernel
     else:
         dom_ms = local_ms / wl.launches_per_step
         achieved = wl.alg_bytes / wl.launches_per_step / (dom_ms / 1e3) / 1e9
@@ -498,7 +529,8 @@ def main():
         "dtype": "f32" if wl.name == "wkv7" else "u4 x f16 -> f32", "data": "synthetic",
         "config": {"workload": wl.name, "l2": l2_note, "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": measured_traffic(wl),
                      "peak_src": peaks["src"], "kernel": kernel, "kernel_ms": dom_ms},
         "step_roofline": {"alg_bytes": wl.alg_bytes, "achieved": step_gbs,
                           "frac": step_gbs / peaks["hbm_gbs"], "unit": "GB/s"},
