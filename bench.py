@@ -135,7 +135,8 @@ def config1_inputs(rng, B=1, T=1024, H=12, N=64):
 
 class WKV7Prefill:
     name = "wkv7"
-    metric = "WKV-7 prefill tok/s (config 1 operator forward, B=1 T=1024 H=12 N=64 fp32)"
+    metric = ("WKV-7 prefill tok/s (config 1 operator forward, B=1 T=1024 H=12 N=64 fp32, "
+              "chunked DPLR form)")
     unit = "tok/s"
     B, T, H, N = 1, 1024, 12, 64
 
@@ -150,19 +151,24 @@ class WKV7Prefill:
         self.pin = [torch.from_numpy(a).pin_memory() for a in self.host]
         self.pin_y = torch.empty(self.y.shape, dtype=torch.float32).pin_memory()
         self.units_per_step = self.B * self.T
-        self.launches_per_step = 1
+        # chunked form: prep (chunk transitions), scan, out
+        self.launches_per_step = 3
+        ws_bytes = int(_lib.lib().rwkv_wkv7_forward_chunked_workspace_size(self.B, self.T, self.H, self.N))
+        self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        self.ws_bytes = ws_bytes
         # algorithmic bytes: 6 inputs + y (fp32) + h_out (h_in = 0 is not read)
         BTHN = self.B * self.T * self.H * self.N
         self.alg_bytes = 4 * (7 * BTHN + self.B * self.H * self.N * self.N)
-        self.kernel = "wkv7_seq_fwd_kernel"
+        self.kernel = "wkv7_chunk_{prep,scan,out} (per launch: the three-kernel step / 3)"
         self.h2d = sum(a.nbytes for a in self.host)
         self.d2h = self.y.numel() * 4
 
     def step(self):
         _lib, P = self._lib, self._lib.P
         st = P(self.torch.cuda.current_stream().cuda_stream)
-        _lib.call("rwkv_wkv7_forward", 0, *(P(t.data_ptr()) for t in self.x), None,
-                  P(self.y.data_ptr()), P(self.h.data_ptr()), self.B, self.T, self.H, self.N, st)
+        _lib.call("rwkv_wkv7_forward_chunked", 0, *(P(t.data_ptr()) for t in self.x), None,
+                  P(self.y.data_ptr()), P(self.h.data_ptr()), None, self.B, self.T, self.H, self.N,
+                  P(self.ws.data_ptr()), self.ws_bytes, st)
 
     def step_e2e(self):
         for d, p in zip(self.x, self.pin):

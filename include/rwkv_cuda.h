@@ -68,6 +68,25 @@ int rwkv_wkv7_forward(int dtype, const void* r, const void* w, const void* k, co
                       const void* a, const void* b, const float* h_in, void* y, float* h_out,
                       int B, int T, int H, int N, rwkv_stream_t stream);
 
+/* Prefill form of rwkv_wkv7_forward, chunked (same arguments and results to
+ * fp32 rounding, ~1e-6 relative).  16-token chunks in the normalised DPLR
+ * form: each chunk's transition S -> S A_c + B_c is built in parallel over
+ * chunks, a scan applies them (one 16x64x64 tensor-core product per chunk
+ * and head), and each chunk's outputs come from its start state -- so the
+ * T-sequential depth drops sixteen-fold.  Unlike rwkv_wkv7_forward it does not
+ * promise the bitwise identities of the sequential form (step = forward at
+ * T=1, split = contiguous).  h_in / h_out as in rwkv_wkv7_forward; sa
+ * [B,T,H,N] fp32 (may be NULL) receives S_{t-1} a_t as the training forward
+ * does.  `workspace`: rwkv_wkv7_forward_chunked_workspace_size bytes of device
+ * memory (3 states per chunk and head).  Replaces wkv7SequenceForward /
+ * wkv7ForwardWithState on the prefill path (Sources/RWKVKernel/WKV7.swift:
+ * 96-148, :242-264). */
+int64_t rwkv_wkv7_forward_chunked_workspace_size(int B, int T, int H, int N);
+int rwkv_wkv7_forward_chunked(int dtype, const void* r, const void* w, const void* k,
+                              const void* v, const void* a, const void* b, const float* h_in,
+                              void* y, float* h_out, float* sa, int B, int T, int H, int N,
+                              void* workspace, int64_t workspace_bytes, rwkv_stream_t stream);
+
 /* Differentiable forward of the training path: as rwkv_wkv7_forward, plus
  * sa [B,T,H,N] fp32 (may be NULL) and h_ckpt [B, H, T/16, N, N] fp32, the state
  * after every 16 steps (the last one equals h_out).  T % 16 == 0.

@@ -24,6 +24,10 @@ int launch_wkv7_step_tail(const float*, const float*, const float*, const float*
 int launch_wkv_tail(const float*, const float*, const float*, const float*, const float*,
                     const float*, const float*, const float*, float*, int, int, int, float,
                     cudaStream_t);
+int launch_wkv7_chunk_fwd(int, const void*, const void*, const void*, const void*, const void*,
+                          const void*, const float*, void*, float*, float*, int, int, int, void*,
+                          cudaStream_t);
+int64_t wkv7_chunk_workspace(int, int, int);
 int64_t wkv7_bwd_seq_workspace(int, int);
 int launch_wkv7_bwd_seq(int, const void*, const void*, const void*, const void*, const void*,
                         const void*, const float*, const float*, const void*, const float*, void*,
@@ -108,6 +112,27 @@ int rwkv_wkv7_forward(int dtype, const void* r, const void* w, const void* k, co
     RWKV_REQUIRE(al16(h_in) && al16(h_out), RWKV_E_UNSUPPORTED, "rwkv_wkv7_forward: state not 16-byte aligned");
     return launch_wkv7_seq(dtype, r, w, k, v, a, b, h_in, y, h_out, nullptr, nullptr, B, T, H,
                            (cudaStream_t)stream);
+}
+
+int64_t rwkv_wkv7_forward_chunked_workspace_size(int B, int T, int H, int N) {
+    (void)N;
+    if (B < 1 || T < 1 || H < 1) return 0;
+    return wkv7_chunk_workspace(B, T, H);
+}
+
+int rwkv_wkv7_forward_chunked(int dtype, const void* r, const void* w, const void* k, const void* v,
+                              const void* a, const void* b, const float* h_in, void* y, float* h_out,
+                              float* sa, int B, int T, int H, int N, void* workspace,
+                              int64_t workspace_bytes, rwkv_stream_t stream) {
+    const void* req[] = {r, w, k, v, a, b, y};
+    if (int rc = check_wkv_common(dtype, req, 7, B, T, H, N, "rwkv_wkv7_forward_chunked")) return rc;
+    const int64_t need = wkv7_chunk_workspace(B, T, H);
+    RWKV_REQUIRE(workspace != nullptr && workspace_bytes >= need, RWKV_E_WORKSPACE,
+                 "rwkv_wkv7_forward_chunked: workspace %lld bytes, need %lld",
+                 (long long)workspace_bytes, (long long)need);
+    RWKV_REQUIRE(al16(workspace), RWKV_E_UNSUPPORTED, "rwkv_wkv7_forward_chunked: workspace not 16-byte aligned");
+    return launch_wkv7_chunk_fwd(dtype, r, w, k, v, a, b, h_in, y, h_out, sa, B, T, H, workspace,
+                                 (cudaStream_t)stream);
 }
 
 int rwkv_wkv7_train_forward(int dtype, const void* r, const void* w, const void* k,

@@ -22,7 +22,7 @@ WKV7_CHUNK = 16      # WKV7.swift:8
 
 # Launch counters, as the reference keeps them for tests (WKV7.swift:181,
 # WKV7Train.swift:358, X070Backbone.swift:435).
-counters = {"wkv7SequenceLaunches": 0, "wkv7TrainForwardLaunches": 0,
+counters = {"wkv7SequenceLaunches": 0, "wkv7ChunkedLaunches": 0, "wkv7TrainForwardLaunches": 0,
             "wkv7BackwardLaunches": 0, "stepKernelCalls": 0, "tailKernelCalls": 0}
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
@@ -95,6 +95,24 @@ def wkv7ForwardChunked(r, w, k, v, a, b, hIn=None):
     """WKV7.swift:107-140: chunked by 16 in the reference; one launch here,
     bit-identical to wkv7SequenceForward as the reference requires."""
     return wkv7SequenceForward(r, w, k, v, a, b, hIn)
+
+
+def wkv7PrefillChunked(r, w, k, v, a, b, hIn=None):
+    """Prefill form of wkv7SequenceForward: 16-token chunks in the normalised
+    DPLR form (rwkv_wkv7_forward_chunked); equal to it to fp32 rounding, not
+    bitwise.  Returns (out [B,T,H,D], hOut [B,H,D,D] fp32)."""
+    B, T, H, D = _check_seq(r, "wkv7PrefillChunked")
+    dt = _common_dtype((r, w, k, v, a, b))
+    r, w, k, v, a, b = _prep((r, w, k, v, a, b), dt)
+    h = _state(hIn, (B, H, D, D))
+    out = torch.empty_like(r)
+    h_out = torch.empty((B, H, D, D), device=r.device, dtype=torch.float32)
+    ws_bytes = int(_lib.lib().rwkv_wkv7_forward_chunked_workspace_size(B, T, H, D))
+    ws = torch.empty(max(ws_bytes, 16), device=r.device, dtype=torch.uint8)
+    call("rwkv_wkv7_forward_chunked", _DT[dt], *map(_ptr, (r, w, k, v, a, b, h, out, h_out)), None,
+         B, T, H, D, _ptr(ws), ws_bytes, _stream())
+    counters["wkv7ChunkedLaunches"] += 1
+    return out, h_out
 
 
 def wkv7Forward(r, w, k, v, a, b):
