@@ -373,6 +373,15 @@ struct X070 {
         return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "%s: %s", name, cudaGetErrorString(e));
     }
 
+    // row kernels: GV = 16-byte column groups per thread, C <= 1024 GV
+    template <typename F>
+    int row_launch(F&& f, const char* name) const {
+        const int gv = (C + 4 * GLUE_T - 1) / (4 * GLUE_T);
+        cudaError_t e = gv <= 1 ? f.template operator()<1>() : gv == 2 ? f.template operator()<2>()
+                      : gv == 3 ? f.template operator()<3>() : f.template operator()<4>();
+        return pdl_check(e, name);
+    }
+
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
         if (f16act) {
             const int tfmt = fmt == 0 ? TC_Q4 : TC_F16;
@@ -429,9 +438,11 @@ struct X070 {
             float* ts = tshift + (size_t)l * Rmax * C;
             float* cs = cshift + (size_t)l * Rmax * C;
             float* st8 = wkv + (size_t)l * Rmax * H * 64 * 64;
-            if ((rc = pdl_check(launch_pdl(x070_tmix_in_kernel<A>, R, GLUE_T, 0, st, (const float*)x,
-                                           (const float*)w.ln1w, (const float*)w.ln1b, ts,
-                                           (const float*)w.coef6, mixp, R, C), "x070_tmix_in_kernel")))
+            if ((rc = row_launch([&]<int GV>() {
+                     return launch_pdl(x070_tmix_in_kernel<A, GV>, R, GLUE_T, 0, st, (const float*)x,
+                                       (const float*)w.ln1w, (const float*)w.ln1b, ts,
+                                       (const float*)w.coef6, mixp, R, C);
+                 }, "x070_tmix_in_kernel")))
                 return rc;
             mark("tmix_in");
             auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
@@ -470,9 +481,11 @@ struct X070 {
             O.j[0] = qjob(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C);
             if ((rc = gemv(0, O, 1, R, st))) return rc;
             mark("gemm_o");
-            if ((rc = pdl_check(launch_pdl(x070_cmix_in_kernel<A>, R, GLUE_T, 0, st, (const float*)x,
-                                           (const float*)w.ln2w, (const float*)w.ln2b, cs,
-                                           (const float*)w.cxk, (A*)xk, C), "x070_cmix_in_kernel")))
+            if ((rc = row_launch([&]<int GV>() {
+                     return launch_pdl(x070_cmix_in_kernel<A, GV>, R, GLUE_T, 0, st, (const float*)x,
+                                       (const float*)w.ln2w, (const float*)w.ln2b, cs,
+                                       (const float*)w.cxk, (A*)xk, C);
+                 }, "x070_cmix_in_kernel")))
                 return rc;
             mark("cmix_in");
             GemvJobs K{};
@@ -484,8 +497,10 @@ struct X070 {
             if ((rc = gemv(0, Vv, 1, R, st))) return rc;
             mark("gemm_value");
         }
-        if ((rc = pdl_check(launch_pdl(x070_ln_out_kernel<A>, R, GLUE_T, 0, st, (const float*)x,
-                                       (const float*)lnow, (const float*)lnob, (A*)lnout, C), "x070_ln_out_kernel")))
+        if ((rc = row_launch([&]<int GV>() {
+                 return launch_pdl(x070_ln_out_kernel<A, GV>, R, GLUE_T, 0, st, (const float*)x,
+                                   (const float*)lnow, (const float*)lnob, (A*)lnout, C);
+             }, "x070_ln_out_kernel")))
             return rc;
         mark("ln_out");
         GemvJobs Hd{};

@@ -98,99 +98,131 @@ x070_embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ 
     }
 }
 
+// Row kernels over C channels with 16-byte accesses: thread t holds columns
+// 4(t + 256 i) .. +3 for i < GV (C % 4 == 0, C <= 1024 GV).
+template <int GV>
+__device__ __forceinline__ void ld_row4(float4* d, const float* __restrict__ p, int C) {
+#pragma unroll
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
+        d[i] = c < C ? *reinterpret_cast<const float4*>(p + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// Two-pass LayerNorm (eps 1e-5) of the row in v[], in place.
+template <int GV>
+__device__ __forceinline__ void ln_row4(float4* v, const float4* w, const float4* b, int C, float* sh) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < GV; i++)
+        if (4 * (threadIdx.x + GLUE_T * i) < C) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = block_sum256(s, sh) / (float)C;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < GV; i++)
+        if (4 * (threadIdx.x + GLUE_T * i) < C) {
+            const float dx = v[i].x - mean, dy = v[i].y - mean, dz = v[i].z - mean, dw = v[i].w - mean;
+            q += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+        }
+    const float den = sqrtf(block_sum256(q, sh) / (float)C + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < GV; i++) {
+        v[i].x = (v[i].x - mean) / den * w[i].x + b[i].x;
+        v[i].y = (v[i].y - mean) / den * w[i].y + b[i].y;
+        v[i].z = (v[i].z - mean) / den * w[i].z + b[i].z;
+        v[i].w = (v[i].w - mean) / den * w[i].w + b[i].w;
+    }
+}
+
+template <typename A>
+__device__ __forceinline__ void st_act4(A* p, float4 v) {
+    p[0] = from_f<A>(v.x); p[1] = from_f<A>(v.y); p[2] = from_f<A>(v.z); p[3] = from_f<A>(v.w);
+}
+__device__ __forceinline__ float4 lerp4(float4 xl, float4 xx, float4 c) {
+    return make_float4(xl.x + xx.x * c.x, xl.y + xx.y * c.y, xl.z + xx.z * c.z, xl.w + xx.w * c.w);
+}
+__device__ __forceinline__ float4 sub4(float4 a, float4 b) {
+    return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+}
+
 // tmix input: xl = ln1(x); xx = shift - xl; shift = xl;
 // mix[m] = xl + xx * coef[m] for m = r, w, k, v, a, g  ([6][R][C], act type).
-template <typename A>
+// The weights (never written during a step) are loaded before the
+// programmatic-launch wait; x and the shift row after it, in one round trip.
+template <typename A, int GV>
 __global__ void __launch_bounds__(GLUE_T)
 x070_tmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
                     const float* __restrict__ lnb, float* __restrict__ shift,
                     const float* __restrict__ coef, A* __restrict__ mix, int R, int C) {
-    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
-    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
-    float v[GLUE_PER];
+    float4 sv[GV], cf[6][GV], w4[GV], b4[GV], v[GV];
 #pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
-        v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
-    }
-    // all loads of the row before any store
-    float sv[GLUE_PER], cf[6][GLUE_PER];
+    for (int m = 0; m < 6; m++) ld_row4<GV>(cf[m], coef + m * C, C);
+    ld_row4<GV>(w4, lnw, C);
+    ld_row4<GV>(b4, lnb, C);
+    pdl_wait();  // x: the previous kernel's output
+    pdl_trigger();
+    ld_row4<GV>(v, x + (int64_t)n * C, C);
+    ld_row4<GV>(sv, shift + (int64_t)n * C, C);
+    ln_row4<GV>(v, w4, b4, C, sh);
 #pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
-        sv[i] = (c < C) ? shift[(int64_t)n * C + c] : 0.f;
-#pragma unroll
-        for (int m = 0; m < 6; m++) cf[m][i] = (c < C) ? coef[m * C + c] : 0.f;
-    }
-    ln_regs(v, C, lnw, lnb, sh);
-#pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
         if (c >= C) continue;
         const int64_t o = (int64_t)n * C + c;
-        const float xx = sv[i] - v[i];
-        shift[o] = v[i];
+        const float4 xx = sub4(sv[i], v[i]);
+        *reinterpret_cast<float4*>(shift + o) = v[i];
 #pragma unroll
-        for (int m = 0; m < 6; m++) st_act(mix + (int64_t)m * R * C + o, v[i] + xx * cf[m][i]);
+        for (int m = 0; m < 6; m++) st_act4(mix + (int64_t)m * R * C + o, lerp4(v[i], xx, cf[m][i]));
     }
 }
 
 // cmix input: xl = ln2(x); xx = shift - xl; shift = xl; out = xl + xx * coef.
-template <typename A>
+template <typename A, int GV>
 __global__ void __launch_bounds__(GLUE_T)
 x070_cmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
                     const float* __restrict__ lnb, float* __restrict__ shift,
                     const float* __restrict__ coef, A* __restrict__ out, int C) {
-    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
-    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
-    float v[GLUE_PER];
+    float4 sv[GV], cf[GV], w4[GV], b4[GV], v[GV];
+    ld_row4<GV>(cf, coef, C);
+    ld_row4<GV>(w4, lnw, C);
+    ld_row4<GV>(b4, lnb, C);
+    pdl_wait();  // x and the shift row: written by earlier kernels of the step
+    pdl_trigger();
+    ld_row4<GV>(v, x + (int64_t)n * C, C);
+    ld_row4<GV>(sv, shift + (int64_t)n * C, C);
+    ln_row4<GV>(v, w4, b4, C, sh);
 #pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
-        v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
-    }
-    float sv[GLUE_PER], cf[GLUE_PER];
-#pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
-        sv[i] = (c < C) ? shift[(int64_t)n * C + c] : 0.f;
-        cf[i] = (c < C) ? coef[c] : 0.f;
-    }
-    ln_regs(v, C, lnw, lnb, sh);
-#pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
         if (c >= C) continue;
         const int64_t o = (int64_t)n * C + c;
-        const float xx = sv[i] - v[i];
-        shift[o] = v[i];
-        st_act(out + o, v[i] + xx * cf[i]);
+        const float4 xx = sub4(sv[i], v[i]);
+        *reinterpret_cast<float4*>(shift + o) = v[i];
+        st_act4(out + o, lerp4(v[i], xx, cf[i]));
     }
 }
 
-template <typename A>
+template <typename A, int GV>
 __global__ void __launch_bounds__(GLUE_T)
 x070_ln_out_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
                    const float* __restrict__ lnb, A* __restrict__ out, int C) {
-    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
-    pdl_trigger();
     __shared__ float sh[33];
     const int n = blockIdx.x;
-    float v[GLUE_PER];
+    float4 w4[GV], b4[GV], v[GV];
+    ld_row4<GV>(w4, lnw, C);
+    ld_row4<GV>(b4, lnb, C);
+    pdl_wait();  // x: the previous kernel's output
+    pdl_trigger();
+    ld_row4<GV>(v, x + (int64_t)n * C, C);
+    ln_row4<GV>(v, w4, b4, C, sh);
 #pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
-        v[i] = (c < C) ? x[(int64_t)n * C + c] : 0.f;
-    }
-    ln_regs(v, C, lnw, lnb, sh);
-#pragma unroll
-    for (int i = 0; i < GLUE_PER; i++) {
-        const int c = threadIdx.x + GLUE_T * i;
-        if (c < C) st_act(out + (int64_t)n * C + c, v[i]);
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
+        if (c < C) st_act4(out + (int64_t)n * C + c, v[i]);
     }
 }
 
