@@ -17,13 +17,12 @@
 //
 // Three launches:
 //   prep  (chunk, head) in parallel: the chunk transition (A_c, B_c)
-//   scan  per head, sequential over chunks: S_{c+1} = S_c A_c + B_c; stores
-//         every chunk's start state
-//   out   (chunk, head, 16 state rows) in parallel: U and Y from the chunk's
-//         start state
-// so the T-sequential depth is one 16 x 64 x 64 product per chunk.  Products
-// run on the tensor cores in 3xTF32 (x = hi + lo, hi*hi + hi*lo + lo*hi: about
-// fp32 accuracy).  Every factor is bounded except 1/c_t: a chunk whose
+//   scan  (head, 8 state rows), sequential over chunks: S_{c+1} = S_c A_c + B_c
+//         in fp32 FMAs; stores every chunk's start state
+//   out   (chunk, head) in parallel: U and Y from the chunk's start state
+// so the T-sequential depth is one 8 x 64 x 64 product per chunk.  The
+// products of prep and out run on the tensor cores in 3xTF32 (x = hi + lo,
+// hi*hi + hi*lo + lo*hi: about fp32 accuracy).  Every factor is bounded except 1/c_t: a chunk whose
 // smallest c_16 is below 1e-30 (decays near zero) takes the sequential update
 // token by token instead (prep builds A_c, B_c by stepping; out steps the
 // state), so no division overflows.  A partial last chunk is padded with
@@ -40,7 +39,6 @@ namespace {
 
 constexpr int CN = 64;      // head size
 constexpr int CL = 16;      // chunk length
-constexpr int CR = 16;      // state rows per CTA (scan / out)
 constexpr int CT = 256;     // threads
 // Row strides (floats) chosen for the m16n8k8 fragment patterns: a row-read
 // operand X[g][k + t] (g = lane/4, t = lane%4) is conflict free when the
@@ -50,6 +48,13 @@ constexpr int CP = CN + 4;   // 68
 constexpr int CQ = CN + 8;   // 72
 constexpr int LP = CL + 4;   // 20
 constexpr float GUARD = 1e-30f;
+
+// A_c in the order the scan loads it: float4 number (k / 2) * 32 + l (k even)
+// holds A[k][2l], A[k][2l+1], A[k+1][2l], A[k+1][2l+1]; warp w of the scan
+// reads float4s 8w * 32 .. (8w + 8) * 32 - 1 (k = 16w .. 16w + 15).
+__device__ __forceinline__ int scan_a_index(int k, int c) {
+    return (((k >> 1) * 32 + (c >> 1)) << 2) + ((k & 1) << 1) + (c & 1);
+}
 
 // ------------------------------------------------------------ tensor cores
 
@@ -273,7 +278,7 @@ wkv7_chunk_prep_kernel(const T* __restrict__ w, const T* __restrict__ k, const T
             __syncthreads();
         }
         for (int e = tid; e < CN * CN; e += CT) {
-            Ag[e] = sm.SA[e / CN][e % CN];
+            Ag[scan_a_index(e / CN, e % CN)] = sm.SA[e / CN][e % CN];
             Bg[e] = sm.SB[e / CN][e % CN];
         }
         return;
@@ -371,91 +376,100 @@ wkv7_chunk_prep_kernel(const T* __restrict__ w, const T* __restrict__ k, const T
             }
             mma3(d, af, bf);
         }
-        float* dst = isA ? Ag : Bg;
 #pragma unroll
-        for (int q = 0; q < 4; q++) dst[frag_i(m0, lane, q) * CN + frag_j(n0, lane, q)] = d[q];
+        for (int q = 0; q < 4; q++) {
+            const int i = frag_i(m0, lane, q), j = frag_j(n0, lane, q);
+            if (isA) Ag[scan_a_index(i, j)] = d[q];
+            else Bg[i * CN + j] = d[q];
+        }
     }
 }
 
 // ------------------------------------------------------------ scan
 
-constexpr int SCAN_RING = 4;  // chunks of A_c / B_c in flight (L2 latency > one chunk's work)
+// The scan is a chain of small products (8 rows x 64 x 64 per CTA and chunk):
+// too small for the tensor cores to pay (3xTF32 on mma.sync needs three
+// products and the legacy tensor path is slow on sm_100), so it runs in plain
+// fp32 FMAs.  CTA = (head, 8 state rows), 4 warps; warp w takes K = 16w ..
+// 16w + 15 for all 8 rows, lane l columns 2l and 2l + 1, and the four partial
+// products are summed with B_c in shared memory.  A_c and B_c come straight
+// from L2 into registers, three chunks ahead.
+constexpr int SR = 8;     // state rows per scan CTA
+constexpr int ST = 128;   // scan threads
 
-struct ScanSmem {
-    float S[2][CR][CP];              // ping-pong state rows (row-read A operand)
-    float Am[SCAN_RING][CN][CQ];     // A_c ring (column-read B operand)
-    float Bs[SCAN_RING][CR][CP];     // this CTA's B_c rows
-};
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src) : "memory");
-}
-
-__global__ void __launch_bounds__(CT)
+__global__ void __launch_bounds__(ST)
 wkv7_chunk_scan_kernel(const float* __restrict__ h_in, const float* __restrict__ Aws,
                        const float* __restrict__ Bws, float* __restrict__ S0ws,
                        float* __restrict__ h_out, int NC) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    ScanSmem& sm = *reinterpret_cast<ScanSmem*>(smem_raw);
-    const int bh = blockIdx.x, dv0 = blockIdx.y * CR;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
-    for (int e = tid; e < CR * CN; e += CT) {
-        const int rr = e / CN, cc = e % CN;
-        sm.S[0][rr][cc] = h_in ? h_in[((size_t)bh * CN + dv0 + rr) * CN + cc] : 0.f;
+    __shared__ __align__(16) float S[SR][CN];      // state rows (broadcast reads)
+    __shared__ __align__(16) float P[4][SR][CN];   // per-warp partial products
+    const int bh = blockIdx.x, dv0 = blockIdx.y * SR;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rr = tid >> 4, c4 = (tid & 15) * 4;   // this thread's 4 state entries
+    constexpr int CH4 = CN * CN / 4;                // float4 per chunk matrix
+    {
+        const float4 s = h_in ? *reinterpret_cast<const float4*>(h_in + ((size_t)bh * CN + dv0 + rr) * CN + c4)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(&S[rr][c4]) = s;
+        *reinterpret_cast<float4*>(S0ws + (size_t)bh * NC * CN * CN + (size_t)(dv0 + rr) * CN + c4) = s;
     }
-    // chunk ch's A_c (1024 16-byte pieces, 4 per thread) and B_c rows (1 per
-    // thread) into ring slot ch % SCAN_RING; one commit group per call, empty
-    // past the last chunk so that the group count stays exact
-    auto issue = [&](int ch) {
+    const float4* Ab = reinterpret_cast<const float4*>(Aws + (size_t)bh * NC * CN * CN) + warp * 8 * 32 + lane;
+    const float4* Bb = reinterpret_cast<const float4*>(Bws + (size_t)bh * NC * CN * CN + (size_t)(dv0 + rr) * CN + c4);
+    float4 a0[8], a1[8], a2[8], b0, b1, b2;
+    auto load = [&](float4 (&av)[8], float4& bv, int ch) {
         if (ch < NC) {
-            const float* Ag = Aws + ((size_t)bh * NC + ch) * CN * CN;
-            const float* Bg = Bws + ((size_t)bh * NC + ch) * CN * CN + (size_t)dv0 * CN;
-            const int buf = ch % SCAN_RING;
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int p = tid + CT * i, rr = p >> 4, c4 = (p & 15) * 4;
-                cp_async16(&sm.Am[buf][rr][c4], Ag + rr * CN + c4);
-            }
-            cp_async16(&sm.Bs[buf][tid >> 4][(tid & 15) * 4], Bg + (tid >> 4) * CN + (tid & 15) * 4);
+            for (int i = 0; i < 8; i++) av[i] = __ldcg(Ab + (size_t)ch * CH4 + i * 32);
+            bv = __ldcg(Bb + (size_t)ch * CH4);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
     };
-#pragma unroll
-    for (int i = 0; i < SCAN_RING - 1; i++) issue(i);
-    const int n0 = 8 * warp;
-    for (int ch = 0; ch < NC; ch++) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(SCAN_RING - 2) : "memory");
-        __syncthreads();  // chunk ch's operands and the previous state are visible
-        issue(ch + SCAN_RING - 1);  // into the slot chunk ch-1 used
-        const int slot = ch % SCAN_RING, cur = ch & 1;
-        // this chunk's start state out (the out kernel's input)
-        {
-            const int rr = tid >> 4, c4 = (tid & 15) * 4;
-            float4 t4v = make_float4(sm.S[cur][rr][c4], sm.S[cur][rr][c4 + 1], sm.S[cur][rr][c4 + 2],
-                                     sm.S[cur][rr][c4 + 3]);
-            *reinterpret_cast<float4*>(S0ws + ((size_t)bh * NC + ch) * CN * CN + (size_t)(dv0 + rr) * CN + c4) = t4v;
-        }
-        float d[4], d3[3][4] = {};
-#pragma unroll
-        for (int q = 0; q < 4; q++) d[q] = sm.Bs[slot][frag_i(0, lane, q)][frag_j(n0, lane, q)];
-#pragma unroll
-        for (int k0 = 0; k0 < CN; k0 += 8) {
-            const float af[4] = {sm.S[cur][g][k0 + t4], sm.S[cur][g + 8][k0 + t4], sm.S[cur][g][k0 + t4 + 4],
-                                 sm.S[cur][g + 8][k0 + t4 + 4]};
-            const float bf[2] = {sm.Am[slot][k0 + t4][n0 + g], sm.Am[slot][k0 + t4 + 4][n0 + g]};
-            mma3x(d3, af, bf);
-        }
-        acc3_sum(d, d3);
-#pragma unroll
-        for (int q = 0; q < 4; q++) sm.S[cur ^ 1][frag_i(0, lane, q)][frag_j(n0, lane, q)] = d[q];
-    }
+    load(a0, b0, 0);
+    load(a1, b1, 1);
+    load(a2, b2, 2);
     __syncthreads();
-    if (h_out)
-        for (int e = tid; e < CR * CN; e += CT) {
-            const int rr = e / CN, cc = e % CN;
-            h_out[((size_t)bh * CN + dv0 + rr) * CN + cc] = sm.S[NC & 1][rr][cc];
+    auto chunk = [&](float4 (&av)[8], float4& bv, int ch) {
+        // columns 2l (acc0) and 2l + 1 (acc1) of the 8 rows; the FMAs are
+        // ordered so that the 16 accumulators' chains interleave
+        float acc0[SR], acc1[SR];
+#pragma unroll
+        for (int r = 0; r < SR; r++) acc0[r] = acc1[r] = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            float4 sv[SR];
+#pragma unroll
+            for (int r = 0; r < SR; r++) sv[r] = *reinterpret_cast<const float4*>(&S[r][16 * warp + 4 * q]);
+            const float4 lo = av[2 * q], hi = av[2 * q + 1];   // k = 16w + 4q .. +3
+#pragma unroll
+            for (int r = 0; r < SR; r++) { acc0[r] = fmaf(sv[r].x, lo.x, acc0[r]); acc1[r] = fmaf(sv[r].x, lo.y, acc1[r]); }
+#pragma unroll
+            for (int r = 0; r < SR; r++) { acc0[r] = fmaf(sv[r].y, lo.z, acc0[r]); acc1[r] = fmaf(sv[r].y, lo.w, acc1[r]); }
+#pragma unroll
+            for (int r = 0; r < SR; r++) { acc0[r] = fmaf(sv[r].z, hi.x, acc0[r]); acc1[r] = fmaf(sv[r].z, hi.y, acc1[r]); }
+#pragma unroll
+            for (int r = 0; r < SR; r++) { acc0[r] = fmaf(sv[r].w, hi.z, acc0[r]); acc1[r] = fmaf(sv[r].w, hi.w, acc1[r]); }
         }
+#pragma unroll
+        for (int r = 0; r < SR; r++)
+            *reinterpret_cast<float2*>(&P[warp][r][2 * lane]) = make_float2(acc0[r], acc1[r]);
+        __syncthreads();   // partial products complete; every warp is done reading S
+        float4 n = bv;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float4 p = *reinterpret_cast<const float4*>(&P[w][rr][c4]);
+            n.x += p.x; n.y += p.y; n.z += p.z; n.w += p.w;
+        }
+        *reinterpret_cast<float4*>(&S[rr][c4]) = n;
+        float* dst = (ch + 1 < NC) ? S0ws + ((size_t)bh * NC + ch + 1) * CN * CN
+                                   : (h_out ? h_out + (size_t)bh * CN * CN : nullptr);
+        if (dst) *reinterpret_cast<float4*>(dst + (size_t)(dv0 + rr) * CN + c4) = n;
+        load(av, bv, ch + 3);
+        __syncthreads();   // the new state is visible; P may be overwritten
+    };
+    for (int ch = 0; ch < NC; ch += 3) {
+        chunk(a0, b0, ch);
+        if (ch + 1 < NC) chunk(a1, b1, ch + 1);
+        if (ch + 2 < NC) chunk(a2, b2, ch + 2);
+    }
 }
 
 // ------------------------------------------------------------ out
@@ -653,10 +667,7 @@ int launch_wkv7_chunk_fwd(int dtype, const void* r, const void* w, const void* k
         prep<<<dim3(NC, B * H), CT, sizeof(PrepSmem), st>>>((const T*)w, (const T*)k, (const T*)v,
                                                             (const T*)a, (const T*)b, Aws, Bws, T_, H, NC);
         if (int rc = check_launch("wkv7_chunk_prep_kernel")) return rc;
-        e = cudaFuncSetAttribute(wkv7_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)sizeof(ScanSmem));
-        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "wkv7 chunked: %s", cudaGetErrorString(e));
-        wkv7_chunk_scan_kernel<<<dim3(B * H, CN / CR), CT, sizeof(ScanSmem), st>>>(h_in, Aws, Bws, S0ws, h_out, NC);
+        wkv7_chunk_scan_kernel<<<dim3(B * H, CN / SR), ST, 0, st>>>(h_in, Aws, Bws, S0ws, h_out, NC);
         if (int rc = check_launch("wkv7_chunk_scan_kernel")) return rc;
         out<<<dim3(NC, B * H), CT, sizeof(OutSmem), st>>>(
             (const T*)r, (const T*)w, (const T*)k, (const T*)v, (const T*)a, (const T*)b, S0ws, (T*)y, sa,
