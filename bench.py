@@ -329,6 +329,90 @@ class Decode15B:
         return cpu_decode_tokps(self.L, self.C, self.V, seconds)
 
 
+class StateTune29B:
+    """Config 5 on the WKV-7 path: the per-layer initial states of x070 2.9B
+    (L=32, H=40) trained by WKVStateTuner, `rows` 4096-token sequences per GPU
+    (data-parallel, weak scaling; the tuner's NCCL allreduce under torchrun)."""
+    name = "statetune"
+    unit = "tok/s"
+    L, H, T, N = 32, 40, 4096, 64
+    NSETS = 4   # distinct per-layer input sets (each 294 MB > L2), cycled over the layers
+
+    def __init__(self, rows=1):
+        self.B = rows
+        self.metric = ("x070 2.9B state-tuning tok/s on the WKV-7 path (config 5: L=32 H=40 T=4096, "
+                       f"{rows} sequence/GPU; per layer train forward + checkpointed backward, "
+                       "NCCL allreduce of the state gradients, global-norm clip + AdamW)")
+
+    def setup(self, torch, dev):
+        from swiftrwkv_b200.state_tune import StateTuneConfig, WKVStateTuner
+        self.torch = torch
+        rank = torch.distributed.get_rank() if torch.distributed.is_initialized() else 0
+        g = torch.Generator(device=dev)
+        g.manual_seed(SEED + rank)
+        shape = (self.B, self.T, self.H, self.N)
+        n = lambda: torch.randn(shape, generator=g, device=dev)
+        self.sets = []
+        for _ in range(self.NSETS):
+            r, k, v = n(), n(), n()
+            w = torch.exp(-torch.exp(-torch.nn.functional.softplus(-n()) - 0.5))
+            kk = torch.nn.functional.normalize(n(), dim=-1)
+            b = kk * torch.sigmoid(n())
+            self.sets.append([r, w, k, v, -kk, b, n()])
+        self.layers = [self.sets[l % self.NSETS] for l in range(self.L)]
+        self.pin = [[x.cpu().pin_memory() for x in s] for s in self.sets]
+        self.tuner = WKVStateTuner(self.L, self.H, config=StateTuneConfig(), device=dev)
+        self.pin_norm = torch.zeros((), dtype=torch.float32).pin_memory()
+        BTHN = self.B * self.T * self.H * self.N
+        BHN2 = self.B * self.H * self.N * self.N
+        # canonical WKV bytes per layer: forward 4(7 BTHN + 2 BHN^2), backward 4(14 BTHN + 3 BHN^2)
+        self.alg_bytes = self.L * 4 * (21 * BTHN + 5 * BHN2)
+        self.bwd_bytes = 4 * (14 * BTHN + 3 * BHN2)
+        self.units_per_step = self.B * self.T
+        # per layer: broadcast, train forward, backward, grad sum; then clip + AdamW (2)
+        self.launches_per_step = 4 * self.L + 2
+        self.kernel = "wkv7_bwd_seq_kernel<float> (one layer's checkpointed backward)"
+        self.h2d = sum(x.numel() * 4 for s in self.sets for x in s)
+        self.d2h = 4
+        self.dh = torch.empty((self.B, self.H, self.N, self.N), device=dev)
+
+    def step(self):
+        self.tuner.step(self.layers)
+
+    def step_e2e(self):
+        for d, p in zip(self.sets, self.pin):
+            for x, y in zip(d, p):
+                x.copy_(y, non_blocking=True)
+        norm = self.tuner.step(self.layers)
+        self.pin_norm.copy_(norm, non_blocking=True)
+
+    def dominant(self):
+        ops = self.tuner.ops
+        *inputs, dy = self.layers[0]
+        ops.layer_grad(inputs, dy, self.tuner.params[0], self.tuner.grads[0])
+
+    @property
+    def dom_bytes(self):
+        # layer_grad = train forward + backward (+ two small state kernels)
+        return self.alg_bytes / self.L
+
+    def cpu(self, seconds):
+        from oracle import oracle as O
+        rng = np.random.default_rng(SEED)
+        Ts = 256
+        host = config1_inputs(rng, 1, Ts, self.H, self.N)
+        dy = rng.standard_normal((1, Ts, self.H, self.N)).astype(np.float32)
+        st = np.zeros((self.H, self.N, self.N), np.float32)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.state_layer_grad(*host, dy, st)
+            n += 1
+        per_layer = (time.perf_counter() - t0) / n
+        return Ts / (per_layer * self.L), (f"{n} oracle layer gradients at T={Ts} H=40 "
+                                            "(train forward + backward), scaled to 32 layers")
+
+
 _CPU_CACHE = {}
 
 
@@ -391,7 +475,8 @@ def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head):
                                           f"step = {L} layers + head")
 
 
-WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "gemv": GemvSuite}
+WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "gemv": GemvSuite,
+             "statetune": StateTune29B}
 
 
 # ----------------------------------------------------------------------- timing
@@ -462,6 +547,8 @@ def make_workload(args):
         return Decode15B(args.rows or 64, args.prompt)
     if args.workload == "gemv":
         return GemvSuite(args.rows or 1)
+    if args.workload == "statetune":
+        return StateTune29B(args.rows or 1)
     return WORKLOADS[args.workload]()
 
 
@@ -532,7 +619,7 @@ def main():
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32" if wl.name == "wkv7" else "u4 x f16 -> f32", "data": "synthetic",
+        "dtype": "f32" if wl.name in ("wkv7", "statetune") else "u4 x f16 -> f32", "data": "synthetic",
         "config": {"workload": wl.name, "l2": l2_note, "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
@@ -545,6 +632,11 @@ def main():
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clocks,
     }
+    if wl.name == "statetune":
+        result["config"].update({"model": "x070 2.9B WKV path (L=32 H=40 N=64)", "seq_len": wl.T,
+                                 "rows_per_gpu": wl.B, "global_batch": wl.B * world,
+                                 "parallelism": f"dp{world} (NCCL allreduce of state gradients)",
+                                 "inputs": f"{wl.NSETS} distinct per-layer sets cycled over 32 layers"})
     if wl.name == "decode":
         result["config"].update({"model": "x070 1.5B (L=24 C=2048 H=32 V=65536 FFN=8192)",
                                  "rows_per_gpu": wl.rows, "global_batch": wl.rows * world,

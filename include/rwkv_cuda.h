@@ -71,9 +71,10 @@ int rwkv_wkv7_forward(int dtype, const void* r, const void* w, const void* k, co
 /* Prefill form of rwkv_wkv7_forward, chunked (same arguments and results to
  * fp32 rounding, ~1e-6 relative).  16-token chunks in the normalised DPLR
  * form: each chunk's transition S -> S A_c + B_c is built in parallel over
- * chunks, a scan applies them (one 16x64x64 tensor-core product per chunk
- * and head), and each chunk's outputs come from its start state -- so the
- * T-sequential depth drops sixteen-fold.  Unlike rwkv_wkv7_forward it does not
+ * chunks (tensor cores), a scan applies them (one 64x64x64 fp32 product per
+ * chunk and head, split over 8 CTAs of 8 state rows), and each chunk's
+ * outputs come from its start state -- so the T-sequential depth drops
+ * sixteen-fold.  Unlike rwkv_wkv7_forward it does not
  * promise the bitwise identities of the sequential form (step = forward at
  * T=1, split = contiguous).  h_in / h_out as in rwkv_wkv7_forward; sa
  * [B,T,H,N] fp32 (may be NULL) receives S_{t-1} a_t as the training forward
@@ -297,6 +298,36 @@ int rwkv_x070_profile_step(rwkv_x070_t model, int rows, float* ms_host, int cap,
                            int names_cap, int* count, rwkv_stream_t stream);
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t model);
 int rwkv_x070_launches_per_step(rwkv_x070_t model);
+
+/* ------------------------------------------------ state tuning (WKV path)
+ * The trainable initial WKV state of a layer, [H, N, N] fp32, shared by every
+ * sequence of the batch (StateTrainableSet, Sources/RWKVGen/InitialState.swift:
+ * 176-251).  N must be 64; pointers 16-byte aligned. */
+
+/* h[b] = state for b < B: the forward's h_in [B, H, N, N] (the state broadcast
+ * of InitialLayerState.broadcast, InitialState.swift:59-73). */
+int rwkv_state_broadcast(const float* state, float* h, int B, int H, int N, rwkv_stream_t stream);
+/* grad (+)= sum over b of dh_in[b], b = 0..B-1 in order (deterministic); the
+ * gradient of the shared state from the backward's dh_in.  accumulate = 0
+ * overwrites grad. */
+int rwkv_state_grad_sum(const float* dh_in, float* grad, int B, int H, int N, int accumulate,
+                        rwkv_stream_t stream);
+/* Workspace bytes rwkv_adamw_clip_step needs for n parameters. */
+int64_t rwkv_adamw_workspace_size(int64_t n);
+/* One optimizer step of Trainer.run (Sources/RWKVGen/Training/Trainer.swift:
+ * 141-161) over n fp32 parameters, in its order: g = grad * grad_scale (the
+ * average: 1/gradAccum, or 1/world after a data-parallel sum); global-norm
+ * clip g *= min(1, clip / (||g|| + 1e-6)) when clip > 0 (clipByGlobalNorm,
+ * :182-189); m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2; upd = (m/c1) /
+ * (sqrt(v/c2) + eps) [+ weight_decay * p]; p -= lr * upd.  c1 = 1 - b1^t and
+ * c2 = 1 - b2^t come from the host's step count t.  Every operation rounds to
+ * fp32 (no fused multiply-add); the norm's sum of squares is taken in double
+ * in a fixed order.  ||g|| (before clipping) goes to *norm_out (device, may be
+ * NULL).  Nothing returns to the host. */
+int rwkv_adamw_clip_step(float* param, float* m, float* v, const float* grad, int64_t n,
+                         float grad_scale, float clip, float lr, float beta1, float beta2, float eps,
+                         float weight_decay, float bias_c1, float bias_c2, float* norm_out,
+                         void* workspace, int64_t workspace_bytes, rwkv_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -265,3 +265,42 @@ def sym_rows(ids, codes, qs, d, IN):
     out = np.empty((ids.size, IN), np.uint16)
     lib().orc_sym_rows(_p(ids), ids.size, _p(codes), _p(qs), _p(d), _p(out), IN)
     return out
+
+
+# ------------------------------------------------------------------ state tuning
+
+def state_layer_grad(r, w, k, v, a, b, dy, state):
+    """Gradient of sum(y * dy) w.r.t. a layer's initial state [H,N,N] shared
+    by the batch (StateTrainableSet, InitialState.swift:176-251): h_in[b] =
+    state, the train forward + v2 backward, then dh_in summed over b in order."""
+    B = r.shape[0]
+    h_in = np.ascontiguousarray(np.broadcast_to(_f32(state), (B,) + state.shape))
+    out = wkv7_train(r, w, k, v, a, b, h_in, dy)
+    dh_in = out[-1]
+    g = np.zeros(state.shape, np.float32)
+    for i in range(B):
+        g = (g + dh_in[i]).astype(np.float32)
+    return g
+
+
+def adamw_clip_step(param, m, v, grad, *, grad_scale, clip, lr, beta1, beta2, eps,
+                    weight_decay, c1, c2):
+    """One optimizer step of Trainer.run (Trainer.swift:141-161) with
+    clipByGlobalNorm (:182-189), each elementwise operation rounded to fp32
+    (numpy float32 arithmetic does not fuse).  The sum of squares is taken in
+    double.  Returns (param, m, v, norm) as new arrays."""
+    f = np.float32
+    g = (_f32(grad) * f(grad_scale)).astype(f)
+    norm = f(np.sqrt(f(np.sum((g * g).astype(np.float64)))))
+    if clip > 0:
+        s = min(f(1), f(f(clip) / f(norm + f(1e-6))))
+        g = (g * f(s)).astype(f)
+    m = (f(beta1) * _f32(m) + (f(1) - f(beta1)) * g).astype(f)
+    v = (f(beta2) * _f32(v) + (f(1) - f(beta2)) * (g * g)).astype(f)
+    mhat = (m / f(c1)).astype(f)
+    vhat = (v / f(c2)).astype(f)
+    upd = (mhat / (np.sqrt(vhat) + f(eps))).astype(f)
+    p = _f32(param)
+    if weight_decay > 0:
+        upd = (upd + f(weight_decay) * p).astype(f)
+    return (p - f(lr) * upd).astype(f), m, v, norm

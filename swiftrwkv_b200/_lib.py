@@ -67,6 +67,10 @@ _SIGS = {
     "rwkv_x070_profile_step": [P, I, P, I, P, I, P, P],
     "rwkv_x070_weight_bytes": [P],
     "rwkv_x070_launches_per_step": [P],
+    "rwkv_state_broadcast": [P, P, I, I, I, P],
+    "rwkv_state_grad_sum": [P, P, I, I, I, I, P],
+    "rwkv_adamw_workspace_size": [I64],
+    "rwkv_adamw_clip_step": [P, P, P, P, I64, F, F, F, F, F, F, F, F, F, P, P, I64, P],
 }
 _RESTYPES = {
     "rwkv_status_string": ctypes.c_char_p,
@@ -74,6 +78,7 @@ _RESTYPES = {
     "rwkv_wkv7_backward_workspace_size": I64,
     "rwkv_wkv7_forward_chunked_workspace_size": I64,
     "rwkv_x070_weight_bytes": I64,
+    "rwkv_adamw_workspace_size": I64,
 }
 
 _lib = None
