@@ -342,7 +342,7 @@ class StateTune29B:
         self.B = rows
         self.metric = ("x070 2.9B state-tuning tok/s on the WKV-7 path (config 5: L=32 H=40 T=4096, "
                        f"{rows} sequence/GPU; per layer train forward + checkpointed backward, "
-                       "NCCL allreduce of the state gradients, global-norm clip + AdamW)")
+                       "NCCL allreduce of the state gradients, global-norm clip + AdamW; chunked DPLR kernels)")
 
     def setup(self, torch, dev):
         from swiftrwkv_b200.state_tune import StateTuneConfig, WKVStateTuner
@@ -369,9 +369,11 @@ class StateTune29B:
         self.alg_bytes = self.L * 4 * (21 * BTHN + 5 * BHN2)
         self.bwd_bytes = 4 * (14 * BTHN + 3 * BHN2)
         self.units_per_step = self.B * self.T
-        # per layer: broadcast, train forward, backward, grad sum; then clip + AdamW (2)
-        self.launches_per_step = 4 * self.L + 2
-        self.kernel = "wkv7_bwd_seq_kernel<float> (one layer's checkpointed backward)"
+        # per layer: broadcast, train forward (prep, scan, out), backward (prep, reverse
+        # scan, out), grad sum; then clip + AdamW (2)
+        self.launches_per_step = 8 * self.L + 2
+        self.kernel = ("one layer's state gradient: chunked train forward + chunked backward "
+                       "(wkv7_chunk_{prep,scan,out}, wkv7_chunk_bwd_{prep,out}, reverse scan)")
         self.h2d = sum(x.numel() * 4 for s in self.sets for x in s)
         self.d2h = 4
         self.dh = torch.empty((self.B, self.H, self.N, self.N), device=dev)

@@ -98,6 +98,18 @@ int rwkv_wkv7_train_forward(int dtype, const void* r, const void* w, const void*
                             void* y, float* h_out, float* sa, float* h_ckpt, int B, int T,
                             int H, int N, rwkv_stream_t stream);
 
+/* Chunked form of rwkv_wkv7_train_forward (same arguments and results to fp32
+ * rounding, plus a workspace of rwkv_wkv7_forward_chunked_workspace_size
+ * bytes): the chunked prefill kernels with each chunk's end state written to
+ * h_ckpt [B, H, T/16, N, N].  T % 16 == 0.  Replaces wkv7TrainWithState's
+ * forward kernel (Sources/RWKVKernel/WKV7Train.swift:26-97, :375-468) on the
+ * prefill-sized path. */
+int rwkv_wkv7_train_forward_chunked(int dtype, const void* r, const void* w, const void* k,
+                                    const void* v, const void* a, const void* b, const float* h_in,
+                                    void* y, float* h_out, float* sa, float* h_ckpt, int B, int T,
+                                    int H, int N, void* workspace, int64_t workspace_bytes,
+                                    rwkv_stream_t stream);
+
 /* Workspace bytes rwkv_wkv7_backward needs for these sizes. */
 int64_t rwkv_wkv7_backward_workspace_size(int B, int T, int H, int N);
 
@@ -113,6 +125,23 @@ int rwkv_wkv7_backward(int dtype, const void* r, const void* w, const void* k, c
                        const void* dy, const float* dh_out, void* dr, void* dw, void* dk,
                        void* dv, void* da, void* db, float* dh_in, int B, int T, int H, int N,
                        void* workspace, int64_t workspace_bytes, rwkv_stream_t stream);
+
+/* Chunked (DPLR) form of rwkv_wkv7_backward: same arguments and results to
+ * fp32 rounding, deterministic, T % 16 == 0.  The gradient at every chunk
+ * boundary comes from a reverse scan (Q' = Q A_c^T + DY B', built per chunk in
+ * parallel), then each chunk's gradients come from its start state (the
+ * h_ckpt / h_in checkpoint) and its boundary gradient as tensor-core products,
+ * so the T-sequential depth is one 64x64x64 product per 16 tokens.  Chunks
+ * whose decays underflow (smallest c_16 < 1e-30) are done token by token.
+ * `workspace`: rwkv_wkv7_backward_chunked_workspace_size bytes (3 states per
+ * chunk and head).  Replaces the VJP of wkv7TrainWithState (Sources/
+ * RWKVKernel/WKV7Train.swift:99-339, :410-420) on the training path. */
+int64_t rwkv_wkv7_backward_chunked_workspace_size(int B, int T, int H, int N);
+int rwkv_wkv7_backward_chunked(int dtype, const void* r, const void* w, const void* k, const void* v,
+                               const void* a, const void* b, const float* h_in, const float* h_ckpt,
+                               const void* dy, const float* dh_out, void* dr, void* dw, void* dk,
+                               void* dv, void* da, void* db, float* dh_in, int B, int T, int H, int N,
+                               void* workspace, int64_t workspace_bytes, rwkv_stream_t stream);
 
 /* rwkv_wkv7_backward without a workspace argument and without allocating.
  * No counterpart in the reference: it exists for hosts that cannot allocate

@@ -41,7 +41,10 @@ _SIGS = {
     "rwkv_wkv7_train_forward": [I, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P],
     "rwkv_wkv7_forward_chunked_workspace_size": [I, I, I, I],
     "rwkv_wkv7_forward_chunked": [I, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P, I64, P],
+    "rwkv_wkv7_train_forward_chunked": [I, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P, I64, P],
     "rwkv_wkv7_backward_workspace_size": [I, I, I, I],
+    "rwkv_wkv7_backward_chunked_workspace_size": [I, I, I, I],
+    "rwkv_wkv7_backward_chunked": [I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P, I64, P],
     "rwkv_wkv7_backward": [I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P, I64, P],
     "rwkv_wkv7_backward_noalloc": [I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, P],
     "rwkv_wkv7_step": [I, P, P, P, P, P, P, P, P, I, I, I, P],
@@ -77,6 +80,7 @@ _RESTYPES = {
     "rwkv_last_error": ctypes.c_char_p,
     "rwkv_wkv7_backward_workspace_size": I64,
     "rwkv_wkv7_forward_chunked_workspace_size": I64,
+    "rwkv_wkv7_backward_chunked_workspace_size": I64,
     "rwkv_x070_weight_bytes": I64,
     "rwkv_adamw_workspace_size": I64,
 }

@@ -25,9 +25,14 @@ int launch_wkv_tail(const float*, const float*, const float*, const float*, cons
                     const float*, const float*, const float*, float*, int, int, int, float,
                     cudaStream_t);
 int launch_wkv7_chunk_fwd(int, const void*, const void*, const void*, const void*, const void*,
-                          const void*, const float*, void*, float*, float*, int, int, int, void*,
-                          cudaStream_t);
+                          const void*, const float*, void*, float*, float*, float*, int, int, int,
+                          void*, cudaStream_t);
 int64_t wkv7_chunk_workspace(int, int, int);
+int64_t wkv7_chunk_bwd_workspace(int, int, int);
+int launch_wkv7_chunk_bwd(int, const void*, const void*, const void*, const void*, const void*,
+                          const void*, const float*, const float*, const void*, const float*, void*,
+                          void*, void*, void*, void*, void*, float*, int, int, int, void*,
+                          cudaStream_t);
 int64_t wkv7_bwd_seq_workspace(int, int);
 int launch_wkv7_bwd_seq(int, const void*, const void*, const void*, const void*, const void*,
                         const void*, const float*, const float*, const void*, const float*, void*,
@@ -131,8 +136,51 @@ int rwkv_wkv7_forward_chunked(int dtype, const void* r, const void* w, const voi
                  "rwkv_wkv7_forward_chunked: workspace %lld bytes, need %lld",
                  (long long)workspace_bytes, (long long)need);
     RWKV_REQUIRE(al16(workspace), RWKV_E_UNSUPPORTED, "rwkv_wkv7_forward_chunked: workspace not 16-byte aligned");
-    return launch_wkv7_chunk_fwd(dtype, r, w, k, v, a, b, h_in, y, h_out, sa, B, T, H, workspace,
-                                 (cudaStream_t)stream);
+    return launch_wkv7_chunk_fwd(dtype, r, w, k, v, a, b, h_in, y, h_out, sa, nullptr, B, T, H,
+                                 workspace, (cudaStream_t)stream);
+}
+
+int rwkv_wkv7_train_forward_chunked(int dtype, const void* r, const void* w, const void* k,
+                                    const void* v, const void* a, const void* b, const float* h_in,
+                                    void* y, float* h_out, float* sa, float* h_ckpt, int B, int T,
+                                    int H, int N, void* workspace, int64_t workspace_bytes,
+                                    rwkv_stream_t stream) {
+    const char* fn = "rwkv_wkv7_train_forward_chunked";
+    const void* req[] = {r, w, k, v, a, b, y, h_ckpt};
+    if (int rc = check_wkv_common(dtype, req, 8, B, T, H, N, fn)) return rc;
+    RWKV_REQUIRE(T % RWKV_WKV7_CHUNK == 0, RWKV_E_SHAPE, "%s: T=%d must be a multiple of 16", fn, T);
+    RWKV_REQUIRE(al16(h_in) && al16(h_out), RWKV_E_UNSUPPORTED, "%s: state not 16-byte aligned", fn);
+    const int64_t need = wkv7_chunk_workspace(B, T, H);
+    RWKV_REQUIRE(workspace != nullptr && workspace_bytes >= need, RWKV_E_WORKSPACE,
+                 "%s: workspace %lld bytes, need %lld", fn, (long long)workspace_bytes, (long long)need);
+    RWKV_REQUIRE(al16(workspace), RWKV_E_UNSUPPORTED, "%s: workspace not 16-byte aligned", fn);
+    return launch_wkv7_chunk_fwd(dtype, r, w, k, v, a, b, h_in, y, h_out, sa, h_ckpt, B, T, H,
+                                 workspace, (cudaStream_t)stream);
+}
+
+int64_t rwkv_wkv7_backward_chunked_workspace_size(int B, int T, int H, int N) {
+    (void)N;
+    if (B < 1 || T < RWKV_WKV7_CHUNK || H < 1) return 0;
+    return wkv7_chunk_bwd_workspace(B, T, H);
+}
+
+int rwkv_wkv7_backward_chunked(int dtype, const void* r, const void* w, const void* k, const void* v,
+                               const void* a, const void* b, const float* h_in, const float* h_ckpt,
+                               const void* dy, const float* dh_out, void* dr, void* dw, void* dk,
+                               void* dv, void* da, void* db, float* dh_in, int B, int T, int H, int N,
+                               void* workspace, int64_t workspace_bytes, rwkv_stream_t stream) {
+    const char* fn = "rwkv_wkv7_backward_chunked";
+    const void* req[] = {r, w, k, v, a, b, h_ckpt, dy, dr, dw, dk, dv, da, db};
+    if (int rc = check_wkv_common(dtype, req, 14, B, T, H, N, fn)) return rc;
+    RWKV_REQUIRE(T % RWKV_WKV7_CHUNK == 0, RWKV_E_SHAPE, "%s: T=%d must be a multiple of 16", fn, T);
+    RWKV_REQUIRE(al16(h_in) && al16(h_ckpt) && al16(dh_out) && al16(dh_in), RWKV_E_UNSUPPORTED,
+                 "%s: state not 16-byte aligned", fn);
+    const int64_t need = wkv7_chunk_bwd_workspace(B, T, H);
+    RWKV_REQUIRE(workspace != nullptr && workspace_bytes >= need, RWKV_E_WORKSPACE,
+                 "%s: workspace %lld bytes, need %lld", fn, (long long)workspace_bytes, (long long)need);
+    RWKV_REQUIRE(al16(workspace), RWKV_E_UNSUPPORTED, "%s: workspace not 16-byte aligned", fn);
+    return launch_wkv7_chunk_bwd(dtype, r, w, k, v, a, b, h_in, h_ckpt, dy, dh_out, dr, dw, dk, dv,
+                                 da, db, dh_in, B, T, H, workspace, (cudaStream_t)stream);
 }
 
 int rwkv_wkv7_train_forward(int dtype, const void* r, const void* w, const void* k,

@@ -164,13 +164,62 @@ def wkv7Backward(r, w, k, v, a, b, hIn, hCkpt, dOut, dHOut=None):
     return (*grads, dh_in)
 
 
+def wkv7TrainForwardChunked(r, w, k, v, a, b, hIn=None):
+    """Chunked form of the training forward (rwkv_wkv7_train_forward_chunked):
+    returns (out, hOut, sa, hCkpt) like the sequential one, to fp32 rounding."""
+    B, T, H, D = _check_seq(r, "wkv7TrainForwardChunked")
+    if T % WKV7_CHUNK:
+        raise ValueError(f"T ({T}) must be divisible by CHUNK {WKV7_CHUNK}")
+    dt = _common_dtype((r, w, k, v, a, b))
+    r, w, k, v, a, b = _prep((r, w, k, v, a, b), dt)
+    h = _state(hIn, (B, H, D, D))
+    out = torch.empty_like(r)
+    h_out = torch.empty((B, H, D, D), device=r.device, dtype=torch.float32)
+    sa = torch.empty(r.shape, device=r.device, dtype=torch.float32)
+    ck = torch.empty((B, H, T // WKV7_CHUNK, D, D), device=r.device, dtype=torch.float32)
+    ws_bytes = int(_lib.lib().rwkv_wkv7_forward_chunked_workspace_size(B, T, H, D))
+    ws = torch.empty(max(ws_bytes, 16), device=r.device, dtype=torch.uint8)
+    call("rwkv_wkv7_train_forward_chunked", _DT[dt], *map(_ptr, (r, w, k, v, a, b, h, out, h_out, sa, ck)),
+         B, T, H, D, _ptr(ws), ws_bytes, _stream())
+    counters["wkv7TrainForwardLaunches"] += 1
+    return out, h_out, sa, ck
+
+
+def wkv7BackwardChunked(r, w, k, v, a, b, hIn, hCkpt, dOut, dHOut=None):
+    """Chunked (DPLR) form of wkv7Backward (rwkv_wkv7_backward_chunked): the
+    same gradients (dr, dw, dk, dv, da, db, dhIn) to fp32 rounding."""
+    B, T, H, D = _check_seq(r, "wkv7BackwardChunked")
+    if T % WKV7_CHUNK:
+        raise ValueError(f"T ({T}) must be divisible by CHUNK {WKV7_CHUNK}")
+    dt = _common_dtype((r, w, k, v, a, b, dOut))
+    r, w, k, v, a, b, dOut = _prep((r, w, k, v, a, b, dOut), dt)
+    h = _state(hIn, (B, H, D, D))
+    dh = _state(dHOut, (B, H, D, D))
+    grads = [torch.empty_like(r) for _ in range(6)]
+    dh_in = torch.empty((B, H, D, D), device=r.device, dtype=torch.float32)
+    ws_bytes = int(_lib.lib().rwkv_wkv7_backward_chunked_workspace_size(B, T, H, D))
+    ws = torch.empty(max(ws_bytes, 16), device=r.device, dtype=torch.uint8)
+    call("rwkv_wkv7_backward_chunked", _DT[dt],
+         *map(_ptr, (r, w, k, v, a, b, h, hCkpt.contiguous(), dOut, dh)), *map(_ptr, grads), _ptr(dh_in),
+         B, T, H, D, _ptr(ws), ws_bytes, _stream())
+    counters["wkv7BackwardLaunches"] += 1
+    return (*grads, dh_in)
+
+
+# The differentiable path's kernels: chunked (DPLR) forward and backward when
+# True, the sequential ones (the reference's kernel structure) when False.
+useChunkedTraining = True
+
+
 class _WKV7Train(torch.autograd.Function):
     """Differentiable WKV-7 with explicit state: forward outputs are kept for
     the backward (wkv7KeepForwardOutputs = true, WKV7Train.swift:354)."""
 
     @staticmethod
     def forward(ctx, r, w, k, v, a, b, h0):
-        out, h_out, sa, ck = _train_forward(r, w, k, v, a, b, h0)
+        ctx.chunked = useChunkedTraining
+        fwd = wkv7TrainForwardChunked if ctx.chunked else _train_forward
+        out, h_out, sa, ck = fwd(r, w, k, v, a, b, h0)
         ctx.save_for_backward(r, w, k, v, a, b, h0, ck)
         ctx.in_dtypes = [t.dtype for t in (r, w, k, v, a, b, h0)]
         return out, h_out
@@ -180,7 +229,8 @@ class _WKV7Train(torch.autograd.Function):
         r, w, k, v, a, b, h0, ck = ctx.saved_tensors
         if d_out is None:
             d_out = torch.zeros_like(r)
-        g = wkv7Backward(r, w, k, v, a, b, h0, ck, d_out, d_h_out)
+        bwd = wkv7BackwardChunked if ctx.chunked else wkv7Backward
+        g = bwd(r, w, k, v, a, b, h0, ck, d_out, d_h_out)
         return tuple(gi.to(dt) for gi, dt in zip(g, ctx.in_dtypes))
 
 

@@ -6,8 +6,8 @@ Sources/RWKVGen/InitialState.swift:176-251, `train: [.wkv]`).  One step:
 
   for each layer, top to bottom (SequentialBackward.swift:180-219 order):
       h_in = broadcast(state[l])                     rwkv_state_broadcast
-      train forward with 16-token checkpoints        rwkv_wkv7_train_forward
-      backward from the layer's upstream dy          rwkv_wkv7_backward
+      train forward with 16-token checkpoints        rwkv_wkv7_train_forward_chunked
+      backward from the layer's upstream dy          rwkv_wkv7_backward_chunked
       grad[l] = sum over the local batch of dh_in    rwkv_state_grad_sum
       allreduce(sum) of grad[l] over the ranks, started as soon as the
       layer is done (NCCL, asynchronous, one bucket per layer)
@@ -110,7 +110,8 @@ class CudaStateOps:
         s = self._seq.get(key)
         if s is None:
             dev = like.device
-            ws_bytes = int(_lib.lib().rwkv_wkv7_backward_workspace_size(B, T, H, N))
+            ws_bytes = max(int(_lib.lib().rwkv_wkv7_backward_chunked_workspace_size(B, T, H, N)),
+                           int(_lib.lib().rwkv_wkv7_forward_chunked_workspace_size(B, T, H, N)))
             s = {
                 "h_in": torch.empty((B, H, N, N), device=dev, dtype=torch.float32),
                 "y": torch.empty_like(like),
@@ -132,9 +133,9 @@ class CudaStateOps:
         st = _stream()
         dt = _DT[r.dtype]
         call("rwkv_state_broadcast", _p(state), _p(s["h_in"]), B, H, N, st)
-        call("rwkv_wkv7_train_forward", dt, *map(_p, inputs), _p(s["h_in"]), _p(s["y"]), None, None,
-             _p(s["ck"]), B, T, H, N, st)
-        call("rwkv_wkv7_backward", dt, *map(_p, inputs), _p(s["h_in"]), _p(s["ck"]), _p(dy), None,
+        call("rwkv_wkv7_train_forward_chunked", dt, *map(_p, inputs), _p(s["h_in"]), _p(s["y"]), None,
+             None, _p(s["ck"]), B, T, H, N, _p(s["ws"]), s["ws_bytes"], st)
+        call("rwkv_wkv7_backward_chunked", dt, *map(_p, inputs), _p(s["h_in"]), _p(s["ck"]), _p(dy), None,
              *map(_p, s["d"]), _p(s["dh_in"]), B, T, H, N, _p(s["ws"]), s["ws_bytes"], st)
         call("rwkv_state_grad_sum", _p(s["dh_in"]), _p(grad), B, H, N, 0, st)
 
