@@ -17,8 +17,16 @@ Workloads (synthetic, seeded 0x5EED2026):
            tok/s = B*T per step.  Inputs (22 MB) are smaller than L2, so L2 is
            flushed (a 256 MB write) before every timed step, outside the timed
            interval.
+  wkv7train  config 1 as the operator row of the survey measures it:
+           forward + backward of the training path (chunked train forward
+           with 16-token checkpoints, chunked DPLR backward), dy ~ N(0,1);
+           tok/s = B*T per step; L2 flushed before every timed step.
   gemv     config 2 -- 4-bit g64 GEMV over the four 1.5B projection shapes,
            rows 1, fp16 activations; GB/s of the packed weight stream.
+  statetune  config 5 on the WKV path -- the per-layer initial states of
+           x070 2.9B (L=32, H=40) trained by WKVStateTuner on one 4096-token
+           sequence per GPU (data-parallel under torchrun: NCCL allreduce of
+           the state gradients), clip + AdamW on the device; tok/s.
 `--impl reference` times the CPU oracle (the reference's Metal/MLX path
 cannot run here) on the same workload and metric, on all host cores.
 """
@@ -185,6 +193,75 @@ class WKV7Prefill:
             n += 1
         dt = time.perf_counter() - t0
         return n * self.B * self.T / dt, f"{n} full config-1 forwards ({n * self.B * self.T} tokens)"
+
+
+class WKV7Train:
+    """Config 1 as SURVEY's operator row measures it: forward + backward of the
+    WKV-7 training path (chunked train forward with checkpoints, chunked DPLR
+    backward), B=1 T=1024 H=12, dy ~ N(0,1)."""
+    name = "wkv7train"
+    metric = ("WKV-7 forward + backward tok/s (config 1 operator, B=1 T=1024 H=12 N=64 fp32, "
+              "chunked DPLR train forward + backward)")
+    unit = "tok/s"
+    B, T, H, N = 1, 1024, 12, 64
+
+    def setup(self, torch, dev):
+        from swiftrwkv_b200 import _lib
+        self.torch, self._lib = torch, _lib
+        rng = np.random.default_rng(SEED)
+        self.host = config1_inputs(rng, self.B, self.T, self.H, self.N)
+        self.host.append(rng.standard_normal(self.host[0].shape).astype(np.float32))   # dy
+        self.x = [torch.from_numpy(a).to(dev) for a in self.host]
+        shp = (self.B, self.T, self.H, self.N)
+        self.y = torch.empty(shp, device=dev)
+        self.ck = torch.empty((self.B, self.H, self.T // 16, self.N, self.N), device=dev)
+        self.g = [torch.empty(shp, device=dev) for _ in range(6)]
+        self.dh = torch.empty((self.B, self.H, self.N, self.N), device=dev)
+        L = _lib.lib()
+        self.ws_bytes = max(int(L.rwkv_wkv7_forward_chunked_workspace_size(self.B, self.T, self.H, self.N)),
+                            int(L.rwkv_wkv7_backward_chunked_workspace_size(self.B, self.T, self.H, self.N)))
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.pin = [torch.from_numpy(a).pin_memory() for a in self.host]
+        self.pin_g = [torch.empty(shp, dtype=torch.float32).pin_memory() for _ in range(6)]
+        self.units_per_step = self.B * self.T
+        # forward: prep, scan, out; backward: prep, reverse scan, out
+        self.launches_per_step = 6
+        BTHN = self.B * self.T * self.H * self.N
+        BHN2 = self.B * self.H * self.N * self.N
+        # canonical bytes: forward 4(7 BTHN + 2 BHN^2) + backward 4(14 BTHN + 3 BHN^2)
+        self.alg_bytes = 4 * (21 * BTHN + 5 * BHN2)
+        self.kernel = ("wkv7_chunk_{prep,scan,out} + wkv7_chunk_bwd_{prep,out} + reverse scan "
+                       "(per launch: the six-kernel step / 6)")
+        self.h2d = sum(a.nbytes for a in self.host)
+        self.d2h = 6 * BTHN * 4
+
+    def step(self):
+        _lib, P = self._lib, self._lib.P
+        st = P(self.torch.cuda.current_stream().cuda_stream)
+        r, w, k, v, a, b, dy = (P(t.data_ptr()) for t in self.x)
+        ws = P(self.ws.data_ptr())
+        _lib.call("rwkv_wkv7_train_forward_chunked", 0, r, w, k, v, a, b, None, P(self.y.data_ptr()), None,
+                  None, P(self.ck.data_ptr()), self.B, self.T, self.H, self.N, ws, self.ws_bytes, st)
+        _lib.call("rwkv_wkv7_backward_chunked", 0, r, w, k, v, a, b, None, P(self.ck.data_ptr()), dy, None,
+                  *(P(t.data_ptr()) for t in self.g), P(self.dh.data_ptr()), self.B, self.T, self.H, self.N,
+                  ws, self.ws_bytes, st)
+
+    def step_e2e(self):
+        for d, p in zip(self.x, self.pin):
+            d.copy_(p, non_blocking=True)
+        self.step()
+        for h, d in zip(self.pin_g, self.g):
+            h.copy_(d, non_blocking=True)
+
+    def cpu(self, seconds):
+        from oracle import oracle as O
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.wkv7_train(*self.host[:6], None, self.host[6])
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * self.B * self.T / dt, f"{n} full config-1 forward + backward passes ({n * self.B * self.T} tokens)"
 
 
 class GemvSuite:
@@ -477,7 +554,7 @@ def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head):
                                           f"step = {L} layers + head")
 
 
-WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "gemv": GemvSuite,
+WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "wkv7train": WKV7Train, "gemv": GemvSuite,
              "statetune": StateTune29B}
 
 
@@ -524,8 +601,11 @@ def run_reference(args, rank):
     cores = os.cpu_count() or 1
     O.set_threads(cores)
     wl = make_workload(args)
-    if wl.name == "wkv7":
-        wl.host = config1_inputs(np.random.default_rng(SEED))
+    if wl.name in ("wkv7", "wkv7train"):
+        rng = np.random.default_rng(SEED)
+        wl.host = config1_inputs(rng)
+        if wl.name == "wkv7train":
+            wl.host.append(rng.standard_normal(wl.host[0].shape).astype(np.float32))
     per = []
     sample = ""
     for i in range(args.warmup + args.steps):
@@ -621,7 +701,7 @@ def main():
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32" if wl.name in ("wkv7", "statetune") else "u4 x f16 -> f32", "data": "synthetic",
+        "dtype": "f32" if wl.name in ("wkv7", "wkv7train", "statetune") else "u4 x f16 -> f32", "data": "synthetic",
         "config": {"workload": wl.name, "l2": l2_note, "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
