@@ -32,10 +32,15 @@ __device__ __forceinline__ int scan_a_index(int k, int c) {
 
 // ------------------------------------------------------------ tensor cores
 
+// x = hi + lo, both rounded to TF32 (10 mantissa bits) to nearest by adding
+// half a TF32 ulp to the bit pattern and masking: hi*hi + hi*lo + lo*hi then
+// carries x to ~2^-22 relative, unbiased.  Integer ops rather than
+// cvt.rna.tf32: the conversion made the 3xTF32 k-step ~1.5x slower on this
+// GPU (measured); truncating instead of rounding biases the sums.
+__device__ __forceinline__ uint32_t tf32_rn(uint32_t bits) { return (bits + 0x1000u) & 0xffffe000u; }
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
-    const float rest = x - __uint_as_float(hi);
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(rest));
+    hi = tf32_rn(__float_as_uint(x));
+    lo = tf32_rn(__float_as_uint(x - __uint_as_float(hi)));
 }
 // D(16x8) += A(16x8, row) * B(8x8, col), m16n8k8 tf32 fragments:
 // a0 = A[g][t], a1 = A[g+8][t], a2 = A[g][t+4], a3 = A[g+8][t+4];
