@@ -93,23 +93,23 @@ __device__ __forceinline__ void run_mm(const MM (&jobs)[NJ]) {
 
 // Stage the listed token tensors of the chunk ([t][channel], row stride
 // CP; NULL pointers are skipped), every load before the first store.
-template <typename T, int NT>
+template <typename T, int NT, int NTH = CT>
 __device__ __forceinline__ void stage_tokens(float* const (&dst)[NT], const T* const (&src)[NT], int bi,
                                              int hi, int H, int T_, int t0) {
-    constexpr int PER = CL * CN / CT;
+    constexpr int PER = CL * CN / NTH;
     T l[NT][PER];
 #pragma unroll
     for (int n = 0; n < NT; n++)
 #pragma unroll
         for (int i = 0; i < PER; i++) {
-            const int e = threadIdx.x + CT * i, tl = e / CN, c = e % CN;
+            const int e = threadIdx.x + NTH * i, tl = e / CN, c = e % CN;
             if (src[n]) l[n][i] = src[n][(((size_t)bi * T_ + t0 + tl) * H + hi) * CN + c];
         }
 #pragma unroll
     for (int n = 0; n < NT; n++)
 #pragma unroll
         for (int i = 0; i < PER; i++) {
-            const int e = threadIdx.x + CT * i, tl = e / CN, c = e % CN;
+            const int e = threadIdx.x + NTH * i, tl = e / CN, c = e % CN;
             if (src[n]) dst[n][tl * CP + c] = to_f(l[n][i]);
         }
 }
@@ -294,6 +294,8 @@ wkv7_chunk_bwd_prep_kernel(const T* __restrict__ r, const T* __restrict__ w, con
 
 // ------------------------------------------------------------ out
 
+constexpr int BT = 512;   // threads of the out kernel (16 warps: its products are latency bound)
+
 struct BOutSmem {
     float rr[CL][CP], ww[CL][CP], kk[CL][CP], vv[CL][CP], aa[CL][CP], bb[CL][CP], dd[CL][CP];
     float c[CL + 1][CN], dsuf[CL][CN];
@@ -317,7 +319,9 @@ struct BOutSmem {
 template <typename T>
 __device__ void chunk_bwd_tokens(BOutSmem& sm, float (*buf)[CN + 1], T* dr, T* dw, T* dk, T* dv, T* da,
                                  T* db, size_t base, int H) {
-    const int tid = threadIdx.x, rr = tid >> 2, c0 = 16 * (tid & 3);
+    // threads 0-255 work (row, 16 columns); the others only take the barriers
+    const int tid = threadIdx.x, rr = (tid >> 2) & (CN - 1), c0 = 16 * (tid & 3);
+    const bool act = tid < 4 * CN;
     float D[16], Sp[16], Sn[16];
 #pragma unroll
     for (int j = 0; j < 16; j++) D[j] = sm.Q[rr][c0 + j];
@@ -351,7 +355,7 @@ __device__ void chunk_bwd_tokens(BOutSmem& sm, float (*buf)[CN + 1], T* dr, T* d
         sa = group_sum<4>(sa);
         e = group_sum<4>(e);
         dvr = group_sum<4>(dvr);
-        if ((tid & 3) == 0) dv[out(t, rr)] = from_f<T>(dvr);
+        if (act && (tid & 3) == 0) dv[out(t, rr)] = from_f<T>(dvr);
 #pragma unroll
         for (int j = 0; j < 16; j++) {
             const int c = c0 + j;
@@ -368,7 +372,7 @@ __device__ void chunk_bwd_tokens(BOutSmem& sm, float (*buf)[CN + 1], T* dr, T* d
                 else if (q == 2) x = Sp[j] * e;
                 else if (q == 3) x = D[j] * sa;
                 else x = Sp[j] * D[j];
-                buf[rr][c0 + j] = x;
+                if (act) buf[rr][c0 + j] = x;
             }
             __syncthreads();
             if (tid < CN) {
@@ -385,7 +389,7 @@ __device__ void chunk_bwd_tokens(BOutSmem& sm, float (*buf)[CN + 1], T* dr, T* d
 }
 
 template <typename T>
-__global__ void __launch_bounds__(CT)
+__global__ void __launch_bounds__(BT)
 wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* __restrict__ k,
                           const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
                           const T* __restrict__ dy, const float* __restrict__ h_in,
@@ -401,19 +405,19 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
         const float* S0g = ch > 0 ? h_ckpt + ((size_t)bh * NC + ch - 1) * CN * CN
                                   : (h_in ? h_in + (size_t)bh * CN * CN : nullptr);
         const float4* Qg = reinterpret_cast<const float4*>(Qws + ((size_t)bh * NC + ch) * CN * CN);
-        float4 s4[4], q4[4];
+        float4 s4[CN * CN / 4 / BT], q4[CN * CN / 4 / BT];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            s4[i] = S0g ? reinterpret_cast<const float4*>(S0g)[tid + CT * i] : make_float4(0.f, 0.f, 0.f, 0.f);
-            q4[i] = Qg[tid + CT * i];
+        for (int i = 0; i < CN * CN / 4 / BT; i++) {
+            s4[i] = S0g ? reinterpret_cast<const float4*>(S0g)[tid + BT * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            q4[i] = Qg[tid + BT * i];
         }
         float* const dst[7] = {&sm.rr[0][0], &sm.ww[0][0], &sm.kk[0][0], &sm.vv[0][0],
                                &sm.aa[0][0], &sm.bb[0][0], &sm.dd[0][0]};
         const T* const src[7] = {r, w, k, v, a, b, dy};
-        stage_tokens<T, 7>(dst, src, bi, hi, H, T_, t0);
+        stage_tokens<T, 7, BT>(dst, src, bi, hi, H, T_, t0);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int p = tid + CT * i, row = p >> 4, c4 = (p & 15) * 4;
+        for (int i = 0; i < CN * CN / 4 / BT; i++) {
+            const int p = tid + BT * i, row = p >> 4, c4 = (p & 15) * 4;
             *reinterpret_cast<float4*>(&sm.S[row][c4]) = s4[i];
             *reinterpret_cast<float4*>(&sm.Q[row][c4]) = q4[i];
         }
@@ -430,7 +434,7 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
     }
 
     suffix_decay(sm.dsuf, sm.ww);
-    for (int e = tid; e < CL * CN; e += CT) {
+    for (int e = tid; e < CL * CN; e += BT) {
         const int t = e / CN, c = e % CN;
         const float ct = sm.c[t + 1][c], c16 = sm.c[CL][c];
         sm.At[t][c] = sm.aa[t][c] * sm.c[t][c];
@@ -463,16 +467,16 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
         run_mm<CN>(jobs);
     }
     __syncthreads();
-    for (int e = tid; e < CL * CL; e += CT) {
+    for (int e = tid; e < CL * CL; e += BT) {
         const int j = e / CL, t = e % CL;
         if (j >= t) { sm.Mb[j][t] = 0.f; sm.Mk[j][t] = 0.f; }
         if (j > t) { sm.Nb[j][t] = 0.f; sm.Nk[j][t] = 0.f; }
     }
     __syncthreads();
-    // warps 2-7 beside the Z chain: X += V M_k, F += DY N_b^T, G2 += DY N_k^T (K = 16)
+    // warps 2.. beside the Z chain: X += V M_k, F += DY N_b^T, G2 += DY N_k^T (K = 16)
     if ((tid >> 5) >= 2) {
         const int warp = (tid >> 5) - 2, lane = tid & 31;
-        for (int tile = warp; tile < 24; tile += 6) {
+        for (int tile = warp; tile < 24; tile += BT / 32 - 2) {
             const int p = tile >> 3, tt = tile & 7, m0 = (tt >> 1) * 16, n0 = (tt & 1) * 8;
             float (*C)[LP] = p == 0 ? sm.X : p == 1 ? sm.F : sm.G2;
             float d[4];
@@ -506,7 +510,7 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
     __syncthreads();
     // masked copies: Lm[0..3] [j][t] for j <= t (udy, vdy) / j < t (ue, ve);
     // Lm[4..7] [m][t] = P[t][m] for m >= t (vdy, udy) / m > t (ve, ue)
-    for (int e = tid; e < CL * CL; e += CT) {
+    for (int e = tid; e < CL * CL; e += BT) {
         const int x = e / CL, t = e % CL;
         sm.Lm[0][x][t] = x <= t ? sm.Pudy[x][t] : 0.f;
         sm.Lm[1][x][t] = x <= t ? sm.Pvdy[x][t] : 0.f;
@@ -539,13 +543,14 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
         run_mm<CL>(jobs);
     }
     __syncthreads();
-    // outputs; thread = (channel, 4 tokens)
+    // outputs; thread = (channel, CL / (BT / 64) tokens)
     {
-        const int i = tid & (CN - 1), tq = tid >> 6;
+        constexpr int TG = BT / CN;   // token groups
+        const int i = tid & (CN - 1), tq = tid / CN;
         const float c16 = sm.c[CL][i];
 #pragma unroll
-        for (int u = 0; u < CL / 4; u++) {
-            const int t = tq + 4 * u;
+        for (int u = 0; u < CL / TG; u++) {
+            const int t = tq + TG * u;
             const float ct = sm.c[t + 1][i];
             dr[out(t, i)] = from_f<T>(ct * sm.dR[i][t]);
             da[out(t, i)] = from_f<T>(sm.c[t][i] * sm.dA[i][t]);
@@ -613,7 +618,7 @@ int launch_wkv7_chunk_bwd(int dtype, const void* r, const void* w, const void* k
         if (int rc = check_launch("wkv7_chunk_bwd_prep_kernel")) return rc;
         wkv7_chunk_scan_kernel<<<dim3(B * H, CN / SR), ST, 0, st>>>(dh_out, Aws, Cws, Qws, dh_in, nullptr, NC, 1);
         if (int rc = check_launch("wkv7_chunk_scan_kernel")) return rc;
-        out<<<dim3(NC, B * H), CT, sizeof(BOutSmem), st>>>(
+        out<<<dim3(NC, B * H), BT, sizeof(BOutSmem), st>>>(
             (const T*)r, (const T*)w, (const T*)k, (const T*)v, (const T*)a, (const T*)b, (const T*)dy, h_in,
             h_ckpt, Qws, (T*)dr, (T*)dw, (T*)dk, (T*)dv, (T*)da, (T*)db, T_, H, NC);
         return check_launch("wkv7_chunk_bwd_out_kernel");

@@ -251,6 +251,43 @@ def wkv7Train(r, w, k, v, a, b):
     return wkv7TrainWithState(r, w, k, v, a, b, None)[0]
 
 
+def wkv7Steps(r, w, k, v, a, b, hIn=None):
+    """Several differentiable steps (WKV7Step.swift:79-100): r..b [B, T, H, D]
+    for any T >= 1, hIn [B, H, D, D] or None (zeros); returns (out [B, T, H, D]
+    fp32, hOut [B, H, D, D]), differentiable w.r.t. all seven inputs.  The
+    reference unrolls MLX ops; here T is padded to a multiple of CHUNK with
+    identity steps (w = 1, r = k = v = a = b = 0: the state passes unchanged,
+    the padded outputs are 0) and the WKV-7 training kernels run forward and
+    backward, so the gradients are those of the unpadded steps."""
+    if r.dim() != 4:
+        raise ValueError(f"wkv7Steps expects [B,T,H,D], got {tuple(r.shape)}")
+    B, T, H, D = _check_seq(r, "wkv7Steps")
+    xs = [x.to(torch.float32) for x in (r, w, k, v, a, b)]
+    for x in xs[1:]:
+        if tuple(x.shape) != (B, T, H, D):
+            raise ValueError(f"wkv7Steps: every input must be [B,T,H,D] = {[B, T, H, D]}")
+    pad = (-T) % WKV7_CHUNK
+    if pad:
+        xs = [torch.cat([x, torch.full((B, pad, H, D), 1.0 if i == 1 else 0.0, device=x.device,
+                                       dtype=torch.float32)], dim=1) for i, x in enumerate(xs)]
+    out, h_out = wkv7TrainWithState(*xs, hIn)
+    return out[:, :T], h_out
+
+
+def wkv7Step(r, w, k, v, a, b, hIn=None):
+    """One differentiable step (WKV7Step.swift:45-67): r..b [B, H, D] (out
+    [B, H, D]) or [B, 1, H, D] (out [B, 1, H, D]); hIn [B, H, D, D] or None.
+    Returns (out fp32, hOut [B, H, D, D])."""
+    if r.dim() == 4:
+        if r.shape[1] != 1:
+            raise ValueError(f"wkv7Step takes exactly one token, for several use wkv7Steps (T={r.shape[1]})")
+        return wkv7Steps(r, w, k, v, a, b, hIn)
+    if r.dim() != 3:
+        raise ValueError(f"wkv7Step expects [B,H,D] or [B,1,H,D], got {tuple(r.shape)}")
+    out, h_out = wkv7Steps(*(x.unsqueeze(1) for x in (r, w, k, v, a, b)), hIn)
+    return out[:, 0], h_out
+
+
 def wkv7StepForward(r, w, k, v, a, b, h):
     """One token (WKV7DecodeKernels.swift:157-173): r..b [H, S] (or [rows, H, S]),
     h [H, S, S] (or [rows, H, S, S]).  Returns (out, h') fp32; h is not modified."""

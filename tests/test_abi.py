@@ -86,3 +86,19 @@ def test_sb6_and_sym_shape_rules():
 def test_tail_requires_warp_multiple_head():
     args = [FAKE] * 9 + [1, 2, 48, ctypes.c_float(64e-5), None]
     assert _lib.status("rwkv_wkv_tail", *args) == _lib.E_UNSUPPORTED
+
+
+def test_wkv7_step_api_validates_shapes_before_any_launch():
+    """wkv7Step / wkv7Steps reject bad ranks and lengths on the host (the
+    reference's preconditions, WKV7Step.swift:49-57, :85)."""
+    import torch
+    from swiftrwkv_b200 import kernel as K
+    x3 = torch.zeros(1, 2, 64)
+    with pytest.raises(ValueError, match="exactly one token"):
+        K.wkv7Step(*(torch.zeros(1, 2, 2, 64) for _ in range(6)))
+    with pytest.raises(ValueError, match="expects"):
+        K.wkv7Step(*(torch.zeros(64) for _ in range(6)))
+    with pytest.raises(ValueError, match="expects"):
+        K.wkv7Steps(*(x3 for _ in range(6)))
+    with pytest.raises(ValueError, match="every input"):
+        K.wkv7Steps(torch.zeros(1, 3, 2, 64), *(torch.zeros(1, 2, 2, 64) for _ in range(5)))
