@@ -131,6 +131,21 @@ class X070Oracle:
     def _mm(self, x, key):
         return self._a(x) @ self.w[key].T
 
+    def _proj(self, x, key):
+        """Projection with its optional LoRA adapter (X070Backbone.swift:746-752):
+        base + scale * (x A^T) B^T, adapter keys "<target>.lora_a" / ".lora_b" /
+        ".lora_scale" (LoRA.swift:118-127).  A and B are stored in fp16 like the
+        other dense matrices; z = scale * (x A^T) is rounded to the activation
+        type, where the runtime stores it."""
+        y = self._mm(x, key)
+        stem = key[:-len(".weight")]
+        A, B = self.w.get(stem + ".lora_a"), self.w.get(stem + ".lora_b")
+        if A is None or B is None:
+            return y
+        scale = float(np.asarray(self.w.get(stem + ".lora_scale", 1.0)).reshape(-1)[0])
+        z = self._a(scale * (self._a(x) @ A.T))
+        return y + z @ B.T
+
     @staticmethod
     def _ln(x, w, b, eps=1e-5):
         mean = x.mean(-1, keepdims=True)
@@ -151,9 +166,9 @@ class X070Oracle:
             xx = st["tshift"][L] - xl
             st["tshift"][L] = xl
             mix = {m: xl + xx * W[p + "x_" + m] for m in "rwkvag"}
-            r = self._mm(mix["r"], p + "r_proj.weight")
-            k = self._mm(mix["k"], p + "k_proj.weight")
-            v = self._mm(mix["v"], p + "v_proj.weight")
+            r = self._proj(mix["r"], p + "r_proj.weight")
+            k = self._proj(mix["k"], p + "k_proj.weight")
+            v = self._proj(mix["v"], p + "v_proj.weight")
             gate = self._mm(sig(self._mm(mix["g"], p + "g_lora_A.weight")), p + "g_lora_B.weight")
             if L == 0:
                 v_first = v.copy()
@@ -177,13 +192,13 @@ class X070Oracle:
             tail = O.wkv_tail(y.reshape(rows, D), r.astype(np.float32), k2.astype(np.float32),
                               v.astype(np.float32), W[p + "r_k"].reshape(D), W[p + "ln_x.weight"],
                               W[p + "ln_x.bias"], gate.astype(np.float32), H, S).astype(np.float64)
-            x = x + self._mm(tail, p + "o_proj.weight")
+            x = x + self._proj(tail, p + "o_proj.weight")
             cp = f"blocks.{L}.cmix."
             xl2 = self._ln(x, W[f"blocks.{L}.ln2.weight"], W[f"blocks.{L}.ln2.bias"])
             xx2 = st["cshift"][L] - xl2
             st["cshift"][L] = xl2
             xk = xl2 + xx2 * W[cp + "x_k"]
-            hk = np.maximum(self._mm(xk, cp + "key.weight"), 0.0)
-            x = x + self._mm(hk * hk, cp + "value.weight")
+            hk = np.maximum(self._proj(xk, cp + "key.weight"), 0.0)
+            x = x + self._proj(hk * hk, cp + "value.weight")
         xo = self._ln(x, W["ln_out.weight"], W["ln_out.bias"])
-        return self._mm(xo, "head.weight")
+        return self._proj(xo, "head.weight")

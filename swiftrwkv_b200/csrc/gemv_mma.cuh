@@ -58,6 +58,7 @@ struct GemvJob {
     void* y;
     int y_stride;
     const float* bias;    // per-output-row bias for ACT_DECAY / ACT_SIGMOID_BIAS
+    float alpha;          // ACT_SCALE factor
 };
 
 enum Act : int {
@@ -67,6 +68,7 @@ enum Act : int {
     ACT_SIGMOID = 3,       // sigmoid(v)                         (g branch, down)
     ACT_DECAY = 4,         // exp(-0.606531 * sigmoid(v + bias)) (w branch, up)
     ACT_SIGMOID_BIAS = 5,  // sigmoid(v + bias)                  (a / v branches, up)
+    ACT_SCALE = 6,         // alpha * v                          (LoRA adapter, down)
 };
 enum Out : int { OUT_F32 = 0, OUT_F16 = 1, OUT_ADD_F32 = 2 };
 
@@ -77,6 +79,7 @@ __device__ __forceinline__ void epilogue(const GemvJob& jb, int o, int n, float 
         case ACT_SIGMOID: v = 1.0f / (1.0f + expf(-v)); break;
         case ACT_DECAY: v = expf(-0.606531f * (1.0f / (1.0f + expf(-(v + jb.bias[o]))))); break;
         case ACT_SIGMOID_BIAS: v = 1.0f / (1.0f + expf(-(v + jb.bias[o]))); break;
+        case ACT_SCALE: v *= jb.alpha; break;
         default: break;
     }
     const int64_t idx = (int64_t)n * jb.y_stride + o;

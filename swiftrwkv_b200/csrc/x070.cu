@@ -63,6 +63,19 @@ struct QMat {
     int OUT = 0, IN = 0;
 };
 
+// A LoRA adapter on a projection (LoRA.swift:118-127, X070Backbone.swift:
+// 746-752): y = base(x) + scale * (x A^T) B^T with A [rank, IN], B [OUT, rank]
+// stored in fp16; active once A and B are both set with the same rank.
+struct Adapter {
+    __half* A = nullptr;
+    __half* B = nullptr;
+    int rank_a = 0, rank_b = 0;
+    float scale = 1.f;
+    bool on() const { return A && B && rank_a == rank_b; }
+};
+constexpr int LORA_MAX_RANK = 256;
+enum { AD_R, AD_K, AD_V, AD_O, AD_KEY, AD_VALUE, AD_N };
+
 struct LayerW {
     float *ln1w = nullptr, *ln1b = nullptr, *ln2w = nullptr, *ln2b = nullptr;
     float* coef6 = nullptr;  // [6, C]: r, w, k, v, a, g
@@ -72,6 +85,7 @@ struct LayerW {
     __half *wA = nullptr, *wB = nullptr, *aA = nullptr, *aB = nullptr;
     __half *gA = nullptr, *gB = nullptr, *vA = nullptr, *vB = nullptr;
     QMat r, k, v, o, key, value;
+    Adapter ad[AD_N];   // LoRA on r, k, v, o (tmix) and key, value (cmix)
 };
 
 struct X070 {
@@ -82,6 +96,9 @@ struct X070 {
     std::vector<void*> allocs;
     std::vector<LayerW> lw;
     QMat emb, head;
+    Adapter head_ad;             // LoRA on the head
+    void* lora_z = nullptr;      // [3][Rmax][LORA_MAX_RANK] adapter down outputs (activation type)
+    float* key_tmp = nullptr;    // [Rmax, F] cmix key pre-activation when it has an adapter
     float *ln0w, *ln0b, *lnow, *lnob;
     // state
     float *wkv, *tshift, *cshift;
@@ -248,7 +265,44 @@ struct X070 {
                    ? ok() : fail(RWKV_E_CUDA, "set_param: copy failed");
     }
 
+    void drop_graphs() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+    }
+    // "<target>.lora_a" [rank, IN], ".lora_b" [OUT, rank], ".lora_scale" [1]
+    // (the reference's adapter keys, LoRA.swift:170-200; scale = alpha / rank).
+    // A change invalidates the captured step graphs (the launch sequence changes).
+    int set_adapter(Adapter& a, const std::string& part, int IN, int OUT, bool key, const float* host, int64_t n) {
+        if (part == "scale") {
+            RWKV_REQUIRE(n == 1, RWKV_E_SHAPE, "set_param: lora_scale takes one value, got %lld", (long long)n);
+            a.scale = host[0];
+            drop_graphs();
+            return ok();
+        }
+        const bool isA = part == "a";
+        RWKV_REQUIRE(isA || part == "b", RWKV_E_SHAPE, "set_param: unknown adapter tensor 'lora_%s'", part.c_str());
+        const int64_t dim = isA ? IN : OUT;
+        RWKV_REQUIRE(n > 0 && n % dim == 0, RWKV_E_SHAPE, "set_param: lora_%s size %lld is not rank x %lld",
+                     part.c_str(), (long long)n, (long long)dim);
+        const int rank = (int)(n / dim);
+        RWKV_REQUIRE(rank % 16 == 0 && rank <= LORA_MAX_RANK, RWKV_E_UNSUPPORTED,
+                     "set_param: adapter rank %d must be a multiple of 16, at most %d", rank, LORA_MAX_RANK);
+        __half*& dst = isA ? a.A : a.B;
+        int& rk = isA ? a.rank_a : a.rank_b;
+        if (!dst || rk != rank) {
+            dst = alloc<__half>((size_t)rank * dim);
+            weight_bytes += (int64_t)rank * dim * 2;
+        }
+        rk = rank;
+        if (!lora_z) lora_z = alloc<char>((size_t)3 * Rmax * LORA_MAX_RANK * act_bytes);
+        if (key && !key_tmp) key_tmp = alloc<float>((size_t)Rmax * F);
+        RWKV_REQUIRE(!alloc_failed && dst && lora_z && (!key || key_tmp), RWKV_E_CUDA, "set_param: adapter allocation failed");
+        drop_graphs();
+        return upload_h(dst, n, host, n);
+    }
+
     int set_param(const std::string& name, const float* host, int64_t n) {
+        if (name.compare(0, 10, "head.lora_") == 0) return set_adapter(head_ad, name.substr(10), C, V, false, host, n);
         if (name == "emb.weight") return upload_q(emb, host, n);
         if (name == "head.weight") return upload_q(head, host, n);
         if (name == "ln0.weight") return upload_f(ln0w, C, host, n);
@@ -290,6 +344,14 @@ struct X070 {
         if (s == "tmix.o_proj.weight") return upload_q(w.o, host, n);
         if (s == "cmix.key.weight") return upload_q(w.key, host, n);
         if (s == "cmix.value.weight") return upload_q(w.value, host, n);
+        static const char* adn[AD_N] = {"tmix.r_proj", "tmix.k_proj", "tmix.v_proj", "tmix.o_proj", "cmix.key",
+                                        "cmix.value"};
+        for (int t = 0; t < AD_N; t++) {
+            const std::string pre = std::string(adn[t]) + ".lora_";
+            if (s.compare(0, pre.size(), pre) == 0)
+                return set_adapter(w.ad[t], s.substr(pre.size()), t == AD_VALUE ? F : C, t == AD_KEY ? F : C,
+                                   t == AD_KEY, host, n);
+        }
         return fail(RWKV_E_SHAPE, "set_param: unknown parameter '%s'", name.c_str());
     }
 
@@ -421,6 +483,40 @@ struct X070 {
         return j;
     }
 
+    // LoRA adapters of up to three projections sharing one down and one up
+    // launch: z = scale * (x A^T) (activation type), y += z B^T.
+    struct LoraJob {
+        const Adapter* ad;
+        const void* x;
+        int xs, IN, OUT;
+        float* y;
+        int ys;
+    };
+    template <typename A>
+    int lora_apply(const LoraJob* lj, int n, int R, cudaStream_t st) {
+        GemvJobs D{}, U{};
+        int nd = 0;
+        for (int i = 0; i < n; i++) {
+            const Adapter& ad = *lj[i].ad;
+            if (!ad.on()) continue;
+            A* z = (A*)lora_z + (size_t)nd * Rmax * LORA_MAX_RANK;
+            GemvJob d = hjob(ad.A, ad.rank_a, lj[i].IN, lj[i].x, lj[i].xs, ACT_SCALE, f16act ? OUT_F16 : OUT_F32, z,
+                             ad.rank_a);
+            d.alpha = ad.scale;
+            D.j[nd] = d;
+            U.j[nd] = hjob(ad.B, lj[i].OUT, ad.rank_a, z, ad.rank_a, ACT_NONE, OUT_ADD_F32, lj[i].y, lj[i].ys);
+            nd++;
+        }
+        if (nd == 0) return RWKV_OK;
+        int rc = gemv(1, D, nd, R, st);
+        if (rc) return rc;
+        mark("lora_adapter_down");
+        rc = gemv(1, U, nd, R, st);
+        if (rc) return rc;
+        mark("lora_adapter_up");
+        return RWKV_OK;
+    }
+
     template <typename A>
     int step_body(int R, cudaStream_t st) {
         const size_t RC = (size_t)R * C;
@@ -452,6 +548,11 @@ struct X070 {
             J.j[2] = qjob(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
             if ((rc = gemv(0, J, 3, R, st))) return rc;
             mark("gemm_rkv");
+            {
+                const LoraJob lj[3] = {{&w.ad[AD_R], M(0), C, C, C, r, C}, {&w.ad[AD_K], M(2), C, C, C, k, C},
+                                       {&w.ad[AD_V], M(3), C, C, C, v, C}};
+                if ((rc = lora_apply<A>(lj, 3, R, st))) return rc;
+            }
             // low-rank down: w (tanh), a, g (sigmoid), v
             GemvJobs D{};
             int nd = 0;
@@ -481,6 +582,10 @@ struct X070 {
             O.j[0] = qjob(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C);
             if ((rc = gemv(0, O, 1, R, st))) return rc;
             mark("gemm_o");
+            {
+                const LoraJob lj[1] = {{&w.ad[AD_O], tail, C, C, C, x, C}};
+                if ((rc = lora_apply<A>(lj, 1, R, st))) return rc;
+            }
             if ((rc = row_launch([&]<int GV>() {
                      return launch_pdl(x070_cmix_in_kernel<A, GV>, R, GLUE_T, 0, st, (const float*)x,
                                        (const float*)w.ln2w, (const float*)w.ln2b, cs,
@@ -489,13 +594,31 @@ struct X070 {
                 return rc;
             mark("cmix_in");
             GemvJobs K{};
-            K.j[0] = qjob(w.key, xk, C, ACT_RELU2, aout, ffn, F);
-            if ((rc = gemv(0, K, 1, R, st))) return rc;
-            mark("gemm_key");
+            if (!w.ad[AD_KEY].on()) {
+                K.j[0] = qjob(w.key, xk, C, ACT_RELU2, aout, ffn, F);
+                if ((rc = gemv(0, K, 1, R, st))) return rc;
+                mark("gemm_key");
+            } else {
+                // the adapter is added before relu^2: pre-activation in fp32, then the activation
+                K.j[0] = qjob(w.key, xk, C, ACT_NONE, OUT_F32, key_tmp, F);
+                if ((rc = gemv(0, K, 1, R, st))) return rc;
+                mark("gemm_key");
+                const LoraJob lj[1] = {{&w.ad[AD_KEY], xk, C, C, F, key_tmp, F}};
+                if ((rc = lora_apply<A>(lj, 1, R, st))) return rc;
+                const int n = R * F;
+                if ((rc = pdl_check(launch_pdl(x070_relu2_cast_kernel<A>, std::min((n + 255) / 256, 4 * sm_count), 256, 0,
+                                               st, (const float*)key_tmp, (A*)ffn, n), "x070_relu2_cast_kernel")))
+                    return rc;
+                mark("relu2");
+            }
             GemvJobs Vv{};
             Vv.j[0] = qjob(w.value, ffn, F, ACT_NONE, OUT_ADD_F32, x, C);
             if ((rc = gemv(0, Vv, 1, R, st))) return rc;
             mark("gemm_value");
+            {
+                const LoraJob lj[1] = {{&w.ad[AD_VALUE], ffn, F, F, C, x, C}};
+                if ((rc = lora_apply<A>(lj, 1, R, st))) return rc;
+            }
         }
         if ((rc = row_launch([&]<int GV>() {
                  return launch_pdl(x070_ln_out_kernel<A, GV>, R, GLUE_T, 0, st, (const float*)x,
@@ -507,6 +630,10 @@ struct X070 {
         Hd.j[0] = qjob(head, lnout, C, ACT_NONE, OUT_F32, logits, V);
         if ((rc = gemv(0, Hd, 1, R, st))) return rc;
         mark("gemm_head");
+        {
+            const LoraJob lj[1] = {{&head_ad, lnout, C, C, V, logits, V}};
+            if ((rc = lora_apply<A>(lj, 1, R, st))) return rc;
+        }
         if ((rc = pdl_check(launch_pdl(x070_argmax_kernel, dim3((V + ARGMAX_SLICE - 1) / ARGMAX_SLICE, R), GLUE_T, 0,
                                        st, (const float*)logits, V, amax_keys), "x070_argmax_kernel")))
             return rc;
@@ -613,7 +740,14 @@ struct X070 {
         return rc;
     }
 
-    int launches_per_step() const { return 1 + L * 10 + 4; }
+    int launches_per_step() const {
+        int n = 1 + L * 10 + 4 + (head_ad.on() ? 2 : 0);
+        for (const LayerW& w : lw) {
+            if (w.ad[AD_R].on() || w.ad[AD_K].on() || w.ad[AD_V].on()) n += 2;
+            n += (w.ad[AD_O].on() ? 2 : 0) + (w.ad[AD_KEY].on() ? 3 : 0) + (w.ad[AD_VALUE].on() ? 2 : 0);
+        }
+        return n;
+    }
 };
 
 }  // namespace rwkv

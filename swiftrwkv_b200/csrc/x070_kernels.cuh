@@ -431,4 +431,17 @@ gemv_cc_kernel(const GemvJobs jobs, int R) {
     }
 }
 
+// relu(h)^2 into the activation type: the cmix key output when a LoRA
+// adapter is added before the activation (n = rows * ffn).
+template <typename A>
+__global__ void __launch_bounds__(256) x070_relu2_cast_kernel(const float* __restrict__ h, A* __restrict__ out,
+                                                              int n) {
+    pdl_trigger();
+    pdl_wait();
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < n; i += gridDim.x * 256) {
+        const float v = fmaxf(h[i], 0.f);
+        out[i] = from_f<A>(v * v);
+    }
+}
+
 }  // namespace rwkv
