@@ -301,7 +301,14 @@ int rwkv_x070_create(const rwkv_x070_config* cfg, rwkv_x070_t* out);
 int rwkv_x070_destroy(rwkv_x070_t model);
 /* Parameter by its reference name ("emb.weight", "blocks.3.tmix.r_proj.weight",
  * ...), from a HOST fp32 array of n elements; the big matrices are quantised
- * on the device (rwkv_q_quantize), the low-rank matrices stored fp16. */
+ * on the device (rwkv_q_quantize), the low-rank matrices stored fp16.
+ * LoRA adapters (Sources/RWKVGen/LoRA.swift:118-127, applied as in
+ * X070Backbone.proj, X070Backbone.swift:746-752: base + scale (x A^T) B^T) use
+ * the reference's keys "<target>.lora_a" [rank, IN] and "<target>.lora_b"
+ * [OUT, rank], plus "<target>.lora_scale" [1] (alpha / rank), for target
+ * "blocks.L.tmix.{r,k,v,o}_proj", "blocks.L.cmix.{key,value}" or "head";
+ * rank a multiple of 16, at most 256; stored fp16.  Changing an adapter drops
+ * the captured step graphs. */
 int rwkv_x070_set_param(rwkv_x070_t model, const char* name, const float* host, int64_t n);
 /* Random init with the x070 recipe (Sources/RWKVGen/Training/X070Init.swift:79-206),
  * drawn on the device from `seed`. */
