@@ -543,7 +543,7 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
         run_mm<CL>(jobs);
     }
     __syncthreads();
-    // outputs; thread = (channel, CL / (BT / 64) tokens)
+    // outputs but dw; thread = (channel, CL / (BT / 64) tokens)
     {
         constexpr int TG = BT / CN;   // token groups
         const int i = tid & (CN - 1), tq = tid / CN;
@@ -557,32 +557,49 @@ wkv7_chunk_bwd_out_kernel(const T* __restrict__ r, const T* __restrict__ w, cons
             dk[out(t, i)] = from_f<T>((c16 * sm.QV[i][t] + sm.Xk[i][t]) / ct);
             db[out(t, i)] = from_f<T>((c16 * sm.QU[i][t] + sm.Xb[i][t]) / ct);
             dv[out(t, i)] = from_f<T>(sm.G2[i][t]);
-            // dw_t = c_{t-1} d_t (q0 + sum_{j<t} b^_j Q^T u_j + k^_j Q^T v_j)
-            //      + (1 / w_t) (sum_{m>=t} r~_m S_0^T dy_m + sum_{m>t} a~_m S_0^T e_m
-            //        + sum_{j<t} [b^_j (sum_{m>=t} (u_j.dy_m) r~_m + sum_{m>t} (u_j.e_m) a~_m)
-            //                   + k^_j (sum_{m>=t} (v_j.dy_m) r~_m + sum_{m>t} (v_j.e_m) a~_m)])
-            float s1 = sm.q0[i];
-            for (int j = 0; j < t; j++) s1 = fmaf(sm.Bh[j][i], sm.QU[i][j], fmaf(sm.Kh[j][i], sm.QV[i][j], s1));
-            float s2 = 0.f;
-            for (int m = CL - 1; m >= t; m--) {
-                s2 = fmaf(sm.Rt[m][i], sm.SDY[i][m], s2);
-                if (m > t) s2 = fmaf(sm.At[m][i], sm.SE[i][m], s2);
+        }
+    }
+    // dw_t = c_{t-1} d_t (q0 + sum_{j<t} b^_j Q^T u_j + k^_j Q^T v_j)
+    //      + (1 / w_t) (sum_{m>=t} r~_m S_0^T dy_m + sum_{m>t} a~_m S_0^T e_m
+    //        + sum_{j<t} [b^_j (sum_{m>=t} (u_j.dy_m) r~_m + sum_{m>t} (u_j.e_m) a~_m)
+    //                   + k^_j (sum_{m>=t} (v_j.dy_m) r~_m + sum_{m>t} (v_j.e_m) a~_m)])
+    // Thread = (channel i, rows j = 2g, 2g + 1 of the dot matrices), 8 per
+    // channel in one warp; t runs down so that the inner sums over m are
+    // running suffix sums; the 8 partial j-sums meet by shuffles.
+    {
+        static_assert(BT == 8 * CN, "eight threads per channel");
+        const int i = 4 * (tid >> 5) + ((tid & 31) >> 3), jg = tid & 7, j0 = 2 * jg, j1 = j0 + 1;
+        const float bh0 = sm.Bh[j0][i], bh1 = sm.Bh[j1][i], kh0 = sm.Kh[j0][i], kh1 = sm.Kh[j1][i];
+        float s1[CL];   // prefix sums over j (the lane with jg == 0 uses them)
+        s1[0] = sm.q0[i];
+#pragma unroll
+        for (int t = 0; t + 1 < CL; t++) s1[t + 1] = fmaf(sm.Bh[t][i], sm.QU[i][t], fmaf(sm.Kh[t][i], sm.QV[i][t], s1[t]));
+        float sb0 = 0.f, sb1 = 0.f, sk0 = 0.f, sk1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int t = CL - 1; t >= 0; t--) {
+            const float rt = sm.Rt[t][i];
+            sb0 = fmaf(sm.Pudy[j0][t], rt, sb0);
+            sk0 = fmaf(sm.Pvdy[j0][t], rt, sk0);
+            sb1 = fmaf(sm.Pudy[j1][t], rt, sb1);
+            sk1 = fmaf(sm.Pvdy[j1][t], rt, sk1);
+            if (t + 1 < CL) {
+                const float at = sm.At[t + 1][i];
+                sb0 = fmaf(sm.Pue[j0][t + 1], at, sb0);
+                sk0 = fmaf(sm.Pve[j0][t + 1], at, sk0);
+                sb1 = fmaf(sm.Pue[j1][t + 1], at, sb1);
+                sk1 = fmaf(sm.Pve[j1][t + 1], at, sk1);
             }
-            for (int j = 0; j < t; j++) {
-                float xb = 0.f, xk = 0.f;
-                for (int m = CL - 1; m >= t; m--) {
-                    const float rm = sm.Rt[m][i];
-                    xb = fmaf(sm.Pudy[j][m], rm, xb);
-                    xk = fmaf(sm.Pvdy[j][m], rm, xk);
-                    if (m > t) {
-                        const float am = sm.At[m][i];
-                        xb = fmaf(sm.Pue[j][m], am, xb);
-                        xk = fmaf(sm.Pve[j][m], am, xk);
-                    }
-                }
-                s2 = fmaf(sm.Bh[j][i], xb, fmaf(sm.Kh[j][i], xk, s2));
+            float x = 0.f;
+            if (j0 < t) x = fmaf(bh0, sb0, fmaf(kh0, sk0, x));
+            if (j1 < t) x = fmaf(bh1, sb1, fmaf(kh1, sk1, x));
+            x += __shfl_xor_sync(0xffffffffu, x, 1);
+            x += __shfl_xor_sync(0xffffffffu, x, 2);
+            x += __shfl_xor_sync(0xffffffffu, x, 4);
+            if (jg == 0) {
+                s2 = fmaf(rt, sm.SDY[i][t], s2);
+                if (t + 1 < CL) s2 = fmaf(sm.At[t + 1][i], sm.SE[i][t + 1], s2);
+                dw[out(t, i)] = from_f<T>(sm.c[t][i] * sm.dsuf[t][i] * s1[t] + (s2 + x) / sm.ww[t][i]);
             }
-            dw[out(t, i)] = from_f<T>(sm.c[t][i] * sm.dsuf[t][i] * s1 + s2 / sm.ww[t][i]);
         }
     }
 }
