@@ -193,6 +193,8 @@ wkv7_chunk_prep_kernel(const T* __restrict__ w, const T* __restrict__ k, const T
 
 // ------------------------------------------------------------ out
 
+constexpr int FT = 512;   // threads of the out kernel (two CTAs per SM)
+
 struct OutSmem {
     float rr[CL][CN], ww[CL][CN], kk[CL][CN], aa[CL][CN], bb[CL][CN];
     float vv[CL * CQ];                                     // [token][dv] (column-read)
@@ -225,7 +227,7 @@ __device__ __forceinline__ void tile_64x16(float (*C)[LP], const float (*A)[LP],
 
 // The chunk's outputs from its start state: CTA = (chunk, head), all 64 rows.
 template <typename T>
-__global__ void __launch_bounds__(CT)
+__global__ void __launch_bounds__(FT, 2)
 wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T* __restrict__ k,
                       const T* __restrict__ v, const T* __restrict__ a, const T* __restrict__ b,
                       const float* __restrict__ S0ws, T* __restrict__ y, float* __restrict__ sa_out,
@@ -238,13 +240,13 @@ wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T*
     {
         // start state (16 floats per thread) with the chunk inputs: one wait on memory
         const float4* S0g = reinterpret_cast<const float4*>(S0ws + ((size_t)bh * NC + ch) * CN * CN);
-        float4 s4[4];
+        float4 s4[CN * CN / 4 / FT];
 #pragma unroll
-        for (int i = 0; i < 4; i++) s4[i] = S0g[tid + CT * i];
-        stage_chunk<T, CN>(sm.rr, sm.ww, sm.kk, sm.aa, sm.bb, sm.vv, CQ, r, w, k, v, a, b, bi, hi, H, T_, t0, 0);
+        for (int i = 0; i < CN * CN / 4 / FT; i++) s4[i] = S0g[tid + FT * i];
+        stage_chunk<T, CN, FT>(sm.rr, sm.ww, sm.kk, sm.aa, sm.bb, sm.vv, CQ, r, w, k, v, a, b, bi, hi, H, T_, t0, 0);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int p = tid + CT * i, rr = p >> 4, c4 = (p & 15) * 4;
+        for (int i = 0; i < CN * CN / 4 / FT; i++) {
+            const int p = tid + FT * i, rr = p >> 4, c4 = (p & 15) * 4;
             sm.S[rr][c4] = s4[i].x; sm.S[rr][c4 + 1] = s4[i].y; sm.S[rr][c4 + 2] = s4[i].z; sm.S[rr][c4 + 3] = s4[i].w;
         }
     }
@@ -254,6 +256,8 @@ wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T*
 
     if (cmin < GUARD) {
         // token by token on all 64 rows: thread = (row, 16 columns), 4 threads per row
+        // (threads 0-255; no barrier follows)
+        if (tid >= 4 * CN) return;
         const int rr = tid >> 2, c0 = 16 * (tid & 3);
         for (int t = 0; t < CL; t++) {
             float sa = 0.f;
@@ -278,7 +282,7 @@ wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T*
         return;
     }
 
-    for (int e = tid; e < CL * CN; e += CT) {
+    for (int e = tid; e < CL * CN; e += FT) {
         const int t = e / CN, c = e % CN;
         const float ct = sm.c[t + 1][c];
         sm.At[t][c] = sm.aa[t][c] * sm.c[t][c];
@@ -288,7 +292,7 @@ wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T*
     }
     __syncthreads();
     // [Bh; Kh; S] (96 x 64) x [A~; R~]^T (64 x 32): 6 x 4 = 24 tiles, 3 per warp
-    for (int tile = warp; tile < 24; tile += CT / 32) {
+    for (int tile = warp; tile < 24; tile += FT / 32) {
         const int mt = tile >> 2, nt = tile & 3;
         const float (*Am)[CP] = mt == 0 ? sm.Bh : mt == 1 ? sm.Kh : sm.S + 16 * (mt - 2);
         const float (*Bm)[CP] = nt < 2 ? sm.At : sm.Rt;
@@ -313,7 +317,7 @@ wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T*
     // warps 2-7, beside the Z chain of warps 0-1: X2 = X + V Mk, Y += V Nk
     // (V[dv][m] = vv[m][dv]: 16 tiles of 16 x 8)
     if (warp >= 2)
-        for (int tile = warp - 2; tile < 16; tile += 6) {
+        for (int tile = warp - 2; tile < 16; tile += FT / 32 - 2) {
             const bool isX = tile < 8;
             const int tt = tile & 7, m0 = (tt >> 1) * 16, n0 = (tt & 1) * 8;
             const float (*Bm)[LP] = isX ? sm.Mk : sm.Nk;
@@ -332,11 +336,11 @@ wkv7_chunk_out_kernel(const T* __restrict__ r, const T* __restrict__ w, const T*
             for (int q = 0; q < 4; q++) (isX ? sm.X2 : sm.Y)[frag_i(m0, lane, q)][frag_j(n0, lane, q)] = d[q];
         }
     const int zb = z_chain(sm.Zb, sm.Pb, sm.Mb);
-    // U = X2 Z: 8 tiles, one per warp
-    tile_64x16(sm.U, sm.X2, sm.Zb[zb], nullptr, (warp >> 1) * 16, (warp & 1) * 8, lane);
+    // U = X2 Z: 8 tiles, one per warp of warps 0-7
+    if (warp < 8) tile_64x16(sm.U, sm.X2, sm.Zb[zb], nullptr, (warp >> 1) * 16, (warp & 1) * 8, lane);
     __syncthreads();
-    // Y += U Nb -> y (and sa = U): 8 tiles, one per warp
-    {
+    // Y += U Nb -> y (and sa = U): 8 tiles, one per warp of warps 0-7
+    if (warp < 8) {
         const int m0 = (warp >> 1) * 16, n0 = (warp & 1) * 8;
         float d[4];
 #pragma unroll
@@ -391,7 +395,7 @@ int launch_wkv7_chunk_fwd(int dtype, const void* r, const void* w, const void* k
         if (int rc = check_launch("wkv7_chunk_prep_kernel")) return rc;
         wkv7_chunk_scan_kernel<<<dim3(B * H, CN / SR), ST, 0, st>>>(h_in, Aws, Bws, S0ws, h_out, ckpt, NC, 0);
         if (int rc = check_launch("wkv7_chunk_scan_kernel")) return rc;
-        out<<<dim3(NC, B * H), CT, sizeof(OutSmem), st>>>(
+        out<<<dim3(NC, B * H), FT, sizeof(OutSmem), st>>>(
             (const T*)r, (const T*)w, (const T*)k, (const T*)v, (const T*)a, (const T*)b, S0ws, (T*)y, sa,
             T_, H, NC);
         return check_launch("wkv7_chunk_out_kernel");

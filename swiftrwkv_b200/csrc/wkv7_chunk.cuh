@@ -112,29 +112,29 @@ __device__ __forceinline__ void mm16(float (*C)[LP], const float (*A)[LP], const
 // [v0, v0 + nv) (nv * 16 a multiple of 256); padded tokens are identity
 // steps.  Every global load is issued before the first shared store, so a
 // CTA waits on memory once.
-template <typename T, int NV>
+template <typename T, int NV, int NTH = CT>
 __device__ __forceinline__ void stage_chunk(float (*rr)[CN], float (*ww)[CN], float (*kk)[CN],
                                             float (*aa)[CN], float (*bb)[CN], float* vv, int vstride,
                                             const T* r, const T* w, const T* k, const T* v,
                                             const T* a, const T* b, int bi, int hi, int H, int T_,
                                             int t0, int v0) {
-    constexpr int PER = CL * CN / CT, VPER = CL * NV / CT;
+    constexpr int PER = CL * CN / NTH, VPER = CL * NV / NTH;
     T lr[PER], lw[PER], lk[PER], la[PER], lb[PER], lv[VPER];
 #pragma unroll
     for (int i = 0; i < PER; i++) {
-        const int e = threadIdx.x + CT * i, tl = e / CN, c = e % CN, t = t0 + tl;
+        const int e = threadIdx.x + NTH * i, tl = e / CN, c = e % CN, t = t0 + tl;
         const size_t o = (((size_t)bi * T_ + min(t, T_ - 1)) * H + hi) * CN + c;
         if (rr) lr[i] = r[o];
         lw[i] = w[o]; lk[i] = k[o]; la[i] = a[o]; lb[i] = b[o];
     }
 #pragma unroll
     for (int i = 0; i < VPER; i++) {
-        const int e = threadIdx.x + CT * i, tl = e / NV, d = e % NV, t = t0 + tl;
+        const int e = threadIdx.x + NTH * i, tl = e / NV, d = e % NV, t = t0 + tl;
         lv[i] = v[(((size_t)bi * T_ + min(t, T_ - 1)) * H + hi) * CN + v0 + d];
     }
 #pragma unroll
     for (int i = 0; i < PER; i++) {
-        const int e = threadIdx.x + CT * i, tl = e / CN, c = e % CN;
+        const int e = threadIdx.x + NTH * i, tl = e / CN, c = e % CN;
         const bool in = t0 + tl < T_;
         if (rr) rr[tl][c] = in ? to_f(lr[i]) : 0.f;
         ww[tl][c] = in ? to_f(lw[i]) : 1.f;
@@ -144,7 +144,7 @@ __device__ __forceinline__ void stage_chunk(float (*rr)[CN], float (*ww)[CN], fl
     }
 #pragma unroll
     for (int i = 0; i < VPER; i++) {
-        const int e = threadIdx.x + CT * i, tl = e / NV, d = e % NV;
+        const int e = threadIdx.x + NTH * i, tl = e / NV, d = e % NV;
         vv[tl * vstride + d] = t0 + tl < T_ ? to_f(lv[i]) : 0.f;
     }
 }
