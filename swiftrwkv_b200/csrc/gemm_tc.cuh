@@ -180,21 +180,21 @@ template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // The 8 codes of packed word w (k = 8w .. 8w+7), dequantised to fp16 in
-// natural k order: out[q] = (w_{2q}, w_{2q+1}).
+// natural k order: out[q] = (w_{2q}, w_{2q+1}).  Byte q holds codes 2q (low
+// nibble) and 2q+1 (high nibble); placed in the two halves under the
+// exponent of 1024 they read 1024 + c_lo and 1024 + 16 c_hi, and one exact
+// HFMA2 by (1, 1/16) and (-1024, -64) turns them into (c_lo, c_hi).  The
+// second HFMA2 is the rounding point, w = half(scale * q + bias).
 __device__ __forceinline__ void dq_word(uint32_t w, __half2 s2, __half2 b2, uint32_t* out) {
-    uint32_t p[4];
+    const __half2 mul = __halves2half2(__ushort_as_half(0x3C00), __ushort_as_half(0x2C00));  // (1, 1/16)
+    const __half2 add = __halves2half2(__ushort_as_half(0xE400), __ushort_as_half(0xD400));  // (-1024, -64)
 #pragma unroll
-    for (int j = 0; j < 4; j++) {  // p[j] = (w_j, w_{j+4})
-        uint32_t h = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-        const __half2 q = __hsub2(*reinterpret_cast<__half2*>(&h),
-                                  __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
-        const __half2 v = __hfma2(q, s2, b2);
-        p[j] = *reinterpret_cast<const uint32_t*>(&v);
+    for (int q = 0; q < 4; q++) {
+        uint32_t h = (__byte_perm(w, 0, 0x4040u | (uint32_t)q | ((uint32_t)q << 8)) & 0x00F0000Fu) | 0x64006400u;
+        const __half2 c = __hfma2(*reinterpret_cast<__half2*>(&h), mul, add);
+        const __half2 v = __hfma2(c, s2, b2);
+        out[q] = *reinterpret_cast<const uint32_t*>(&v);
     }
-    out[0] = __byte_perm(p[0], p[1], 0x5410);
-    out[1] = __byte_perm(p[2], p[3], 0x5410);
-    out[2] = __byte_perm(p[0], p[1], 0x7632);
-    out[3] = __byte_perm(p[2], p[3], 0x7632);
 }
 
 // 4 / 8 columns into raw registers; complete them with tmem_ld_wait()
@@ -230,9 +230,10 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t smem_addr, int rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
     return r;
 }
-// posted store into a peer CTA's shared memory (ordered by the next cluster barrier)
-__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
-    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+// posted 16-byte store into a peer CTA's shared memory (ordered by the next cluster barrier)
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, const uint32_t* v) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+                 "r"(v[3]) : "memory");
 }
 
 }  // namespace tc
@@ -283,7 +284,8 @@ struct TcCfg {
     static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 needs N % 16 == 0, 16..256");
     static_assert(BN <= TC_A_COL, "accumulator columns");
-    static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * BN * 4, "split-K receive buffers reuse the stage buffers");
+    static constexpr int RP = BN + 4;                     // split-K receive row pitch (floats): 16-byte rows, conflict-free
+    static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * RP * 4, "split-K receive buffers reuse the stage buffers");
     static_assert(TOTAL <= 227 * 1024, "shared memory per CTA");
     static_assert(FMT == TC_F16 || (CPR % TC_QW == 0 && CPW >= 1 && CPW <= 2),
                   "a dequant warp's chunks lie in one group");
@@ -507,39 +509,54 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     if (S > 1) {
         // Split-K over the (1, 1, S) cluster.  CTA z owns rows [128z/S, 128(z+1)/S)
         // of the tile and receives, from every split zs, those rows of its
-        // partial into rbuf[zs][BN][NRM] (its own stage buffers, idle once
-        // every CTA of the cluster has passed the first barrier).  Every thread
-        // of every CTA takes both barriers, on every path.
+        // partial into rbuf[zs][row][RP] (its own stage buffers, idle once
+        // every CTA of the cluster has passed the first barrier), 16 bytes per
+        // store.  Every thread of every CTA takes both barriers, on every path.
+        constexpr int RP = C::RP;
         const int NRM = (TC_BM + S - 1) / S;
         const uint32_t rbuf = tc::saddr(smem);
         tc::cluster_sync();
+        // a wait that gave up anywhere in the cluster set *err before the
+        // barrier: read it now, its latency hidden behind the partial stores
+        const int gave_up = warp >= 2 ? *(volatile int*)err : 0;
         if (warp >= 2) {
             const int rl = 32 * (warp & 3) + lane, h = (warp - 2) >> 2;
             const int zo = ((rl + 1) * S + TC_BM - 1) / TC_BM - 1;  // owner of row rl
             const int lr = rl - TC_BM * zo / S;
-            const uint32_t dst = tc::map_rank(rbuf + (uint32_t)((kz * BN + h * CW) * NRM + lr) * 4, zo);
+            const uint32_t dst = tc::map_rank(rbuf + (uint32_t)((kz * NRM + lr) * RP + h * CW) * 4, zo);
 #pragma unroll
-            for (int c = 0; c < CW; c++) tc::st_cluster_u32(dst + (uint32_t)(c * NRM) * 4, acc[c]);
+            for (int c = 0; c < CW; c += 4) tc::st_cluster_v4(dst + (uint32_t)c * 4, acc + c);
         }
         tc::cluster_sync();
-        if (warp >= 2 && !*(volatile int*)err) {
+        if (warp >= 2 && !gave_up) {
+            // task = (row, 4 columns): the S partials summed in split order
+            // (deterministic), then 4 outputs; lanes take consecutive rows, so
+            // the reads are conflict-free and the stores coalesce along o
             const GemvJob g = jb.g;
             const int r0 = TC_BM * kz / S, nr = TC_BM * (kz + 1) / S - r0;
             const float* rb = reinterpret_cast<const float*>(smem);
             const bool plain = g.act == ACT_NONE && g.out == OUT_F32;
-            for (int e = tid - 64; e < nr * BN; e += 32 * TC_DQW) {
-                const int c = e / nr, lr = e - c * nr;
-                const float* src = rb + c * NRM + lr;
-                float p[TC_MAX_SPLIT];
+            for (int e = tid - 64; e < nr * (BN / 4); e += 32 * TC_DQW) {
+                const int cq = e / nr, lr = e - cq * nr;
+                const float* src = rb + lr * RP + 4 * cq;
+                float4 v = *reinterpret_cast<const float4*>(src);
+                for (int z = 1; z < S; z++) {
+                    const float4 p = *reinterpret_cast<const float4*>(src + z * NRM * RP);
+                    v.x += p.x;
+                    v.y += p.y;
+                    v.z += p.z;
+                    v.w += p.w;
+                }
+                const int o = m0 + r0 + lr;
+                if (o >= OUT) continue;
+                const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int z = 0; z < TC_MAX_SPLIT; z++) p[z] = z < S ? src[z * BN * NRM] : 0.f;
-                float v = 0.f;
-#pragma unroll
-                for (int z = 0; z < TC_MAX_SPLIT; z++) v += p[z];  // split order; the zero tail is exact
-                const int o = m0 + r0 + lr, n = n0 + c;
-                if (o < OUT && n < args.R) {
-                    if (plain) ((float*)g.y)[(int64_t)n * g.y_stride + o] = v;
-                    else epilogue(g, o, n, v);
+                for (int j = 0; j < 4; j++) {
+                    const int n = n0 + 4 * cq + j;
+                    if (n < args.R) {
+                        if (plain) ((float*)g.y)[(int64_t)n * g.y_stride + o] = vv[j];
+                        else epilogue(g, o, n, vv[j]);
+                    }
                 }
             }
         }
