@@ -161,10 +161,11 @@ x070_tmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
     for (int m = 0; m < 6; m++) ld_row4<GV>(cf[m], coef + m * C, C);
     ld_row4<GV>(w4, lnw, C);
     ld_row4<GV>(b4, lnb, C);
+    // the shift row was last written by this kernel one step earlier
+    ld_row4<GV>(sv, shift + (int64_t)n * C, C);
     pdl_wait();  // x: the previous kernel's output
     pdl_trigger();
     ld_row4<GV>(v, x + (int64_t)n * C, C);
-    ld_row4<GV>(sv, shift + (int64_t)n * C, C);
     ln_row4<GV>(v, w4, b4, C, sh);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
@@ -190,10 +191,11 @@ x070_cmix_in_kernel(const float* __restrict__ x, const float* __restrict__ lnw,
     ld_row4<GV>(cf, coef, C);
     ld_row4<GV>(w4, lnw, C);
     ld_row4<GV>(b4, lnb, C);
-    pdl_wait();  // x and the shift row: written by earlier kernels of the step
+    // the shift row was last written by this kernel one step earlier
+    ld_row4<GV>(sv, shift + (int64_t)n * C, C);
+    pdl_wait();  // x: written by earlier kernels of the step
     pdl_trigger();
     ld_row4<GV>(v, x + (int64_t)n * C, C);
-    ld_row4<GV>(sv, shift + (int64_t)n * C, C);
     ln_row4<GV>(v, w4, b4, C, sh);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
@@ -247,8 +249,6 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
                 const float* __restrict__ lnxw, const float* __restrict__ lnxb,
                 const float* __restrict__ g, float* __restrict__ state, A* __restrict__ out,
                 int H, int layer0) {
-    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
-    pdl_trigger();
     constexpr int N = 64, RPW = 16;  // rows per warp
     __shared__ __align__(16) float r_s[N], w_s[N], kp_s[N], aw_s[N], bw_s[N], v_s[N], y_s[N];
     __shared__ __align__(16) float rk_s[N], lw_s[N], lb_s[N], g_s[N];
@@ -259,19 +259,30 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
     const int half = lane >> 4, c0 = 4 * (lane & 15);
     const size_t vb = (size_t)rh * N;   // [R, H, N] element base of this (row, head)
     const size_t hb = (size_t)hi * N;   // [H, N] parameter base
+    // The state and the per-head parameters are read before the wait on the
+    // predecessor: no kernel of the step before this one writes them (the
+    // state was last written by this kernel one step earlier, and the row
+    // kernels in between wait for completion before letting successors
+    // start), so their loads overlap the predecessor's tail.
     float* hp = state + (size_t)rh * N * N + (size_t)(RPW * warp + half) * N + c0;
     float4 s[RPW / 2];
 #pragma unroll
     for (int p = 0; p < RPW / 2; p++) s[p] = *reinterpret_cast<const float4*>(hp + (size_t)2 * p * N);
+    const int pc = threadIdx.x & (N - 1);
+    const float par0 = threadIdx.x < N ? kkw[hb + pc] : rkw[hb + pc];
+    const float par1 = threadIdx.x < N ? kaw[hb + pc] : lnxw[hb + pc];
+    const float par2 = threadIdx.x < N ? 0.f : lnxb[hb + pc];
+    pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
+    pdl_trigger();
     if (threadIdx.x < N) {  // warps 0-1: per-column vectors; column c = threadIdx.x
         const int c = threadIdx.x;
         const float kr = kraw[vb + c], aa = a[vb + c];
-        const float kk = kr * kkw[hb + c];
+        const float kk = kr * par0;
         float ss = warp_sum(kk * kk);
         if ((c & 31) == 0) red[c >> 5] = ss;
         r_s[c] = r[vb + c];
         w_s[c] = wdec[vb + c];
-        const float kp = kr * (1.0f + (aa - 1.0f) * kaw[hb + c]);
+        const float kp = kr * (1.0f + (aa - 1.0f) * par1);
         kp_s[c] = kp;
         // value row c
         float vd = vraw[vb + c];
@@ -289,9 +300,9 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
         bw_s[c] = kn * aa;
     } else {  // warps 2-3: the tail's per-head parameters and the gate
         const int c = threadIdx.x - N;
-        rk_s[c] = rkw[hb + c];
-        lw_s[c] = lnxw[hb + c];
-        lb_s[c] = lnxb[hb + c];
+        rk_s[c] = par0;
+        lw_s[c] = par1;
+        lb_s[c] = par2;
         g_s[c] = g[vb + c];
     }
     __syncthreads();
