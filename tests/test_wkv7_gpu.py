@@ -91,6 +91,18 @@ def test_step_equals_forward_at_t1_bitwise(cuda, rng, H):
     assert torch.equal(ys, y[0, 0]) and torch.equal(hs, h[0])
 
 
+def test_step_many_items_equals_forward_bitwise(cuda, rng):
+    """A full decode batch (64 rows x 32 heads, more CTAs than fit on the
+    GPU at once): still the forward at T = 1 bit for bit."""
+    from swiftrwkv_b200 import kernel as K
+    rows, H = 64, 32
+    ins = [dev(x) for x in wkv_inputs(rng, rows, 1, H)]
+    h0 = dev((rng.standard_normal((rows, H, 64, 64)) * 0.1).astype(np.float32))
+    y, h = K.wkv7SequenceForward(*ins, h0)
+    ys, hs = K.wkv7StepForward(*(x[:, 0] for x in ins), h0)
+    assert torch.equal(ys, y[:, 0]) and torch.equal(hs, h)
+
+
 def test_step_dtype_independence(cuda, rng):
     """DecodeKernelTests.swift:43-53: the result does not depend on the input
     dtype once values are the same (bf16-exact inputs in bf16 and fp32)."""
@@ -102,10 +114,12 @@ def test_step_dtype_independence(cuda, rng):
     assert torch.equal(y16, y32) and torch.equal(h16, h32)
 
 
-def test_step_tail_matches_oracle(cuda, oracle, rng):
-    """The fused step+tail against the oracle's step followed by its tail (<= 1e-5)."""
+@pytest.mark.parametrize("rows", [5, 64])
+def test_step_tail_matches_oracle(cuda, oracle, rng, rows):
+    """The fused step+tail against the oracle's step followed by its tail
+    (<= 1e-5), on a few rows and on a full 64-row decode batch."""
     from swiftrwkv_b200 import kernel as K
-    rows, H = 5, 32
+    H = 32
     ins = [x[:, 0] for x in wkv_inputs(rng, rows, 1, H)]
     h0 = (rng.standard_normal((rows, H, 64, 64)) * 0.1).astype(np.float32)
     g = rng.standard_normal((rows, H, 64)).astype(np.float32)
