@@ -138,6 +138,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _nccl_problem():
+    rng = np.random.default_rng(21)
+    L, BG, T, H = 2, 4, 32, 4
+    layers = _layers(rng, L, BG, T, H)
+    init = torch.from_numpy((rng.standard_normal((L, H, 64, 64)) * 0.1).astype(np.float32))
+    return L, BG, H, layers, init
+
+
 def _nccl_worker(rank, world, port, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -146,10 +154,7 @@ def _nccl_worker(rank, world, port, out_dir):
                                          timeout=datetime.timedelta(seconds=60),
                                          device_id=torch.device("cuda", rank))
     try:
-        rng = np.random.default_rng(21)
-        L, BG, T, H = 2, 4, 32, 4
-        layers = _layers(rng, L, BG, T, H)
-        init = torch.from_numpy((rng.standard_normal((L, H, 64, 64)) * 0.1).astype(np.float32))
+        L, BG, H, layers, init = _nccl_problem()
         sl = WKVStateTuner.local_slice(BG, rank, world)
         local = [[x[sl].contiguous().cuda() for x in t] for t in layers]
         tu = WKVStateTuner(L, H, config=StateTuneConfig(lr=1e-2, warmupSteps=0, maxSteps=4),
@@ -158,13 +163,6 @@ def _nccl_worker(rank, world, port, out_dir):
             tu.step(local)
         torch.cuda.synchronize()
         torch.save({"params": tu.params.cpu()}, os.path.join(out_dir, f"rank{rank}.pt"))
-        if rank == 0:
-            one = WKVStateTuner(L, H, config=StateTuneConfig(lr=1e-2, warmupSteps=0, maxSteps=4),
-                                initial=init.cuda(), grad_scale=1.0 / world)
-            full = [[x.cuda() for x in t] for t in layers]
-            for _ in range(2):
-                one.step(full)
-            torch.save({"params": one.params.cpu()}, os.path.join(out_dir, "single.pt"))
     finally:
         torch.distributed.destroy_process_group()
 
@@ -175,6 +173,14 @@ def test_nccl_two_ranks_equal_one_process(tmp_path):
     torch.multiprocessing.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)),
                                           nprocs=world, join=True, start_method="spawn")
     r0, r1 = (torch.load(tmp_path / f"rank{r}.pt")["params"] for r in range(world))
-    one = torch.load(tmp_path / "single.pt")["params"]
+    # the same two steps in this process (no process group: no allreduce) over
+    # the whole batch, gradients averaged over the ranks' count
+    L, BG, H, layers, init = _nccl_problem()
+    single = WKVStateTuner(L, H, config=StateTuneConfig(lr=1e-2, warmupSteps=0, maxSteps=4),
+                           initial=init.cuda(), grad_scale=1.0 / world)
+    full = [[x.cuda() for x in t] for t in layers]
+    for _ in range(2):
+        single.step(full)
+    one = single.params.cpu()
     assert torch.equal(r0, r1)
     np.testing.assert_allclose(r0.numpy(), one.numpy(), rtol=0, atol=1e-5)
