@@ -114,6 +114,11 @@ struct X070 {
     // there is forwarded to this stream, ordered by events on both sides.
     cudaStream_t own = nullptr;
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    // The low-rank branches (down + up) of a layer run on `side`, beside the
+    // r/k/v GEMM, when both take the tensor-core path (which keeps no shared
+    // workspace): fork after tmix_in, join before the WKV step.
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     // split-K partials and tickets of the tensor-core GEMMs
     float* gws = nullptr;
     int* gtickets = nullptr;
@@ -220,6 +225,9 @@ struct X070 {
         cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking);
         cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+        cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking);
+        cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming);
     }
 
     ~X070() {
@@ -229,6 +237,9 @@ struct X070 {
         if (own) cudaStreamDestroy(own);
         if (ev_in) cudaEventDestroy(ev_in);
         if (ev_out) cudaEventDestroy(ev_out);
+        if (side) cudaStreamDestroy(side);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (ev_join) cudaEventDestroy(ev_join);
     }
 
     // ----- parameters
@@ -468,6 +479,11 @@ struct X070 {
         return check_launch("gemv_cc_kernel");
     }
 
+    // whether gemv() takes the tensor-core path for these jobs
+    bool tc_path(int fmt, const GemvJobs& jobs, int nj, int R) const {
+        return f16act && plan_tc(fmt == 0 ? TC_Q4 : TC_F16, jobs, nj, R, sm_count).ok;
+    }
+
     static GemvJob qjob(const QMat& q, const void* x, int xs, int act, int out, void* y, int ys,
                         const float* bias = nullptr) {
         GemvJob j{};
@@ -546,13 +562,6 @@ struct X070 {
             J.j[0] = qjob(w.r, M(0), C, ACT_NONE, OUT_F32, r, C);
             J.j[1] = qjob(w.k, M(2), C, ACT_NONE, OUT_F32, k, C);
             J.j[2] = qjob(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
-            if ((rc = gemv(0, J, 3, R, st))) return rc;
-            mark("gemm_rkv");
-            {
-                const LoraJob lj[3] = {{&w.ad[AD_R], M(0), C, C, C, r, C}, {&w.ad[AD_K], M(2), C, C, C, k, C},
-                                       {&w.ad[AD_V], M(3), C, C, C, v, C}};
-                if ((rc = lora_apply<A>(lj, 3, R, st))) return rc;
-            }
             // low-rank down: w (tanh), a, g (sigmoid), v
             GemvJobs D{};
             int nd = 0;
@@ -560,16 +569,35 @@ struct X070 {
             D.j[nd++] = hjob(w.aA, ra, C, M(4), C, ACT_NONE, aout, hidp + rw, hid);
             D.j[nd++] = hjob(w.gA, rg, C, M(5), C, ACT_SIGMOID, aout, hidp + rw + ra, hid);
             if (l > 0) D.j[nd++] = hjob(w.vA, rv, C, M(3), C, ACT_NONE, aout, hidp + rw + ra + rg, hid);
-            if ((rc = gemv(1, D, nd, R, st))) return rc;
-            mark("lora_down");
             GemvJobs U{};
             int nu = 0;
             U.j[nu++] = hjob(w.wB, C, rw, hidp, hid, ACT_DECAY, OUT_F32, wdec, C, w.wbias);
             U.j[nu++] = hjob(w.aB, C, ra, hidp + rw, hid, ACT_SIGMOID_BIAS, OUT_F32, a, C, w.abias);
             U.j[nu++] = hjob(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, g, C);
             if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
-            if ((rc = gemv(1, U, nu, R, st))) return rc;
+            // the low-rank branch reads only tmix_in's mixes and writes only
+            // w/a/g/v': beside the r/k/v GEMM when neither needs the shared
+            // split-K workspace (the step profiler keeps one stream)
+            const bool fork = side && !profiling && tc_path(0, J, 3, R) && tc_path(1, D, nd, R) &&
+                              tc_path(1, U, nu, R);
+            cudaStream_t sb = fork ? side : st;
+            if (fork) {
+                cudaEventRecord(ev_fork, st);
+                cudaStreamWaitEvent(side, ev_fork, 0);
+            }
+            if ((rc = gemv(1, D, nd, R, sb))) return rc;
+            mark("lora_down");
+            if ((rc = gemv(1, U, nu, R, sb))) return rc;
             mark("lora_up");
+            if (fork) cudaEventRecord(ev_join, side);
+            if ((rc = gemv(0, J, 3, R, st))) return rc;
+            mark("gemm_rkv");
+            {
+                const LoraJob lj[3] = {{&w.ad[AD_R], M(0), C, C, C, r, C}, {&w.ad[AD_K], M(2), C, C, C, k, C},
+                                       {&w.ad[AD_V], M(3), C, C, C, v, C}};
+                if ((rc = lora_apply<A>(lj, 3, R, st))) return rc;
+            }
+            if (fork) cudaStreamWaitEvent(st, ev_join, 0);
             if ((rc = pdl_check(launch_pdl(x070_wkv_kernel<A>, R * H, 128, 0, st, (const float*)r,
                                            (const float*)wdec, (const float*)k, (const float*)v,
                                            (const float*)a, (const float*)vv, vfirst, (const float*)w.kkw,
