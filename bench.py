@@ -41,6 +41,15 @@ import sys
 import threading
 import time
 
+# The CPU legs run the oracle's OpenMP loops on every host core.  The few small
+# numpy matmuls they also make get one BLAS thread, set before numpy loads
+# OpenBLAS: a BLAS pool of one thread per core spinning beside the OpenMP pool
+# slowed the CPU decode baseline ~40x when nothing capped it (under torchrun
+# OMP_NUM_THREADS=1 capped it, so N=1 and N>1 disagreed).
+BLAS_THREADS = 1
+os.environ.setdefault("OPENBLAS_NUM_THREADS", str(BLAS_THREADS))
+os.environ.setdefault("MKL_NUM_THREADS", str(BLAS_THREADS))
+
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -368,42 +377,62 @@ class Decode15B:
         self.alg_bytes = self.m.weight_bytes + self.state_bytes + shift_bytes
         self.units_per_step = self.rows
         self.launches_per_step = self.m.launches_per_step
-        self.kernel = ("wkv7_step_kernel<float,1> via rwkv_wkv7_step_tail (the step's WKV+tail over "
-                       "one layer's rows x heads)")
-        self.pin_ids = torch.zeros(self.rows, dtype=torch.int32).pin_memory()
+        # e2e: the previous step's tokens go host -> device, this step's
+        # argmax comes back to the host, which waits for it (as generate does)
+        self.pin_ids = torch.from_numpy(prompts[:, -1].copy()).pin_memory()
         self.pin_out = torch.zeros(self.rows, dtype=torch.int32).pin_memory()
         self.dev_ids = torch.zeros(self.rows, dtype=torch.int32, device=dev)
+        self.dev_next = torch.zeros(self.rows, dtype=torch.int32, device=dev)
         self.h2d = self.rows * 4
         self.d2h = self.rows * 4
-        # the dominant kernel family, timed on its own: the WKV step + tail
-        # over all rows x heads of one layer (state read + write)
-        self.wkv = [torch.randn((self.rows, H, 64), device=dev) for _ in range(7)]
-        self.wkv_state = torch.zeros((self.rows, H, 64, 64), device=dev)
-        self.wkv_par = [torch.randn(self.C, device=dev) for _ in range(3)]
-        self.wkv_out = torch.empty((self.rows, self.C), device=dev)
-        self.dom_bytes = self.rows * H * (64 * 64 * 4 * 2 + 8 * 64 * 4)
+        self._family()
+
+    def _family(self):
+        """The dominant kernel family: the 4-bit projection GEMMs of the step
+        (r/k/v, o, key, value in every layer, and the head)."""
+        R, C, F, V, L = self.rows, self.C, 4 * self.C, self.V, self.L
+        q = lambda OUT, IN: OUT * IN * (0.5 + 4 / 64)
+        self.family = {
+            "gemm_rkv": 3 * (q(C, C) + R * C * 2 + R * C * 4),
+            "gemm_o": q(C, C) + R * C * 2 + R * C * 8,          # y += : read + write
+            "gemm_key": q(F, C) + R * C * 2 + R * F * 2,        # relu^2 out fp16
+            "gemm_value": q(C, F) + R * F * 2 + R * C * 8,
+            "gemm_head": q(V, C) + R * C * 2 + R * V * 4,
+        }
+        self.family_launches = 4 * L + 1
+        self.dom_bytes = (L * sum(v for k, v in self.family.items() if k != "gemm_head")
+                          + self.family["gemm_head"]) / self.family_launches
+        kern = ("gemm_tc_kernel<TC_Q4> (tcgen05 4-bit GEMM, TMA + TMEM)" if R > 8 else
+                "gemm_w4_kernel (mma.sync 4-bit GEMV mode)")
+        self.kernel = (f"{kern}: r/k/v, o, key, value x {L} layers + head = {self.family_launches} "
+                       "launches per step; per-launch time from the runtime's step profiler "
+                       "(rwkv_x070_profile_step: an event after every launch of a captured step)")
 
     def step(self):
         self.m.step_greedy(self.rows, None, use_graph=True)
 
     def step_e2e(self):
         self.dev_ids.copy_(self.pin_ids, non_blocking=True)
-        self.m.step_greedy(self.rows, self.dev_ids, use_graph=True)
-        # next ids live in the runtime; read them back through a graph-free step output
-        self.pin_out.copy_(self.dev_ids, non_blocking=True)
+        self.m.step_greedy(self.rows, self.dev_ids, use_graph=True, next_ids=self.dev_next)
+        self.pin_out.copy_(self.dev_next, non_blocking=True)
+        self.torch.cuda.current_stream().synchronize()
+        self.pin_ids.copy_(self.pin_out)
 
-    def dominant(self):
-        from swiftrwkv_b200 import _lib
-        P = _lib.P
-        r, w, k, v, a, b, g = self.wkv
-        rk, lw, lb = self.wkv_par
-        _lib.call("rwkv_wkv7_step_tail", *(P(t.data_ptr()) for t in (r, w, k, v, a, b)),
-                  P(self.wkv_state.data_ptr()), *(P(t.data_ptr()) for t in (rk, lw, lb, g)),
-                  P(self.wkv_out.data_ptr()), self.rows, self.C // 64, 64, _lib.F(64e-5),
-                  P(self.torch.cuda.current_stream().cuda_stream))
+    def dominant_ms(self, reps):
+        """Average device time per launch of the GEMM family inside the step."""
+        tot, n = 0.0, 0
+        for _ in range(reps):
+            agg, _ = self.m.profile_step(self.rows)
+            for name in self.family:
+                c, t = agg.get(name, (0, 0.0))
+                tot += t
+                n += c
+        if n != reps * self.family_launches:
+            raise RuntimeError(f"step profiler saw {n} family launches, expected {reps * self.family_launches}")
+        return tot / n
 
-    def cpu(self, seconds):
-        return cpu_decode_tokps(self.L, self.C, self.V, seconds)
+    def cpu(self, seconds, rows=None):
+        return cpu_decode_tokps(self.L, self.C, self.V, seconds, rows or self.rows)
 
 
 class StateTune29B:
@@ -495,35 +524,38 @@ class StateTune29B:
 _CPU_CACHE = {}
 
 
-def cpu_decode_tokps(L, C, V, seconds):
-    """CPU oracle decode of one row at 1.5B shapes: one layer (its 4-bit GEMVs
-    on packed weights, the low-rank branches, WKV step + tail) and the head
-    GEMV are timed, and the step is extrapolated as L layers + head."""
+def cpu_decode_tokps(L, C, V, seconds, rows=1):
+    """CPU oracle decode of `rows` rows at 1.5B shapes: one layer (its 4-bit
+    GEMVs on packed weights, the low-rank branches, WKV step + tail, all over
+    the rows) and the head GEMV are timed, and the step is extrapolated as L
+    layers + head."""
     from oracle import oracle as O
     from oracle.x070_oracle import lora_ranks
-    if (L, C, V) in _CPU_CACHE:
-        return _cpu_decode_time(L, seconds, *_CPU_CACHE[(L, C, V)])
-    rng = np.random.default_rng(SEED)
-    H, F = C // 64, 4 * C
-    rk = lora_ranks(C)
+    key = (L, C, V)
+    if key not in _CPU_CACHE:
+        rng = np.random.default_rng(SEED)
+        H, F = C // 64, 4 * C
+        rk = lora_ranks(C)
 
-    def q(OUT, IN):
-        W = (rng.standard_normal((OUT, IN)) * 0.02).astype(np.float16).astype(np.float32)
-        return O.affine_quantize(W)
+        def q(OUT, IN):
+            W = (rng.standard_normal((OUT, IN)) * 0.02).astype(np.float16).astype(np.float32)
+            return O.affine_quantize(W)
 
-    mats = {n: q(*sh) for n, sh in (("r", (C, C)), ("k", (C, C)), ("v", (C, C)), ("o", (C, C)),
-                                     ("key", (F, C)), ("value", (C, F)))}
-    lora = {n: ((rng.standard_normal((rk[n], C)) * 0.05).astype(np.float32),
-                (rng.standard_normal((C, rk[n])) * 0.05).astype(np.float32)) for n in "wavg"}
-    state = np.zeros((1, H, 64, 64), np.float32)
-    x = rng.standard_normal((1, C)).astype(np.float32)
-    head = q(V, C)
-    _CPU_CACHE[(L, C, V)] = (C, H, mats, lora, state, x, head)
-    return _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head)
+        mats = {n: q(*sh) for n, sh in (("r", (C, C)), ("k", (C, C)), ("v", (C, C)), ("o", (C, C)),
+                                         ("key", (F, C)), ("value", (C, F)))}
+        lora = {n: ((rng.standard_normal((rk[n], C)) * 0.05).astype(np.float32),
+                    (rng.standard_normal((C, rk[n])) * 0.05).astype(np.float32)) for n in "wavg"}
+        _CPU_CACHE[key] = (C, H, mats, lora, q(V, C))
+    C, H, mats, lora, head = _CPU_CACHE[key]
+    rng = np.random.default_rng(SEED + rows)
+    state = np.zeros((rows, H, 64, 64), np.float32)
+    x = rng.standard_normal((rows, C)).astype(np.float32)
+    return _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head, rows)
 
 
-def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head):
+def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head, rows):
     from oracle import oracle as O
+    ones, zeros = np.ones(C, np.float32), np.zeros(C, np.float32)
 
     def layer():
         rr = O.affine_gemv(x, *mats["r"])
@@ -531,9 +563,8 @@ def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head):
         vv = O.affine_gemv(x, *mats["v"])
         hs = {n: (x @ lora[n][0].T) @ lora[n][1].T for n in "wavg"}
         wd = np.exp(-0.606531 / (1 + np.exp(-hs["w"]))).astype(np.float32)
-        y, _ = O.wkv7_step(*(t.reshape(1, H, 64) for t in (rr, wd, kk, vv, -kk, kk)), state)
-        t = O.wkv_tail(y.reshape(1, C), rr, kk, vv, np.ones(C, np.float32), np.ones(C, np.float32),
-                       np.zeros(C, np.float32), hs["g"].astype(np.float32), H, 64)
+        y, _ = O.wkv7_step(*(t.reshape(rows, H, 64) for t in (rr, wd, kk, vv, -kk, kk)), state)
+        t = O.wkv_tail(y.reshape(rows, C), rr, kk, vv, ones, ones, zeros, hs["g"].astype(np.float32), H, 64)
         o = O.affine_gemv(t, *mats["o"])
         hk = np.maximum(O.affine_gemv(x + o, *mats["key"]), 0)
         return O.affine_gemv(hk * hk, *mats["value"])
@@ -550,8 +581,12 @@ def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head):
         O.affine_gemv(x, *head)
         m += 1
     t_head = (time.perf_counter() - t0) / m
-    return 1.0 / (L * t_layer + t_head), (f"1 row; {n} timed x070 1.5B layers + {m} head GEMVs, "
-                                          f"step = {L} layers + head")
+    return rows / (L * t_layer + t_head), (f"{rows} rows; {n} timed x070 1.5B layers + {m} head GEMVs "
+                                           f"over all rows, step = {L} layers + head")
+
+
+def cpu_threads(cores):
+    return {"openmp": cores, "blas": int(os.environ.get("OPENBLAS_NUM_THREADS", BLAS_THREADS))}
 
 
 WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "wkv7train": WKV7Train, "gemv": GemvSuite,
@@ -593,13 +628,15 @@ def max_over_ranks(torch, val, dist):
 
 
 def run_reference(args, rank):
-    """CPU arm: the oracle restatement on all host cores, same metric/config."""
+    """CPU arm: the oracle restatement on all host cores, same metric/config.
+    Under torchrun rank 0 alone runs it, over the whole job's rows."""
     if rank != 0:
         return
     from oracle import oracle as O
     O.build()
     cores = os.cpu_count() or 1
     O.set_threads(cores)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     wl = make_workload(args)
     if wl.name in ("wkv7", "wkv7train"):
         rng = np.random.default_rng(SEED)
@@ -608,20 +645,51 @@ def run_reference(args, rank):
             wl.host.append(rng.standard_normal(wl.host[0].shape).astype(np.float32))
     per = []
     sample = ""
+    # each step a bounded sample: the whole run stays within a few minutes
+    budget = min(4.0, 120.0 / (args.warmup + args.steps))
+    config = {"workload": wl.name}
     for i in range(args.warmup + args.steps):
-        v, sample = wl.cpu(2.0 if wl.name != "decode" else 4.0)
+        if wl.name == "decode":
+            v, sample = wl.cpu(budget, rows=wl.rows * world)
+        else:
+            v, sample = wl.cpu(budget)
         if i >= args.warmup:
             per.append(v)
+    if wl.name == "decode":
+        config.update({"model": "x070 1.5B (L=24 C=2048 H=32 V=65536 FFN=8192)", "rows_per_gpu": wl.rows,
+                       "global_batch": wl.rows * world, "base": "MLX affine 4-bit g64"})
     value = statistics.median(per)
     out = {"impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
            "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": wl.name},
+           "config": config,
            "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cores, "kind": "port",
-                            "sample": sample},
+                            "threads": cpu_threads(cores), "sample": sample},
            "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
+
+
+def wkv_prefill_line(torch, dev, args, peaks, flush_l2):
+    """BASELINE's second metric beside decode: WKV-7 prefill tok/s on config 1
+    (the chunked forward), with its own roofline; timed like the main line."""
+    pw = WKV7Prefill()
+    pw.setup(torch, dev)
+    times = timed(torch, pw.step, args.steps, args.warmup, flush_l2, False)
+    e2e = timed(torch, pw.step_e2e, args.steps, args.warmup, flush_l2, False)
+    ms = sum(times) / len(times)
+    ms_e2e = sum(e2e) / len(e2e)
+    gbs = pw.alg_bytes / (ms / 1e3) / 1e9
+    return {"metric": pw.metric, "value": pw.units_per_step / (ms / 1e3), "unit": pw.unit,
+            "ms_per_step": ms, "dtype": "f32", "l2": "flushed (256 MB write) before every timed step",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_src": peaks["src"],
+                         "kernel": "wkv7_chunk_{prep,scan,out}: the three-launch step (canonical bytes "
+                                   "4(7 BTHN + BHN^2) over the step's time)",
+                         "kernel_ms": ms},
+            "e2e": {"value": pw.units_per_step / (ms_e2e / 1e3), "unit": pw.unit,
+                    "h2d_bytes_per_step": pw.h2d, "d2h_bytes_per_step": pw.d2h},
+            "gpu_launches": pw.launches_per_step * args.steps, "_wl": pw}
 
 
 def make_workload(args):
@@ -687,7 +755,12 @@ def main():
     peaks = load_peaks()
     local_ms = sum(times) / len(times)
     step_gbs = wl.alg_bytes / (local_ms / 1e3) / 1e9
-    if hasattr(wl, "dominant"):
+    if hasattr(wl, "dominant_ms"):
+        # the dominant kernel family timed inside the step (per-launch device times)
+        dom_ms = wl.dominant_ms(3)
+        achieved = wl.dom_bytes / (dom_ms / 1e3) / 1e9
+        kernel = wl.kernel
+    elif hasattr(wl, "dominant"):
         # the dominant kernel timed on its own stream position, L2 flushed before each launch
         dt = timed(torch, wl.dominant, args.steps, args.warmup, flush_l2, False)
         dom_ms = sum(dt) / len(dt)
@@ -723,6 +796,8 @@ def main():
         result["config"].update({"model": "x070 1.5B (L=24 C=2048 H=32 V=65536 FFN=8192)",
                                  "rows_per_gpu": wl.rows, "global_batch": wl.rows * world,
                                  "prompt": wl.PROMPT, "base": "MLX affine 4-bit g64"})
+    if wl.name == "decode" and world == 1:
+        result["prefill"] = wkv_prefill_line(torch, dev, args, peaks, flush_l2)
     if rank == 0 and world == 1:
         from oracle import oracle as O
         O.build()
@@ -730,7 +805,12 @@ def main():
         O.set_threads(cores)
         v, sample = wl.cpu(args.cpu_seconds)
         result["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": cores, "kind": "port",
-                                  "sample": sample}
+                                  "threads": cpu_threads(cores), "sample": sample}
+        if "prefill" in result:
+            pw = result["prefill"].pop("_wl")
+            pv, psample = pw.cpu(min(args.cpu_seconds, 5.0))
+            result["prefill"]["cpu_baseline"] = {"value": pv, "unit": pw.unit, "cores": cores, "kind": "port",
+                                                 "threads": cpu_threads(cores), "sample": psample}
     if rank == 0:
         print(json.dumps(result))
     if dist:

@@ -151,8 +151,9 @@ int rwkv_wkv7_backward_chunked(int dtype, const void* r, const void* w, const vo
  * device.  The recompute scratch is a fixed array built into the library:
  * RWKV_NOALLOC_MAX_HEADS (batch, head) pairs x 272 KiB = 63.75 MiB, held by
  * every GPU that loads the library until the process exits; B*H above the
- * limit returns RWKV_E_SHAPE.  The first call on a device looks the array up
- * (do it before any stream capture).  All calls on a device share the array:
+ * limit returns RWKV_E_SHAPE.  The first call on a device, and the first
+ * after the device's context changed (a cudaDeviceReset), looks the array's
+ * address up (make that call before any stream capture).  All calls on a device share the array:
  * calls that overlap on the GPU race, so order them on one stream.  Same
  * arguments and results as rwkv_wkv7_backward otherwise. */
 #define RWKV_NOALLOC_MAX_HEADS 240
@@ -164,7 +165,7 @@ int rwkv_wkv7_backward_noalloc(int dtype, const void* r, const void* w, const vo
 
 /* One-token decode step for `rows` independent rows: r..b, y [rows, H, N];
  * h [rows, H, N, N] fp32 updated in place.
- * Replaces wkv7StepForward (Sources/RWKVKernel/WKV7DecodeKernels.swift:157-173). */
+ * Replaces wkv7StepForward (Sources/RWKVKernel/WKV7DecodeKernels.swift:73-89). */
 int rwkv_wkv7_step(int dtype, const void* r, const void* w, const void* k, const void* v,
                    const void* a, const void* b, float* h, void* y, int rows, int H, int N,
                    rwkv_stream_t stream);
@@ -173,7 +174,7 @@ int rwkv_wkv7_step(int dtype, const void* r, const void* w, const void* k, const
  * bonus (sum r*k*r_k)*v, times the gate:
  *   out = ((norm(wkv)*ln_w + ln_b) + (sum r*k*r_k) * v) * g.
  * wkv, r, k, v, g, out: [rows, H*S] fp32; rk, ln_w, ln_b: [H*S] fp32.
- * Replaces wkvTail (Sources/RWKVKernel/WKV7DecodeKernels.swift:190-262). */
+ * Replaces wkvTail (Sources/RWKVKernel/WKV7DecodeKernels.swift:106-178). */
 int rwkv_wkv_tail(const float* wkv, const float* r, const float* k, const float* v,
                   const float* rk, const float* ln_w, const float* ln_b, const float* g,
                   float* out, int rows, int H, int S, float eps, rwkv_stream_t stream);
@@ -201,6 +202,22 @@ int rwkv_wkv7_step_tail(const float* r, const float* w, const float* k, const fl
 int rwkv_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* scales,
                 const void* biases, int sdtype, int ydtype, void* y, int rows, int OUT, int IN,
                 int group, int bits, rwkv_stream_t stream);
+
+/* Wait errors of rwkv_q_gemm's tensor-core path (fp16 x, 4-bit group 64,
+ * rows > 8).  Its pipeline waits are bounded in time; a wait that gives up
+ * leaves that call's output invalid and records it per device.  The next
+ * rwkv_q_gemm on that device returns RWKV_E_TIMEOUT, clears the record and
+ * launches nothing (a launch still in flight may record it later).
+ * rwkv_q_gemm_status synchronises `stream`, then returns RWKV_E_TIMEOUT (and
+ * clears the record) if one is set, else RWKV_OK: a host that must know
+ * whether the outputs it is about to use are valid calls it.  No counterpart
+ * in the reference, whose Metal kernels have no bounded waits. */
+int rwkv_q_gemm_status(rwkv_stream_t stream);
+/* Sets the record as a wait that gives up would: the device flag, which makes
+ * the next tensor-core launch skip its work, and with host_record != 0 also
+ * the host record.  For testing a host's handling of RWKV_E_TIMEOUT without a
+ * device fault.  No counterpart in the reference. */
+int rwkv_q_gemm_inject_wait_error(int host_record, rwkv_stream_t stream);
 
 /* Dense W [OUT, IN] in odtype: float(q)*float(scale) + float(bias), one
  * rounding.  Replaces MLX `dequantized` as used at
@@ -270,7 +287,7 @@ int rwkv_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_t*
 
 /* Embedding rows of an 8-bit sym table, fp16 out [n_ids, IN]:
  * out = half(code * half(qs*d)).  Replaces RwkvqSymRowTable.rows
- * (Sources/RWKVQuant/RwkvqSymRows.swift:402-411). */
+ * (Sources/RWKVQuant/RwkvqSymRows.swift:26-78). */
 int rwkv_sym_rows(const int32_t* ids, int n_ids, const uint8_t* codes, const uint8_t* qs,
                   const uint16_t* d, uint16_t* out, int vocab, int IN, rwkv_stream_t stream);
 
@@ -326,6 +343,17 @@ int rwkv_x070_step(rwkv_x070_t model, const int32_t* ids, int rows, float* logit
  * recurrently, then n_new tokens per row into out [rows, n_new]. */
 int rwkv_x070_generate(rwkv_x070_t model, const int32_t* prompt_host, int rows, int prompt_len,
                        int n_new, int32_t* out_host, rwkv_stream_t stream);
+/* Wait errors of the model's tensor-core GEMMs (bounded pipeline waits; see
+ * rwkv_q_gemm_status): a step after one gave up returns RWKV_E_TIMEOUT,
+ * clears the record and launches nothing; rwkv_x070_generate checks it at
+ * the end too.  rwkv_x070_status synchronises `stream` and reports (and
+ * clears) the record: RWKV_E_TIMEOUT means the state and outputs since the
+ * last report are not valid.  rwkv_x070_inject_wait_error sets it as a wait
+ * that gives up would (the device flag; with host_record also the host
+ * record), for testing a host's error handling without a device fault.  No
+ * counterpart in the reference. */
+int rwkv_x070_status(rwkv_x070_t model, rwkv_stream_t stream);
+int rwkv_x070_inject_wait_error(rwkv_x070_t model, int host_record, rwkv_stream_t stream);
 /* Step profiler (tracing): one eager step with a CUDA event after every
  * launch; writes per-launch device milliseconds to ms_host[0..*count) and the
  * launch names, '\n'-separated, to names_host.  Advances the state like a step.

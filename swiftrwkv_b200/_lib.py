@@ -51,6 +51,8 @@ _SIGS = {
     "rwkv_wkv_tail": [P, P, P, P, P, P, P, P, P, I, I, I, F, P],
     "rwkv_wkv7_step_tail": [P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, F, P],
     "rwkv_q_gemm": [I, P, P, P, P, I, I, P, I, I, I, I, I, P],
+    "rwkv_q_gemm_status": [P],
+    "rwkv_q_gemm_inject_wait_error": [I, P],
     "rwkv_q_dequant": [P, P, P, I, I, P, I, I, I, I, P],
     "rwkv_q_rows": [P, I, P, P, P, I, I, P, I, I, I, I, P],
     "rwkv_q_quantize": [I, P, P, P, P, I, I, I, I, P],
@@ -68,6 +70,8 @@ _SIGS = {
     "rwkv_x070_step": [P, P, I, P, P, I, P],
     "rwkv_x070_generate": [P, P, I, I, I, P, P],
     "rwkv_x070_profile_step": [P, I, P, I, P, I, P, P],
+    "rwkv_x070_status": [P, P],
+    "rwkv_x070_inject_wait_error": [P, I, P],
     "rwkv_x070_weight_bytes": [P],
     "rwkv_x070_launches_per_step": [P],
     "rwkv_state_broadcast": [P, P, I, I, I, P],

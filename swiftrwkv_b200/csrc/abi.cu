@@ -40,6 +40,8 @@ int launch_wkv7_bwd_seq(int, const void*, const void*, const void*, const void*,
                         cudaStream_t);
 int launch_q_gemm(int, const void*, const uint32_t*, const void*, const void*, int, int, void*,
                   int, int, int, int, int, cudaStream_t);
+int q_gemm_status(cudaStream_t);
+int q_gemm_inject_wait_error(int, cudaStream_t);
 int launch_q_dequant(const uint32_t*, const void*, const void*, int, int, void*, const int32_t*,
                      int, int, int, int, int, cudaStream_t);
 int launch_q_quantize(int, const void*, uint32_t*, void*, void*, int, int, int, int, cudaStream_t);
@@ -262,6 +264,12 @@ int rwkv_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* scale
     RWKV_REQUIRE(al16(x) && al16(wq), RWKV_E_UNSUPPORTED, "rwkv_q_gemm: x / wq not 16-byte aligned");
     return launch_q_gemm(xdtype, x, wq, scales, biases, sdtype, ydtype, y, rows, OUT, IN, group,
                          bits, (cudaStream_t)stream);
+}
+
+int rwkv_q_gemm_status(rwkv_stream_t stream) { return q_gemm_status((cudaStream_t)stream); }
+
+int rwkv_q_gemm_inject_wait_error(int host_record, rwkv_stream_t stream) {
+    return q_gemm_inject_wait_error(host_record, (cudaStream_t)stream);
 }
 
 int rwkv_q_dequant(const uint32_t* wq, const void* scales, const void* biases, int sdtype,

@@ -91,6 +91,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err
     }
 }
 
+// The same wait, blind to *err: for asynchronous work this CTA started and
+// must see finish before it moves on (TMA copies into its shared memory, the
+// MMAs before the final commit).  Gives up only on its own time limit, and
+// then sets *err.
+__device__ __forceinline__ bool mbar_wait_own(uint64_t* b, uint32_t parity, int* err) {
+    if (mbar_try(b, parity)) return true;
+    const uint64_t t0 = gtime();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 63) == 0 && gtime() - t0 > WAIT_LIMIT_NS) {
+            atomicExch(err, 1);
+            return false;
+        }
+    }
+}
+
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
@@ -259,10 +275,16 @@ struct alignas(64) TcJob {
     GemvJob g;         // scales, biases, OUT, IN, epilogue
 };
 
+// err: device flag that a wait which gives up sets (the other roles of every
+// CTA of the launch watch it and wind down); a CTA that gave up, or that found
+// the flag already set at entry and skipped its work, also writes 1 to
+// err_host (mapped pinned host memory), so the host learns of it without a
+// copy.  Neither is cleared by the kernel.
 struct TcArgs {
     TcJob j[TC_JOBS];
     int njobs, R, S;
     int* err;
+    int* err_host;
 };
 
 template <int FMT, int BN, int GPS, int ST>
@@ -313,6 +335,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     uint64_t* aempty = afull + ST_A;
     uint64_t* done = aempty + ST_A;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::T_OFF);
+    int* skip_slot = reinterpret_cast<int*>(smem + C::T_OFF + 8);
 
     const TcJob& jb = args.j[blockIdx.y];
     const int OUT = jb.g.OUT, IN = jb.g.IN;
@@ -341,6 +364,10 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         }
         tc::mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // a wait of an earlier launch gave up and nobody has cleared the flag:
+        // every role skips its work (no copies, no MMAs, no output), so the
+        // launch ends at once and the host is told again
+        *skip_slot = *(volatile int*)err;
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -351,12 +378,13 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
     __syncthreads();
     tc::tc_after();
     const uint32_t tmem = *tmem_slot;
-    bool ok = true;
+    const bool skip = *skip_slot != 0;
+    bool ok = !skip;
     constexpr int CW = BN / TC_QW;  // accumulator columns per dequant warp
     uint32_t acc[CW];
 
     if (warp == 0) {
-        if (lane == 0) {  // ---- TMA producer
+        if (lane == 0 && !skip) {  // ---- TMA producer
             // weights do not depend on the previous kernel: the first stages'
             // weights stream (and are dequantised) before its activations are ready
             auto load_w = [&](int i) {
@@ -385,25 +413,31 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             int issued = pre;
             for (int i = pre; i < nst; i++) {
                 const int s = i % ST;
-                if (!tc::mbar_wait(sempty + s, ((i / ST) - 1) & 1, err)) break;
+                if (!tc::mbar_wait(sempty + s, ((i / ST) - 1) & 1, err)) {
+                    ok = false;
+                    break;
+                }
                 load_w(i);
                 load_x(i);
                 issued = i + 1;
             }
-            // the copies this thread issued have landed before the CTA may exit
+            // the copies this thread issued have landed before the CTA may
+            // exit or reuse the stage buffers (whatever the other roles did)
             for (int i = max(0, issued - ST); i < issued; i++) {
-                tc::mbar_wait(wfull + (i % ST), (i / ST) & 1, err);
-                tc::mbar_wait(xfull + (i % ST), (i / ST) & 1, err);
+                if (!tc::mbar_wait_own(wfull + (i % ST), (i / ST) & 1, err)) ok = false;
+                if (!tc::mbar_wait_own(xfull + (i % ST), (i / ST) & 1, err)) ok = false;
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
             constexpr uint32_t IDESC = tc::idesc_f16(TC_BM, BN);
-            for (int i = 0; i < nst; i++) {
+            for (int i = 0; i < (skip ? 0 : nst); i++) {
                 const int s = i % ST, a = i % ST_A;
-                if (!tc::mbar_wait(wfull + s, (i / ST) & 1, err) || !tc::mbar_wait(xfull + s, (i / ST) & 1, err))
+                if (!tc::mbar_wait(wfull + s, (i / ST) & 1, err) || !tc::mbar_wait(xfull + s, (i / ST) & 1, err) ||
+                    (FMT == TC_Q4 && !tc::mbar_wait(afull + a, (i / ST_A) & 1, err))) {
+                    ok = false;
                     break;
-                if (FMT == TC_Q4 && !tc::mbar_wait(afull + a, (i / ST_A) & 1, err)) break;
+                }
                 tc::tc_after();
                 const uint32_t xs = tc::saddr(smem + s * C::STAGE + C::C_BYTES);
                 const uint32_t ta = tmem + TC_A_COL + a * (32 * GPS);
@@ -452,6 +486,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
             tc::cp_commit();
         };
         if constexpr (FMT == TC_Q4) {
+        if (!skip) {
 #pragma unroll
         for (int i = 0; i < TC_SRING - 1; i++) fetch(i);
         for (int i = 0; i < nst; i++) {
@@ -481,9 +516,15 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         }
         tc::cp_wait<0>();
         }
-        ok = tc::mbar_wait(done, 0, err) && ok;
+        }
+        // every MMA has finished before the accumulator is read, the stage
+        // buffers are reused for the split-K exchange and TMEM is freed
+        ok = tc::mbar_wait_own(done, 0, err) && ok;
         tc::tc_after();
-        pdl_wait();  // (returns at once: the producer's wait preceded every MMA)
+        // returns at once when the producer's wait preceded the MMAs; in the
+        // skip path it keeps the grid from completing before its predecessor,
+        // whose completion the grid's dependents rely on
+        pdl_wait();
         // ---- accumulator: row rl, this warp's half of the BN columns
         const GemvJob g = jb.g;  // a register copy: stores below cannot alias it
         const uint32_t tacc = tmem + lane_base;
@@ -562,10 +603,14 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         }
     }
     tc::tc_before();
-    __syncthreads();
+    const int bad = __syncthreads_or(!ok && (warp >= 2 || lane == 0));
     if (warp == 1) {
         tc::tc_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+    }
+    if (tid == 0 && bad) {
+        *(volatile int*)args.err_host = 1;
+        __threadfence_system();
     }
 }
 
@@ -583,6 +628,63 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     }();
     return fn;
 }
+
+static __global__ void tc_set_flag_kernel(int* p, int v) { *p = v; }
+
+// The wait-error record of the tensor-core GEMMs that share it: the device
+// flag the kernel's waits watch (TcArgs::err) and a mapped pinned host int
+// (TcArgs::err_host) that a CTA which gave up sets, so that the host can test
+// it with a plain load.  The kernel never clears either: take() and status()
+// report and clear them.
+struct TcWaitFlag {
+    int* dev = nullptr;       // device memory, owned by the caller
+    int* host = nullptr;      // host view of the mapped int
+    int* host_dev = nullptr;  // the same int, as the device addresses it
+
+    bool init(int* dev_int) {
+        dev = dev_int;
+        if (cudaHostAlloc((void**)&host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+            host = nullptr;
+            return false;
+        }
+        *(volatile int*)host = 0;
+        if (cudaHostGetDevicePointer((void**)&host_dev, host, 0) != cudaSuccess) return false;
+        return true;
+    }
+    void release() {
+        if (host) cudaFreeHost(host);
+        host = host_dev = nullptr;
+    }
+    // Without synchronising: true when a CTA has recorded a wait that gave up
+    // (a launch still running may record one later).  Clears both flags, the
+    // device one in stream order on `st`.
+    bool take(cudaStream_t st) {
+        if (!host || *(volatile int*)host == 0) return false;
+        *(volatile int*)host = 0;
+        cudaMemsetAsync(dev, 0, sizeof(int), st);
+        return true;
+    }
+    // Synchronises `st`, then reports and clears either flag.
+    int status(cudaStream_t st, const char* who) {
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "%s: stream synchronisation failed", who);
+        int d = 0;
+        if (cudaMemcpy(&d, dev, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+            return fail(RWKV_E_CUDA, "%s: flag read failed", who);
+        const bool h = host && *(volatile int*)host != 0;
+        if (!d && !h) return ok();
+        if (host) *(volatile int*)host = 0;
+        cudaMemset(dev, 0, sizeof(int));
+        return fail(RWKV_E_TIMEOUT, "%s: a tensor-core GEMM pipeline wait gave up; its outputs are not valid", who);
+    }
+    // Marks the record as a wait that gives up would: the device flag, and
+    // with host_record also the host int.
+    int inject(int host_record, cudaStream_t st) {
+        tc_set_flag_kernel<<<1, 1, 0, st>>>(dev, 1);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "inject: synchronisation failed");
+        if (host_record && host) *(volatile int*)host = 1;
+        return check_launch("tc_set_flag_kernel");
+    }
+};
 
 struct TcPlan {
     int BN = 0, GPS = 0, S = 1, nnb = 0, mblocks = 0;
@@ -743,10 +845,11 @@ inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, bool pdl, cudaS
 }
 
 // jobs -> tensor maps -> launch.  err: device int that a wait which gives up
-// sets to 1.
+// sets to 1; err_host: device-visible pointer to a mapped pinned host int
+// that a CTA which gave up (or skipped its work) sets to 1.
 // pdl: launch as a programmatic dependent of the previous kernel in the stream.
 inline cudaError_t launch_tc(int FMT, const GemvJobs& jobs, int njobs, int R, const TcPlan& p,
-                             int* err, cudaStream_t st, bool pdl = false) {
+                             int* err, int* err_host, cudaStream_t st, bool pdl = false) {
     TcArgs a{};
     for (int i = 0; i < njobs; i++)
         if (!encode_tc_maps(FMT, a.j[i], jobs.j[i], R, p.BN, p.GPS)) return cudaErrorInvalidValue;
@@ -754,6 +857,7 @@ inline cudaError_t launch_tc(int FMT, const GemvJobs& jobs, int njobs, int R, co
     a.R = R;
     a.S = p.S;
     a.err = err;
+    a.err_host = err_host;
     const int BN = p.BN;
 #define X_(F, B, G, T) launch_tc_t<F, B, G, T>(a, p, pdl, st)
     RWKV_TC_CONFIGS(FMT, X_)

@@ -265,6 +265,7 @@ struct GemmScratch {
     float* ws = nullptr;
     int* tickets = nullptr;
     int* err = nullptr;  // set by a tensor-core GEMM wait that gave up
+    TcWaitFlag flag;     // err and its mapped host record
     size_t floats = 0, tickets_n = 0;
     int sm_count = 148;
     std::mutex mu;
@@ -289,6 +290,10 @@ static GemmScratch* gemm_scratch() {
         return nullptr;
     }
     s->err = s->tickets + s->tickets_n;
+    if (!s->flag.init(s->err)) {
+        delete s;
+        return nullptr;
+    }
     per_dev[dev] = s;
     return s;
 }
@@ -333,10 +338,15 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
         j.y_stride = OUT;
         GemmScratch* sc = gemm_scratch();
         if (!sc) return fail(RWKV_E_CUDA, "rwkv_q_gemm: workspace allocation failed");
+        // a wait of an earlier call on this device gave up: report it once
+        // (sticky until this call), clear it, launch nothing
+        if (sc->flag.take(st))
+            return fail(RWKV_E_TIMEOUT, "rwkv_q_gemm: a tensor-core GEMM wait of an earlier call gave up; "
+                                        "its outputs are not valid (flag cleared, nothing launched)");
         // more than 8 rows: tcgen05 (TMA + TMEM) when the shapes allow it
         const TcPlan tp = plan_tc(TC_Q4, jobs, 1, rows, sc->sm_count);
         if (tp.ok) {
-            cudaError_t e = launch_tc(TC_Q4, jobs, 1, rows, tp, sc->err, st);
+            cudaError_t e = launch_tc(TC_Q4, jobs, 1, rows, tp, sc->err, sc->flag.host_dev, st);
             if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemm_tc_kernel: %s", cudaGetErrorString(e));
             return ok();
         }
@@ -384,6 +394,18 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
             });
         });
     });
+}
+
+int q_gemm_status(cudaStream_t st) {
+    GemmScratch* sc = gemm_scratch();
+    if (!sc) return fail(RWKV_E_CUDA, "rwkv_q_gemm_status: workspace allocation failed");
+    return sc->flag.status(st, "rwkv_q_gemm");
+}
+
+int q_gemm_inject_wait_error(int host_record, cudaStream_t st) {
+    GemmScratch* sc = gemm_scratch();
+    if (!sc) return fail(RWKV_E_CUDA, "rwkv_q_gemm_inject_wait_error: workspace allocation failed");
+    return sc->flag.inject(host_record, st);
 }
 
 int launch_q_dequant(const uint32_t* wq, const void* scales, const void* biases, int sdtype,

@@ -18,7 +18,9 @@
 // No allocation: the array's device address is looked up once per device
 // (cudaGetSymbolAddress, with that device current) on the first call there;
 // that first call on a device should therefore come before any stream
-// capture.  The kernel is the same one rwkv_wkv7_backward launches.
+// capture.  The address is kept with the id of the context it was looked up
+// in; a call in another context on that device (after a cudaDeviceReset, say)
+// looks it up again.  The kernel is the same one rwkv_wkv7_backward launches.
 //
 // Sharing: every call on a device uses the same array, and the array keeps
 // the previous call's contents.  Nothing in it has to start at zero -- each
@@ -26,6 +28,8 @@
 // cleared.  Two calls in flight on the same device at the same time (on
 // different streams, or from different threads without ordering) race on the
 // array and give wrong gradients; order them on one stream.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -51,11 +55,36 @@ static __device__ __align__(256) float g_bwd_scratch[NOALLOC_BYTES / 4];
 
 constexpr int MAX_DEVICES = 64;
 
+// Unique id of the calling thread's current context (0 when the driver entry
+// points are unavailable: the cached address is then kept per device).
+unsigned long long current_context_id() {
+    static PFN_cuCtxGetCurrent_v4000 get_cur = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_cur = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_cur && get_id && get_cur(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, &id) == CUDA_SUCCESS) return id;
+    return 0;
+}
+
 // Device address of g_bwd_scratch on the current device, looked up on the
-// first call there (nullptr and the error recorded on failure).
+// first call there, and again when the device's current context has changed
+// (nullptr and the error recorded on failure).
 float* scratch_on_current_device() {
     static std::mutex mu;
     static float* addr[MAX_DEVICES] = {};
+    static unsigned long long ctx_of[MAX_DEVICES] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -66,8 +95,11 @@ float* scratch_on_current_device() {
         fail(RWKV_E_UNSUPPORTED, "rwkv_wkv7_backward_noalloc: device %d beyond %d", dev, MAX_DEVICES);
         return nullptr;
     }
+    // 0 until the runtime has made the device's context current (the lookup
+    // below does), else the id that tells a reset device's new context apart
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx_of[dev] != ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_bwd_scratch);
         if (e != cudaSuccess || p == nullptr) {
@@ -76,6 +108,7 @@ float* scratch_on_current_device() {
             return nullptr;
         }
         addr[dev] = static_cast<float*>(p);
+        ctx_of[dev] = current_context_id();
     }
     return addr[dev];
 }

@@ -123,6 +123,7 @@ struct X070 {
     float* gws = nullptr;
     int* gtickets = nullptr;
     int* gerr = nullptr;  // set by a tensor-core GEMM wait that gave up
+    TcWaitFlag gflag;     // gerr and its mapped host record
     size_t gws_floats = 0, gtickets_n = 0;
     int sm_count = 148;
     // step profiler: an event node after every launch of a captured step
@@ -222,6 +223,7 @@ struct X070 {
         gws = alloc<float>(gws_floats);
         gtickets = alloc<int>(gtickets_n + 1);
         gerr = gtickets + gtickets_n;
+        if (!alloc_failed && !gflag.init(gerr)) alloc_failed = true;
         cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking);
         cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
         cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
@@ -234,6 +236,7 @@ struct X070 {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
+        gflag.release();
         if (own) cudaStreamDestroy(own);
         if (ev_in) cudaEventDestroy(ev_in);
         if (ev_out) cudaEventDestroy(ev_out);
@@ -460,7 +463,7 @@ struct X070 {
             const int tfmt = fmt == 0 ? TC_Q4 : TC_F16;
             const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
             if (tp.ok) {
-                cudaError_t e = launch_tc(tfmt, jobs, nj, R, tp, gerr, st, /*pdl=*/true);
+                cudaError_t e = launch_tc(tfmt, jobs, nj, R, tp, gerr, gflag.host_dev, st, /*pdl=*/true);
                 return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm_tc: %s", cudaGetErrorString(e));
             }
             GemmPlan p = plan_any(jobs, nj, R, sm_count);
@@ -839,6 +842,10 @@ int rwkv_x070_step(rwkv_x070_t h, const int32_t* ids, int rows, float* logits, i
     X070& m = *reinterpret_cast<X070*>(h);
     RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax, RWKV_E_SHAPE, "rows %d not in 1..%d", rows, m.Rmax);
     cudaStream_t st = (cudaStream_t)stream;
+    // a GEMM wait of an earlier step gave up: report it once, clear it, run nothing
+    if (m.gflag.take(st))
+        return fail(RWKV_E_TIMEOUT, "rwkv_x070_step: a tensor-core GEMM wait of an earlier step gave up; "
+                                    "the state is not valid (flag cleared, nothing launched)");
     if (ids) cudaMemcpyAsync(m.ids, ids, rows * 4, cudaMemcpyDeviceToDevice, st);
     int rc = use_graph ? m.graph_step_any(rows, st) : m.run_step(rows, st);
     if (rc) return rc;
@@ -854,6 +861,9 @@ int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int 
     RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax && prompt_len >= 1 && n_new >= 0, RWKV_E_SHAPE,
                  "rwkv_x070_generate: rows %d prompt %d new %d", rows, prompt_len, n_new);
     cudaStream_t st = (cudaStream_t)stream;
+    if (m.gflag.take(st))
+        return fail(RWKV_E_TIMEOUT, "rwkv_x070_generate: a tensor-core GEMM wait of an earlier step gave up "
+                                    "(flag cleared, nothing launched)");
     std::vector<int32_t> col(rows);
     for (int t = 0; t < prompt_len; t++) {
         for (int n = 0; n < rows; n++) col[n] = prompt_host[(size_t)n * prompt_len + t];
@@ -867,11 +877,18 @@ int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int 
         if (s + 1 < n_new)
             if (int rc = m.graph_step_any(rows, st)) return rc;
     }
-    int gave_up = 0;
-    cudaMemcpyAsync(&gave_up, m.gerr, sizeof(int), cudaMemcpyDeviceToHost, st);
-    if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "generate: sync failed");
-    if (gave_up) return fail(RWKV_E_TIMEOUT, "generate: a tensor-core GEMM pipeline wait timed out");
+    if (int rc = m.gflag.status(st, "rwkv_x070_generate")) return rc;
     return check_launch("rwkv_x070_generate");
+}
+
+int rwkv_x070_status(rwkv_x070_t h, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_status: NULL handle");
+    return reinterpret_cast<X070*>(h)->gflag.status((cudaStream_t)stream, "rwkv_x070");
+}
+
+int rwkv_x070_inject_wait_error(rwkv_x070_t h, int host_record, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_inject_wait_error: NULL handle");
+    return reinterpret_cast<X070*>(h)->gflag.inject(host_record, (cudaStream_t)stream);
 }
 
 int rwkv_x070_profile_step(rwkv_x070_t h, int rows, float* ms_host, int cap, char* names_host,

@@ -289,7 +289,7 @@ def wkv7Step(r, w, k, v, a, b, hIn=None):
 
 
 def wkv7StepForward(r, w, k, v, a, b, h):
-    """One token (WKV7DecodeKernels.swift:157-173): r..b [H, S] (or [rows, H, S]),
+    """One token (WKV7DecodeKernels.swift:73-89): r..b [H, S] (or [rows, H, S]),
     h [H, S, S] (or [rows, H, S, S]).  Returns (out, h') fp32; h is not modified."""
     single = r.dim() == 2
     if single:
@@ -311,12 +311,12 @@ def wkv7StepForward(r, w, k, v, a, b, h):
 
 
 def wkvTailApplies(headSize: int) -> bool:
-    """WKV7DecodeKernels.swift:176."""
+    """WKV7DecodeKernels.swift:92."""
     return headSize % 32 == 0
 
 
 def wkvTail(wkv, r, k, v, rK, lnWeight, lnBias, gate, nHead, headSize, rows=1, eps=64e-5):
-    """Fused tmix tail (WKV7DecodeKernels.swift:190-262): returns [rows, D] fp32."""
+    """Fused tmix tail (WKV7DecodeKernels.swift:106-178): returns [rows, D] fp32."""
     H, S = nHead, headSize
     if not wkvTailApplies(S):
         raise ValueError(f"tail: S={S} not a multiple of the warp width")

@@ -219,7 +219,7 @@ def symGEMVFused(xstack, qblk, qs, d, outPer, inFeatures, bits):
 
 @dataclass
 class RwkvqSymRowTable:
-    """8-bit sym embedding rows on demand (RwkvqSymRows.swift:385-422)."""
+    """8-bit sym embedding rows on demand (RwkvqSymRows.swift:26-78)."""
     codes: torch.Tensor  # uint8 [rows, IN]
     qs: torch.Tensor     # uint8 [rows, IN/16]
     d: torch.Tensor      # fp16 [rows, ceil(IN/256)]

@@ -117,13 +117,21 @@ class X070Backbone:
              None, int(use_graph), self._s())
         return logits
 
-    def step_greedy(self, rows: int, ids=None, use_graph: bool = True):
-        """Device-resident greedy loop: feeds `ids` (or the previous argmax)."""
+    def step_greedy(self, rows: int, ids=None, use_graph: bool = True, next_ids=None):
+        """Device-resident greedy loop: feeds `ids` (or the previous argmax);
+        the argmax of this step also goes to `next_ids` (device int32 [rows])
+        when given."""
         p = None
         if ids is not None:
             ids = torch.as_tensor(ids, dtype=torch.int32, device="cuda").reshape(-1).contiguous()
             p = _lib.P(ids.data_ptr())
-        call("rwkv_x070_step", self.h, p, rows, None, None, int(use_graph), self._s())
+        q = None
+        if next_ids is not None:
+            if next_ids.dtype != torch.int32 or not next_ids.is_cuda or not next_ids.is_contiguous() \
+                    or next_ids.numel() < rows:
+                raise ValueError("next_ids must be a contiguous device int32 tensor of >= rows elements")
+            q = _lib.P(next_ids.data_ptr())
+        call("rwkv_x070_step", self.h, p, rows, None, q, int(use_graph), self._s())
 
     def profile_step(self, rows: int):
         """One eager step with per-launch device times: {kernel: (launches, ms)}

@@ -42,11 +42,12 @@ def _grads_like(r, B, H):
         torch.full((B, H, 64, 64), float("nan"), device=r.device, dtype=torch.float32)]
 
 
-def _backward(noalloc, ins, h0, ck, dy, dh, B, T, H):
+def _backward(noalloc, ins, h0, ck, dy, dh, B, T, H, dtype=None):
     from swiftrwkv_b200 import _lib
     out = _grads_like(ins[0], B, H)
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    common = (_lib.F32, *map(_p, ins), _p(h0), _p(ck), _p(dy), _p(dh), *map(_p, out), B, T, H, 64)
+    dtype = _lib.F32 if dtype is None else dtype
+    common = (dtype, *map(_p, ins), _p(h0), _p(ck), _p(dy), _p(dh), *map(_p, out), B, T, H, 64)
     if noalloc:
         _lib.call("rwkv_wkv7_backward_noalloc", *common, st)
     else:
@@ -71,6 +72,50 @@ def test_noalloc_backward_matches_workspace_backward_twice():
             g, w = g.cpu().numpy(), w.cpu().numpy()
             assert np.isfinite(g).all(), name
             assert rel_err(g, w) < GRAD_TOL, (B, T, H, name)
+
+
+def _compare(got, want, tol, what):
+    torch.cuda.synchronize()
+    for name, g, w in zip(("dr", "dw", "dk", "dv", "da", "db", "dh_in"), got, want):
+        g, w = g.float().cpu().numpy(), w.float().cpu().numpy()
+        assert np.isfinite(g).all(), (what, name)
+        assert rel_err(g, w) < tol, (what, name, rel_err(g, w))
+
+
+def test_noalloc_backward_bf16_matches_workspace_backward():
+    """bf16 inputs and gradients (the bf16 bound of the backward, 2e-2)."""
+    from swiftrwkv_b200 import _lib, kernel as K
+    assert torch.cuda.is_available(), "gpu tests need a CUDA device"
+    _lib.lib()
+    rng = np.random.default_rng(7)
+    B, T, H = 2, 32, 3
+    ins, h0, dy, dh = _case(rng, B, T, H)
+    ins = [x.to(torch.bfloat16) for x in ins]
+    dy = dy.to(torch.bfloat16)
+    _, _, _, ck = K._train_forward(*ins, h0)
+    want = _backward(False, ins, h0, ck, dy, dh, B, T, H, _lib.BF16)
+    got = _backward(True, ins, h0, ck, dy, dh, B, T, H, _lib.BF16)
+    _compare(got, want, 2e-2, "bf16")
+
+
+def test_noalloc_backward_zero_state_after_a_nonzero_call():
+    """h_in = NULL and dh_out = NULL (zero state, no upstream state gradient)
+    right after a call with non-zero ones: the scratch keeps that call's
+    states, and the zero-start call must not see them."""
+    from swiftrwkv_b200 import _lib, kernel as K
+    assert torch.cuda.is_available(), "gpu tests need a CUDA device"
+    _lib.lib()
+    rng = np.random.default_rng(11)
+    B, T, H = 2, 48, 4
+    ins, h0, dy, dh = _case(rng, B, T, H)
+    _, _, _, ck = K._train_forward(*ins, h0)
+    _compare(_backward(True, ins, h0, ck, dy, dh, B, T, H), _backward(False, ins, h0, ck, dy, dh, B, T, H),
+             GRAD_TOL, "non-zero state")
+    ins2, _, dy2, _ = _case(rng, B, T, H)
+    _, _, _, ck2 = K._train_forward(*ins2, None)
+    want = _backward(False, ins2, None, ck2, dy2, None, B, T, H)
+    got = _backward(True, ins2, None, ck2, dy2, None, B, T, H)
+    _compare(got, want, GRAD_TOL, "zero state")
 
 
 def test_noalloc_backward_rejects_more_heads_than_its_scratch():
