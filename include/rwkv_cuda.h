@@ -339,10 +339,41 @@ int rwkv_x070_reset_state(rwkv_x070_t model, int rows, rwkv_stream_t stream);
  * the first, capturing call). */
 int rwkv_x070_step(rwkv_x070_t model, const int32_t* ids, int rows, float* logits,
                    int32_t* next_ids, int use_graph, rwkv_stream_t stream);
-/* Greedy generation with HOST buffers: prompts [rows, prompt_len] fed
- * recurrently, then n_new tokens per row into out [rows, n_new]. */
+/* Parallel prefill of right-padded prompts: ids device int32 [rows, T];
+ * lengths_host HOST int32 [rows], each in 1..T (NULL = all T; positions past
+ * a row's length are padding).  Runs whole blocks of positions per launch
+ * (sequence-mode glue, the projections as tensor-core GEMMs over every token
+ * of the block, the chunked WKV-7 forward), masking padding so that w = 1,
+ * k = 0, b = 0 there -- the state of a row stops at its last real token --
+ * and takes each row's token-shift state at that token.  Continues from the
+ * rows' current state (reset first for a fresh start).  logits: device fp32
+ * [rows, vocab] of each row's last real token, or NULL; next_ids: device
+ * int32 [rows] (their argmax) or NULL; the argmax is also kept as the next
+ * step's input (rwkv_x070_step with ids = NULL).  Block buffers are
+ * allocated on first use and kept by the model.
+ * Replaces prefill / prefillBatch over bodyWithState (Sources/RWKVGen/
+ * X070Generation.swift:344-355, BatchGenerate.swift:36-51,
+ * X070Backbone.swift:1011-1048; padding mask RWKVBlock.swift:221-237,
+ * lastRealIndex RWKVBatchState.swift:159-175). */
+int rwkv_x070_prefill(rwkv_x070_t model, const int32_t* ids, const int32_t* lengths_host, int rows, int T,
+                      float* logits, int32_t* next_ids, rwkv_stream_t stream);
+/* Greedy generation with HOST buffers: prompts [rows, prompt_len] prefilled
+ * in parallel (rwkv_x070_prefill), then n_new tokens per row into out
+ * [rows, n_new].  Continues from the rows' current state. */
 int rwkv_x070_generate(rwkv_x070_t model, const int32_t* prompt_host, int rows, int prompt_len,
                        int n_new, int32_t* out_host, rwkv_stream_t stream);
+/* generateBatch with ragged prompts and stop tokens, HOST buffers: prompts
+ * [rows, max_len] right-padded, lengths_host [rows] (NULL = all max_len);
+ * rows start from a zero state; greedy; a row stops after emitting one of
+ * the n_stop ids in stop_host (the stop id is kept) or after n_new tokens,
+ * and a stopped row leaves the batch (its state rows are compacted away, so
+ * later steps run on the live rows only).  out_host [rows, n_new] receives
+ * each row's tokens, out_len_host [rows] their counts.
+ * Replaces X070Backbone.generateBatch (Sources/RWKVGen/BatchGenerate.swift:
+ * 69-116) with the argmax sampler. */
+int rwkv_x070_generate_batch(rwkv_x070_t model, const int32_t* prompts_host, const int32_t* lengths_host,
+                             int rows, int max_len, int n_new, const int32_t* stop_host, int n_stop,
+                             int32_t* out_host, int32_t* out_len_host, rwkv_stream_t stream);
 /* Wait errors of the model's tensor-core GEMMs (bounded pipeline waits; see
  * rwkv_q_gemm_status): a step after one gave up returns RWKV_E_TIMEOUT,
  * clears the record and launches nothing; rwkv_x070_generate checks it at

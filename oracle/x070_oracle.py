@@ -37,13 +37,20 @@ class Cfg:
         self.ranks = lora_ranks(n_embd)
 
 
-def tiny_weights(cfg: Cfg, seed: int = 42):
-    """Random weights on the TinyBackbone recipe (all matrices non-zero)."""
+def tiny_weights(cfg: Cfg, seed: int = 42, fan_in_scale: bool = False):
+    """Random weights on the TinyBackbone recipe (all matrices non-zero).
+
+    TinyBackbone draws every matrix with std 0.05, which suits its width
+    (D = 128 .. 256).  fan_in_scale=True keeps that conditioning at any width:
+    a matrix's std becomes 0.05 * sqrt(256 / fan_in), so projections keep
+    unit gain at D = 2048 as they do at D = 256."""
     rng = np.random.default_rng(seed)
     D, H, S, V, F = cfg.n_embd, cfg.n_head, cfg.head_size, cfg.vocab, cfg.ffn
     r = cfg.ranks
 
     def n(shape, scale=0.05):
+        if fan_in_scale and np.ndim(shape) == 1 and len(shape) == 2 and scale == 0.05:
+            scale = 0.05 * np.sqrt(256.0 / shape[1])
         return (rng.standard_normal(shape) * scale).astype(np.float32)
 
     w = {"emb.weight": n((V, D), 0.1), "ln0.weight": np.ones(D, np.float32),
@@ -103,15 +110,24 @@ def _is_quant(name):
 class X070Oracle:
     """Recurrent decode for `rows` independent rows."""
 
+    # fp16 activations and more rows than this: the quantised projections are
+    # products with the weight dequantised INTO fp16 (MLX's quantized matmul,
+    # which the runtime's tensor-core path follows); up to it, with the exact
+    # dequantised weight (MLX's quantized matrix-vector product).
+    GEMV_MAX_ROWS = 8
+
     def __init__(self, cfg: Cfg, weights: dict, act="f16", quant_bits=4, group=64):
         self.cfg, self.act = cfg, act
         self.w = {}
+        self.w16 = {}
         for k, v in weights.items():
             v = np.asarray(v, np.float32)
             if quant_bits and v.ndim == 2 and _is_quant(k):
                 v16 = v.astype(np.float16).astype(np.float32)
                 wq, sc, bi = O.affine_quantize(v16, group, quant_bits)
                 v = O.affine_dequant(wq, sc, bi, group, quant_bits)
+                if act == "f16" and k != "emb.weight":
+                    self.w16[k] = v.astype(np.float16).astype(np.float64)
             elif v.ndim == 2:          # dense low-rank branches: fp16 storage
                 v = v.astype(np.float16).astype(np.float32)
             self.w[k] = v.astype(np.float64)
@@ -129,7 +145,8 @@ class X070Oracle:
         return x.astype(np.float32).astype(np.float64)
 
     def _mm(self, x, key):
-        return self._a(x) @ self.w[key].T
+        w = self.w16.get(key) if x.shape[0] > self.GEMV_MAX_ROWS else None
+        return self._a(x) @ (self.w[key] if w is None else w).T
 
     def _proj(self, x, key):
         """Projection with its optional LoRA adapter (X070Backbone.swift:746-752):

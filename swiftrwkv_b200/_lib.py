@@ -69,6 +69,8 @@ _SIGS = {
     "rwkv_x070_reset_state": [P, I, P],
     "rwkv_x070_step": [P, P, I, P, P, I, P],
     "rwkv_x070_generate": [P, P, I, I, I, P, P],
+    "rwkv_x070_prefill": [P, P, P, I, I, P, P, P],
+    "rwkv_x070_generate_batch": [P, P, P, I, I, I, P, I, P, P, P],
     "rwkv_x070_profile_step": [P, I, P, I, P, I, P, P],
     "rwkv_x070_status": [P, P],
     "rwkv_x070_inject_wait_error": [P, I, P],

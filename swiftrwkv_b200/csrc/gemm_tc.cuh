@@ -751,7 +751,9 @@ inline int tc_gps(int FMT, int BN) { return FMT == TC_F16 ? 1 : BN <= 64 ? 4 : 2
 
 inline TcPlan plan_tc(int FMT, const GemvJobs& jobs, int njobs, int R, int sm_count) {
     TcPlan p{};
-    if (R <= 8 || R > 256 || njobs < 1 || njobs > TC_JOBS) return p;
+    // decode batches (R <= 256) and prefill token blocks (R up to 64 Ki rows,
+    // 128-row n-blocks, no split-K once the n-blocks fill the GPU)
+    if (R <= 8 || R > 65536 || njobs < 1 || njobs > TC_JOBS) return p;
     for (int i = 0; i < njobs; i++)
         if (!tc_job_ok(FMT, jobs.j[i])) return p;
     p.BN = R <= 16 ? 16 : R <= 32 ? 32 : R <= 64 ? 64 : 128;

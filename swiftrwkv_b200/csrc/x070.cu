@@ -23,6 +23,14 @@
 namespace rwkv {
 
 int launch_q_quantize(int, const void*, uint32_t*, void*, void*, int, int, int, int, cudaStream_t);
+int64_t wkv7_chunk_workspace(int, int, int);
+int launch_wkv7_chunk_fwd(int, const void*, const void*, const void*, const void*, const void*, const void*,
+                          const float*, void*, float*, float*, float*, int, int, int, void*, cudaStream_t);
+
+// Prefill processes the prompts in blocks of Ts positions of every row, with
+// rows * Ts <= PF_TOKENS token rows per block (Ts a multiple of 16), so its
+// buffers stay bounded whatever the prompt length.
+constexpr int PF_TOKENS = 8192;
 
 // -------------------------------------------------------- device init helpers
 
@@ -236,6 +244,8 @@ struct X070 {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
+        pf_free();
+        if (pf_prompt) cudaFree(pf_prompt);
         gflag.release();
         if (own) cudaStreamDestroy(own);
         if (ev_in) cudaEventDestroy(ev_in);
@@ -511,14 +521,19 @@ struct X070 {
         float* y;
         int ys;
     };
+    // zbuf: [3][zrows][LORA_MAX_RANK] of the activation type, zrows >= R.
     template <typename A>
-    int lora_apply(const LoraJob* lj, int n, int R, cudaStream_t st) {
+    int lora_apply(const LoraJob* lj, int n, int R, cudaStream_t st, void* zbuf = nullptr, int zrows = 0) {
+        if (!zbuf) {
+            zbuf = lora_z;
+            zrows = Rmax;
+        }
         GemvJobs D{}, U{};
         int nd = 0;
         for (int i = 0; i < n; i++) {
             const Adapter& ad = *lj[i].ad;
             if (!ad.on()) continue;
-            A* z = (A*)lora_z + (size_t)nd * Rmax * LORA_MAX_RANK;
+            A* z = (A*)zbuf + (size_t)nd * zrows * LORA_MAX_RANK;
             GemvJob d = hjob(ad.A, ad.rank_a, lj[i].IN, lj[i].x, lj[i].xs, ACT_SCALE, f16act ? OUT_F16 : OUT_F32, z,
                              ad.rank_a);
             d.alpha = ad.scale;
@@ -771,6 +786,247 @@ struct X070 {
         return rc;
     }
 
+    // ----- parallel prefill (bodyWithState over right-padded prompts)
+
+    std::vector<void*> pf_allocs;
+    int pf_cap = 0;      // token rows the block buffers hold
+    int pf_prompt_cap = 0;
+    float *pf_x = nullptr, *pf_ln1 = nullptr, *pf_ln2 = nullptr, *pf_r = nullptr, *pf_k = nullptr, *pf_v = nullptr;
+    float *pf_w = nullptr, *pf_a = nullptr, *pf_g = nullptr, *pf_vv = nullptr, *pf_vfirst = nullptr;
+    float *pf_aw = nullptr, *pf_bw = nullptr, *pf_y = nullptr, *pf_keytmp = nullptr;
+    void *pf_mix = nullptr, *pf_hidden = nullptr, *pf_tail = nullptr, *pf_xk = nullptr, *pf_ffn = nullptr;
+    void *pf_z = nullptr, *pf_ws = nullptr;
+    int32_t *pf_ids = nullptr, *pf_len = nullptr, *pf_prompt = nullptr, *pf_keep = nullptr;
+    float* pf_gather = nullptr;  // one layer of WKV state rows, for the row drop
+
+    void pf_free() {
+        for (void* p : pf_allocs) cudaFree(p);
+        pf_allocs.clear();
+        pf_cap = 0;
+    }
+    template <typename T>
+    T* pf_alloc(size_t n, bool& bad) {
+        void* p = nullptr;
+        if (bad || cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)) != cudaSuccess) {
+            bad = true;
+            return nullptr;
+        }
+        pf_allocs.push_back(p);
+        return (T*)p;
+    }
+    // Block buffers for `ntok` token rows (allocated on first use, grown when
+    // a larger block comes; the model keeps them until it is destroyed).
+    int ensure_prefill(int ntok, int Ts, int rows) {
+        const int64_t ws_need = wkv7_chunk_workspace(rows, Ts, H);
+        if (ntok <= pf_cap && ws_need <= pf_ws_bytes) return RWKV_OK;
+        cudaDeviceSynchronize();  // a previous block may still use the old buffers
+        pf_free();
+        bool bad = false;
+        const size_t NC = (size_t)ntok * C;
+        float** f32s[] = {&pf_x, &pf_ln1, &pf_ln2, &pf_r, &pf_k, &pf_v, &pf_w, &pf_a, &pf_g, &pf_vv, &pf_vfirst,
+                          &pf_aw, &pf_bw, &pf_y};
+        for (float** q : f32s) *q = pf_alloc<float>(NC, bad);
+        pf_mix = pf_alloc<char>(6 * NC * act_bytes, bad);
+        pf_hidden = pf_alloc<char>((size_t)ntok * hid * act_bytes, bad);
+        pf_tail = pf_alloc<char>(NC * act_bytes, bad);
+        pf_xk = pf_alloc<char>(NC * act_bytes, bad);
+        pf_ffn = pf_alloc<char>((size_t)ntok * F * act_bytes, bad);
+        pf_z = pf_alloc<char>((size_t)3 * ntok * LORA_MAX_RANK * act_bytes, bad);
+        pf_keytmp = pf_alloc<float>((size_t)ntok * F, bad);
+        pf_ws_bytes = std::max<int64_t>(ws_need, wkv7_chunk_workspace(std::max(1, ntok / 16), 16, H));
+        pf_ws = pf_alloc<char>((size_t)pf_ws_bytes, bad);
+        pf_ids = pf_alloc<int32_t>(ntok, bad);
+        pf_len = pf_alloc<int32_t>(Rmax, bad);
+        pf_keep = pf_alloc<int32_t>(Rmax, bad);
+        pf_gather = pf_alloc<float>(std::max((size_t)Rmax * H * 4096, (size_t)Rmax * C), bad);
+        if (bad) {
+            pf_free();
+            return fail(RWKV_E_CUDA, "prefill: block buffer allocation failed (%d token rows)", ntok);
+        }
+        pf_cap = ntok;
+        return RWKV_OK;
+    }
+    int64_t pf_ws_bytes = 0;
+
+    // Block size: Ts positions per row, a multiple of 16, rows * Ts <= PF_TOKENS.
+    int prefill_block(int rows, int T) const {
+        const int T16 = (T + 15) / 16 * 16;
+        const int fit = std::max(16, PF_TOKENS / rows / 16 * 16);
+        return std::min(T16, fit);
+    }
+
+    // One block of Ts positions through every layer (rows' state advances);
+    // rows whose last real token lies in the block get ln_out of it in lnout.
+    template <typename A>
+    int prefill_block_body(const int32_t* prompt, int T, int rows, int p0, int Ts, cudaStream_t st) {
+        const int N = rows * Ts;
+        const size_t NC = (size_t)N * C;
+        const int aout = f16act ? OUT_F16 : OUT_F32;
+        A* mixp = (A*)pf_mix;
+        A* hidp = (A*)pf_hidden;
+        x070_pf_ids_kernel<<<(N + 255) / 256, 256, 0, st>>>(prompt, T, p0, Ts, rows, pf_ids);
+        x070_embed_kernel<<<N, GLUE_T, 0, st>>>(pf_ids, emb.wq, emb.sc, emb.bi, nullptr, ln0w, ln0b, pf_x, C, V);
+        int rc = check_launch("x070 prefill embed");
+        if (rc) return rc;
+        auto rows_launch = [&](auto&& f, const char* name) { return row_launch(f, name); };
+        for (int l = 0; l < L; l++) {
+            LayerW& w = lw[l];
+            float* ts = tshift + (size_t)l * Rmax * C;
+            float* cs = cshift + (size_t)l * Rmax * C;
+            float* st8 = wkv + (size_t)l * Rmax * H * 64 * 64;
+            if ((rc = rows_launch([&]<int GV>() {
+                     x070_ln_out_kernel<float, GV><<<N, GLUE_T, 0, st>>>(pf_x, w.ln1w, w.ln1b, pf_ln1, C);
+                     x070_pf_tmix_mix_kernel<A, GV><<<N, GLUE_T, 0, st>>>(pf_ln1, ts, w.coef6, mixp, N, Ts, C);
+                     return cudaGetLastError();
+                 }, "x070 prefill tmix input")))
+                return rc;
+            auto M = [&](int m) { return (const void*)(mixp + (size_t)m * NC); };
+            GemvJobs J{};
+            J.j[0] = qjob(w.r, M(0), C, ACT_NONE, OUT_F32, pf_r, C);
+            J.j[1] = qjob(w.k, M(2), C, ACT_NONE, OUT_F32, pf_k, C);
+            J.j[2] = qjob(w.v, M(3), C, ACT_NONE, OUT_F32, pf_v, C);
+            if ((rc = gemv(0, J, 3, N, st))) return rc;
+            {
+                const LoraJob lj[3] = {{&w.ad[AD_R], M(0), C, C, C, pf_r, C}, {&w.ad[AD_K], M(2), C, C, C, pf_k, C},
+                                       {&w.ad[AD_V], M(3), C, C, C, pf_v, C}};
+                if ((rc = lora_apply<A>(lj, 3, N, st, pf_z, pf_cap))) return rc;
+            }
+            GemvJobs D{};
+            int nd = 0;
+            D.j[nd++] = hjob(w.wA, rw, C, M(1), C, ACT_TANH, aout, hidp, hid);
+            D.j[nd++] = hjob(w.aA, ra, C, M(4), C, ACT_NONE, aout, hidp + rw, hid);
+            D.j[nd++] = hjob(w.gA, rg, C, M(5), C, ACT_SIGMOID, aout, hidp + rw + ra, hid);
+            if (l > 0) D.j[nd++] = hjob(w.vA, rv, C, M(3), C, ACT_NONE, aout, hidp + rw + ra + rg, hid);
+            if ((rc = gemv(1, D, nd, N, st))) return rc;
+            GemvJobs U{};
+            int nu = 0;
+            U.j[nu++] = hjob(w.wB, C, rw, hidp, hid, ACT_DECAY, OUT_F32, pf_w, C, w.wbias);
+            U.j[nu++] = hjob(w.aB, C, ra, hidp + rw, hid, ACT_SIGMOID_BIAS, OUT_F32, pf_a, C, w.abias);
+            U.j[nu++] = hjob(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, pf_g, C);
+            if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, pf_vv, C, w.vbias);
+            if ((rc = gemv(1, U, nu, N, st))) return rc;
+            x070_pf_prep_kernel<<<dim3(N, (H + 7) / 8), 256, 0, st>>>(pf_w, pf_k, pf_v, pf_a, pf_vv, pf_vfirst, pf_aw,
+                                                                     pf_bw, w.kkw, w.kaw, pf_len, p0, Ts, H, (int)(l == 0));
+            if ((rc = check_launch("x070_pf_prep_kernel"))) return rc;
+            // the state advances in place: each scan CTA reads and writes only its own state rows
+            if ((rc = launch_wkv7_chunk_fwd(RWKV_F32, pf_r, pf_w, pf_k, pf_v, pf_aw, pf_bw, st8, pf_y, st8, nullptr,
+                                            nullptr, rows, Ts, H, pf_ws, st)))
+                return rc;
+            x070_pf_tail_kernel<A><<<dim3(N, (H + 7) / 8), 256, 0, st>>>(pf_y, pf_r, pf_k, pf_v, w.rkw, w.lnxw, w.lnxb,
+                                                                        pf_g, (A*)pf_tail, H);
+            if ((rc = check_launch("x070_pf_tail_kernel"))) return rc;
+            GemvJobs O{};
+            O.j[0] = qjob(w.o, pf_tail, C, ACT_NONE, OUT_ADD_F32, pf_x, C);
+            if ((rc = gemv(0, O, 1, N, st))) return rc;
+            {
+                const LoraJob lj[1] = {{&w.ad[AD_O], pf_tail, C, C, C, pf_x, C}};
+                if ((rc = lora_apply<A>(lj, 1, N, st, pf_z, pf_cap))) return rc;
+            }
+            if ((rc = rows_launch([&]<int GV>() {
+                     x070_ln_out_kernel<float, GV><<<N, GLUE_T, 0, st>>>(pf_x, w.ln2w, w.ln2b, pf_ln2, C);
+                     x070_pf_cmix_mix_kernel<A, GV><<<N, GLUE_T, 0, st>>>(pf_ln2, cs, w.cxk, (A*)pf_xk, Ts, C);
+                     return cudaGetLastError();
+                 }, "x070 prefill cmix input")))
+                return rc;
+            GemvJobs K{};
+            if (!w.ad[AD_KEY].on()) {
+                K.j[0] = qjob(w.key, pf_xk, C, ACT_RELU2, aout, pf_ffn, F);
+                if ((rc = gemv(0, K, 1, N, st))) return rc;
+            } else {
+                K.j[0] = qjob(w.key, pf_xk, C, ACT_NONE, OUT_F32, pf_keytmp, F);
+                if ((rc = gemv(0, K, 1, N, st))) return rc;
+                const LoraJob lj[1] = {{&w.ad[AD_KEY], pf_xk, C, C, F, pf_keytmp, F}};
+                if ((rc = lora_apply<A>(lj, 1, N, st, pf_z, pf_cap))) return rc;
+                const int n = N * F;
+                x070_relu2_cast_kernel<A><<<std::min((n + 255) / 256, 4 * sm_count), 256, 0, st>>>(pf_keytmp, (A*)pf_ffn, n);
+                if ((rc = check_launch("x070_relu2_cast_kernel"))) return rc;
+            }
+            GemvJobs Vv{};
+            Vv.j[0] = qjob(w.value, pf_ffn, F, ACT_NONE, OUT_ADD_F32, pf_x, C);
+            if ((rc = gemv(0, Vv, 1, N, st))) return rc;
+            {
+                const LoraJob lj[1] = {{&w.ad[AD_VALUE], pf_ffn, F, F, C, pf_x, C}};
+                if ((rc = lora_apply<A>(lj, 1, N, st, pf_z, pf_cap))) return rc;
+            }
+            x070_pf_commit_kernel<<<rows, 256, 0, st>>>(pf_ln1, pf_ln2, ts, cs, pf_len, p0, Ts, C);
+            if ((rc = check_launch("x070_pf_commit_kernel"))) return rc;
+        }
+        return rows_launch([&]<int GV>() {
+            x070_pf_lnout_kernel<A, GV><<<rows, GLUE_T, 0, st>>>(pf_x, lnow, lnob, (A*)lnout, pf_len, p0, Ts, C);
+            return cudaGetLastError();
+        }, "x070_pf_lnout_kernel");
+    }
+
+    // Prompts [rows, T] (device, right-padded) with host lengths (nullptr: all
+    // T): every block, then the head over each row's last real token and the
+    // greedy argmax into ids.  Continues from the rows' current state.
+    int prefill(const int32_t* prompt, const int32_t* len_host, int rows, int T, cudaStream_t st) {
+        std::vector<int32_t> lens(rows, T);
+        int maxlen = 0;
+        for (int i = 0; i < rows; i++) {
+            if (len_host) lens[i] = len_host[i];
+            RWKV_REQUIRE(lens[i] >= 1 && lens[i] <= T, RWKV_E_SHAPE,
+                         "prefill: row %d length %d not in 1..%d (no empty prompt)", i, lens[i], T);
+            maxlen = std::max(maxlen, lens[i]);
+        }
+        const int Ts = prefill_block(rows, maxlen);
+        if (int rc = ensure_prefill(rows * Ts, Ts, rows)) return rc;
+        cudaMemcpyAsync(pf_len, lens.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+        for (int p0 = 0; p0 < maxlen; p0 += Ts) {
+            const int rc = f16act ? prefill_block_body<__half>(prompt, T, rows, p0, Ts, st)
+                                  : prefill_block_body<float>(prompt, T, rows, p0, Ts, st);
+            if (rc) return rc;
+        }
+        // the head over the rows' hidden states, then greedy ids: the decode step's tail
+        GemvJobs Hd{};
+        Hd.j[0] = qjob(head, lnout, C, ACT_NONE, OUT_F32, logits, V);
+        int rc = gemv(0, Hd, 1, rows, st);
+        if (rc) return rc;
+        {
+            const LoraJob lj[1] = {{&head_ad, lnout, C, C, V, logits, V}};
+            if ((rc = f16act ? lora_apply<__half>(lj, 1, rows, st) : lora_apply<float>(lj, 1, rows, st))) return rc;
+        }
+        x070_argmax_kernel<<<dim3((V + ARGMAX_SLICE - 1) / ARGMAX_SLICE, rows), GLUE_T, 0, st>>>(logits, V, amax_keys);
+        x070_argmax_finish_kernel<<<(rows + 127) / 128, 128, 0, st>>>(amax_keys, ids, rows);
+        return check_launch("x070 prefill head");
+    }
+
+    // Rows keep[0..nkeep) of the state move to rows 0..nkeep-1 (in order).
+    int gather_rows(const int32_t* keep_host, int nkeep, cudaStream_t st) {
+        if (!pf_gather) return fail(RWKV_E_CUDA, "gather_rows: no buffers");
+        cudaMemcpyAsync(pf_keep, keep_host, nkeep * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+        const int64_t ES = (int64_t)H * 4096;
+        const int grid = 4 * sm_count;
+        for (int l = 0; l < L; l++) {
+            float* blocks[3] = {wkv + (size_t)l * Rmax * ES, tshift + (size_t)l * Rmax * C, cshift + (size_t)l * Rmax * C};
+            const int64_t E[3] = {ES, C, C};
+            for (int q = 0; q < 3; q++) {
+                x070_gather_rows_kernel<<<grid, 256, 0, st>>>(blocks[q], pf_gather, pf_keep, nkeep, E[q]);
+                cudaMemcpyAsync(blocks[q], pf_gather, (size_t)nkeep * E[q] * 4, cudaMemcpyDeviceToDevice, st);
+            }
+        }
+        return check_launch("x070_gather_rows_kernel");
+    }
+
+    // Device copy of host prompts [rows, T] for generate (its own buffer,
+    // grown when needed, freed with the model).
+    int stage_prompt(const int32_t* host, int rows, int T, cudaStream_t st) {
+        const int n = rows * T;
+        if (n > pf_prompt_cap) {
+            cudaStreamSynchronize(st);  // an earlier prefill may still read the old buffer
+            if (pf_prompt) cudaFree(pf_prompt);
+            pf_prompt = nullptr;
+            pf_prompt_cap = 0;
+            if (cudaMalloc(&pf_prompt, (size_t)n * 4) != cudaSuccess) {
+                pf_prompt = nullptr;
+                return fail(RWKV_E_CUDA, "generate: prompt buffer allocation failed");
+            }
+            pf_prompt_cap = n;
+        }
+        cudaMemcpyAsync(pf_prompt, host, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+        return RWKV_OK;
+    }
+
     int launches_per_step() const {
         int n = 1 + L * 10 + 4 + (head_ad.on() ? 2 : 0);
         for (const LayerW& w : lw) {
@@ -865,11 +1121,9 @@ int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int 
         return fail(RWKV_E_TIMEOUT, "rwkv_x070_generate: a tensor-core GEMM wait of an earlier step gave up "
                                     "(flag cleared, nothing launched)");
     std::vector<int32_t> col(rows);
-    for (int t = 0; t < prompt_len; t++) {
-        for (int n = 0; n < rows; n++) col[n] = prompt_host[(size_t)n * prompt_len + t];
-        cudaMemcpyAsync(m.ids, col.data(), rows * 4, cudaMemcpyHostToDevice, st);
-        if (int rc = m.graph_step_any(rows, st)) return rc;
-    }
+    // the prompt in parallel (prefill), then one token per step
+    if (int rc = m.stage_prompt(prompt_host, rows, prompt_len, st)) return rc;
+    if (int rc = m.prefill(m.pf_prompt, nullptr, rows, prompt_len, st)) return rc;
     for (int s = 0; s < n_new; s++) {
         cudaMemcpyAsync(col.data(), m.ids, rows * 4, cudaMemcpyDeviceToHost, st);
         if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "generate: sync failed");
@@ -879,6 +1133,72 @@ int rwkv_x070_generate(rwkv_x070_t h, const int32_t* prompt_host, int rows, int 
     }
     if (int rc = m.gflag.status(st, "rwkv_x070_generate")) return rc;
     return check_launch("rwkv_x070_generate");
+}
+
+int rwkv_x070_prefill(rwkv_x070_t h, const int32_t* ids, const int32_t* lengths_host, int rows, int T,
+                      float* logits, int32_t* next_ids, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h && ids, RWKV_E_NULL, "rwkv_x070_prefill: NULL argument");
+    X070& m = *reinterpret_cast<X070*>(h);
+    RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax && T >= 1, RWKV_E_SHAPE, "rwkv_x070_prefill: rows %d (1..%d), T %d",
+                 rows, m.Rmax, T);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (m.gflag.take(st))
+        return fail(RWKV_E_TIMEOUT, "rwkv_x070_prefill: a tensor-core GEMM wait of an earlier call gave up "
+                                    "(flag cleared, nothing launched)");
+    if (int rc = m.prefill(ids, lengths_host, rows, T, st)) return rc;
+    if (logits) cudaMemcpyAsync(logits, m.logits, (size_t)rows * m.V * 4, cudaMemcpyDeviceToDevice, st);
+    if (next_ids) cudaMemcpyAsync(next_ids, m.ids, rows * 4, cudaMemcpyDeviceToDevice, st);
+    return check_launch("rwkv_x070_prefill");
+}
+
+int rwkv_x070_generate_batch(rwkv_x070_t h, const int32_t* prompts_host, const int32_t* lengths_host, int rows,
+                             int max_len, int n_new, const int32_t* stop_host, int n_stop, int32_t* out_host,
+                             int32_t* out_len_host, rwkv_stream_t stream) {
+    RWKV_REQUIRE(h && prompts_host && out_host && out_len_host, RWKV_E_NULL, "rwkv_x070_generate_batch: NULL argument");
+    RWKV_REQUIRE(n_stop == 0 || stop_host, RWKV_E_NULL, "rwkv_x070_generate_batch: NULL stop list");
+    X070& m = *reinterpret_cast<X070*>(h);
+    RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax && max_len >= 1 && n_new >= 0 && n_stop >= 0, RWKV_E_SHAPE,
+                 "rwkv_x070_generate_batch: rows %d prompt %d new %d stops %d", rows, max_len, n_new, n_stop);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (m.gflag.take(st))
+        return fail(RWKV_E_TIMEOUT, "rwkv_x070_generate_batch: a tensor-core GEMM wait of an earlier call gave up "
+                                    "(flag cleared, nothing launched)");
+    for (int i = 0; i < rows; i++) out_len_host[i] = 0;
+    if (int rc = rwkv_x070_reset_state(h, rows, stream)) return rc;
+    if (int rc = m.stage_prompt(prompts_host, rows, max_len, st)) return rc;
+    if (int rc = m.prefill(m.pf_prompt, lengths_host, rows, max_len, st)) return rc;
+    std::vector<int> alive(rows);
+    for (int i = 0; i < rows; i++) alive[i] = i;
+    std::vector<int32_t> col(rows), next, keep;
+    for (int s = 0; s < n_new; s++) {
+        const int na = (int)alive.size();
+        cudaMemcpyAsync(col.data(), m.ids, na * 4, cudaMemcpyDeviceToHost, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "generate_batch: sync failed");
+        next.clear();
+        keep.clear();
+        for (int r = 0; r < na; r++) {
+            const int i = alive[r];
+            const int32_t id = col[r];
+            out_host[(size_t)i * n_new + out_len_host[i]++] = id;
+            bool stop = false;
+            for (int q = 0; q < n_stop && !stop; q++) stop = stop_host[q] == id;
+            if (stop) continue;
+            next.push_back(id);
+            keep.push_back(r);
+        }
+        if (keep.empty() || s + 1 >= n_new) break;
+        if ((int)keep.size() < na) {
+            // finished rows leave the batch (RWKVBatchState.gather)
+            if (int rc = m.gather_rows(keep.data(), (int)keep.size(), st)) return rc;
+            std::vector<int> a2(keep.size());
+            for (size_t q = 0; q < keep.size(); q++) a2[q] = alive[keep[q]];
+            alive.swap(a2);
+        }
+        cudaMemcpyAsync(m.ids, next.data(), next.size() * 4, cudaMemcpyHostToDevice, st);
+        if (int rc = m.graph_step_any((int)next.size(), st)) return rc;
+    }
+    if (int rc = m.gflag.status(st, "rwkv_x070_generate_batch")) return rc;
+    return check_launch("rwkv_x070_generate_batch");
 }
 
 int rwkv_x070_status(rwkv_x070_t h, rwkv_stream_t stream) {

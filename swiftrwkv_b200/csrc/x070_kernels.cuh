@@ -342,6 +342,194 @@ x070_wkv_kernel(const float* __restrict__ r, const float* __restrict__ wdec,
     st_act(out + vb + l + 32, o1);
 }
 
+// ---------------------------------------------------------------- prefill
+// Parallel prefill over a block of `Ts` positions of every row (the
+// reference's bodyWithState, X070Backbone.swift:1011-1048, over right-padded
+// prompts, BatchGenerate.swift:36-51): token n = row * Ts + t sits at prompt
+// position p0 + t; it is a real token when p0 + t < len[row], else padding.
+// Buffers of these kernels are [rows * Ts, C] (= [rows, Ts, H, 64]).
+
+// The block's token ids from the right-padded [rows, T] prompt matrix.
+__global__ void x070_pf_ids_kernel(const int32_t* __restrict__ ids, int T, int p0, int Ts, int rows,
+                                   int32_t* __restrict__ out) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= rows * Ts) return;
+    const int row = n / Ts, p = p0 + n % Ts;
+    out[n] = p < T ? ids[(int64_t)row * T + p] : 0;
+}
+
+// tmix input over a block (rwkvTmixForward's token shift and lerps,
+// RWKVBlock.swift:171-178): xl = ln1(x) (given), prev = the row's shift row
+// at t = 0 else xl of token n - 1; mix[m] = xl + (prev - xl) * coef[m].
+template <typename A, int GV>
+__global__ void __launch_bounds__(GLUE_T)
+x070_pf_tmix_mix_kernel(const float* __restrict__ ln, const float* __restrict__ shift,
+                        const float* __restrict__ coef, A* __restrict__ mix, int N, int Ts, int C) {
+    const int n = blockIdx.x, t = n % Ts, row = n / Ts;
+    float4 cf[6][GV], v[GV], pv[GV];
+#pragma unroll
+    for (int m = 0; m < 6; m++) ld_row4<GV>(cf[m], coef + m * C, C);
+    ld_row4<GV>(v, ln + (int64_t)n * C, C);
+    ld_row4<GV>(pv, t == 0 ? shift + (int64_t)row * C : ln + (int64_t)(n - 1) * C, C);
+#pragma unroll
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
+        if (c >= C) continue;
+        const int64_t o = (int64_t)n * C + c;
+        const float4 xx = sub4(pv[i], v[i]);
+#pragma unroll
+        for (int m = 0; m < 6; m++) st_act4(mix + (int64_t)m * N * C + o, lerp4(v[i], xx, cf[m][i]));
+    }
+}
+
+// cmix input over a block (rwkvCmixForward, RWKVBlock.swift:297-300).
+template <typename A, int GV>
+__global__ void __launch_bounds__(GLUE_T)
+x070_pf_cmix_mix_kernel(const float* __restrict__ ln, const float* __restrict__ shift,
+                        const float* __restrict__ coef, A* __restrict__ out, int Ts, int C) {
+    const int n = blockIdx.x, t = n % Ts, row = n / Ts;
+    float4 cf[GV], v[GV], pv[GV];
+    ld_row4<GV>(cf, coef, C);
+    ld_row4<GV>(v, ln + (int64_t)n * C, C);
+    ld_row4<GV>(pv, t == 0 ? shift + (int64_t)row * C : ln + (int64_t)(n - 1) * C, C);
+#pragma unroll
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
+        if (c < C) st_act4(out + (int64_t)n * C + c, lerp4(v[i], sub4(pv[i], v[i]), cf[i]));
+    }
+}
+
+// The WKV inputs of a block (the caller math of RWKVBlock.swift:207-237),
+// one warp per (token, head), lanes on channels c and c + 32:
+//   kk = l2norm(k * k_k);  k' = k * (1 + (a - 1) * k_a)
+//   v' = v (layer 0, also stored as v_first) or v + (v_first - v) * vv
+//   a_wkv = -kk;  b_wkv = kk * a
+//   padding (p0 + t >= len): w = 1, k' = 0, b_wkv = 0, so the step is the
+//   identity on the state (RWKVBlock.swift:221-237).
+// w, k, v are rewritten in place; a_wkv / b_wkv go to aw / bw.
+__global__ void __launch_bounds__(256)
+x070_pf_prep_kernel(float* __restrict__ w, float* __restrict__ k, float* __restrict__ v,
+                    const float* __restrict__ a, const float* __restrict__ vv,
+                    float* __restrict__ vfirst, float* __restrict__ aw, float* __restrict__ bw,
+                    const float* __restrict__ kkw, const float* __restrict__ kaw,
+                    const int32_t* __restrict__ len, int p0, int Ts, int H, int layer0) {
+    constexpr int N = 64;
+    const int n = blockIdx.x, head = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (head >= H) return;
+    const bool real = p0 + n % Ts < len[n / Ts];
+    const int64_t base = ((int64_t)n * H + head) * N;
+    float kk[2], kr[2], aa[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int c = lane + 32 * j;
+        kr[j] = k[base + c];
+        aa[j] = a[base + c];
+        kk[j] = kr[j] * kkw[head * N + c];
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(kk[0] * kk[0] + kk[1] * kk[1]) + 1e-12f);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int c = lane + 32 * j;
+        const int64_t o = base + c;
+        const float kn = kk[j] * inv;
+        const float kp = kr[j] * (1.0f + (aa[j] - 1.0f) * kaw[head * N + c]);
+        float vd = v[o];
+        if (layer0) {
+            vfirst[o] = vd;
+        } else {
+            const float f = vfirst[o];
+            vd = vd + (f - vd) * vv[o];
+        }
+        v[o] = vd;
+        aw[o] = -kn;
+        if (real) {
+            k[o] = kp;
+            bw[o] = kn * aa[j];
+        } else {
+            w[o] = 1.0f;
+            k[o] = 0.0f;
+            bw[o] = 0.0f;
+        }
+    }
+}
+
+// tmix tail of a block, one warp per (token, head): GroupNorm(64e-5) of the
+// WKV output y, bonus (sum r*k'*r_k) * v', gate -> out (activation type);
+// the same arithmetic as the decode kernel's tail.
+template <typename A>
+__global__ void __launch_bounds__(256)
+x070_pf_tail_kernel(const float* __restrict__ y, const float* __restrict__ r, const float* __restrict__ kp,
+                    const float* __restrict__ v, const float* __restrict__ rkw, const float* __restrict__ lnxw,
+                    const float* __restrict__ lnxb, const float* __restrict__ g, A* __restrict__ out, int H) {
+    constexpr int N = 64;
+    const int n = blockIdx.x, head = blockIdx.y * 8 + (threadIdx.x >> 5), l = threadIdx.x & 31;
+    if (head >= H) return;
+    const int64_t base = ((int64_t)n * H + head) * N;
+    const int hb = head * N;
+    float dp = r[base + l] * kp[base + l] * rkw[hb + l] + r[base + l + 32] * kp[base + l + 32] * rkw[hb + l + 32];
+    dp = warp_sum(dp);
+    const float x0 = y[base + l], x1 = y[base + l + 32];
+    const float mean = warp_sum(x0 + x1) * (1.0f / N);
+    const float d0 = x0 - mean, d1 = x1 - mean;
+    const float var = warp_sum(d0 * d0 + d1 * d1) * (1.0f / N);
+    const float invs = 1.0f / sqrtf(var + 64e-5f);
+    const float o0 = (d0 * invs * lnxw[hb + l] + lnxb[hb + l] + dp * v[base + l]) * g[base + l];
+    const float o1 = (d1 * invs * lnxw[hb + l + 32] + lnxb[hb + l + 32] + dp * v[base + l + 32]) * g[base + l + 32];
+    st_act(out + base + l, o0);
+    st_act(out + base + l + 32, o1);
+}
+
+// End of a block for one layer: each row's token-shift state becomes the
+// normalised input at its last real token inside the block (gatherLast at
+// lastRealIndex, RWKVBatchState.swift:159-175); rows without a real token
+// in the block keep theirs.
+__global__ void __launch_bounds__(256)
+x070_pf_commit_kernel(const float* __restrict__ ln1, const float* __restrict__ ln2, float* __restrict__ tshift,
+                      float* __restrict__ cshift, const int32_t* __restrict__ len, int p0, int Ts, int C) {
+    const int row = blockIdx.x;
+    const int last = min(len[row] - 1, p0 + Ts - 1) - p0;
+    if (last < 0) return;
+    const int64_t src = ((int64_t)row * Ts + last) * C, dst = (int64_t)row * C;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        tshift[dst + c] = ln1[src + c];
+        cshift[dst + c] = ln2[src + c];
+    }
+}
+
+// ln_out of each row's last real token, when it lies in this block -> out
+// [rows, C] (activation type): the hidden state the head reads.
+template <typename A, int GV>
+__global__ void __launch_bounds__(GLUE_T)
+x070_pf_lnout_kernel(const float* __restrict__ x, const float* __restrict__ lnw, const float* __restrict__ lnb,
+                     A* __restrict__ out, const int32_t* __restrict__ len, int p0, int Ts, int C) {
+    __shared__ float sh[33];
+    const int row = blockIdx.x;
+    const int last = len[row] - 1 - p0;
+    if (last < 0 || last >= Ts) return;
+    float4 w4[GV], b4[GV], v[GV];
+    ld_row4<GV>(w4, lnw, C);
+    ld_row4<GV>(b4, lnb, C);
+    ld_row4<GV>(v, x + ((int64_t)row * Ts + last) * C, C);
+    ln_row4<GV>(v, w4, b4, C, sh);
+#pragma unroll
+    for (int i = 0; i < GV; i++) {
+        const int c = 4 * (threadIdx.x + GLUE_T * i);
+        if (c < C) st_act4(out + (int64_t)row * C + c, v[i]);
+    }
+}
+
+// generateBatch's row drop (RWKVBatchState.gather, BatchGenerate.swift:
+// 105-108): rows keep[i] -> i of one layer's [rows, E] float block, through
+// `tmp` (keep is increasing, but a destination may still be a later source).
+__global__ void x070_gather_rows_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                        const int32_t* __restrict__ keep, int nkeep, int64_t E) {
+    const int64_t total = (int64_t)nkeep * E;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / E, e = i - r * E;
+        dst[i] = src[(int64_t)keep[r] * E + e];
+    }
+}
+
 // Greedy sampler: first index of the maximum logit per row.  Each CTA scans
 // a slice of one row and folds (value, index) into a 64-bit key with
 // atomicMax: the high word is the float mapped to an order-preserving

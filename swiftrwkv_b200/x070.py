@@ -149,16 +149,57 @@ class X070Backbone:
             agg[name] = (c + 1, tot + t)
         return agg, seq
 
-    def generateBatch(self, prompts, n_new: int):
-        """Greedy generation, host in / host out: prompts int [rows, T] (equal
-        lengths) -> new tokens int32 [rows, n_new].  State starts from zero."""
-        p = np.ascontiguousarray(np.asarray(prompts, np.int32))
-        rows, T = p.shape
-        self.reset(rows)
-        out = np.zeros((rows, n_new), np.int32)
-        call("rwkv_x070_generate", self.h, p.ctypes.data_as(ctypes.c_void_p), rows, T, n_new,
-             out.ctypes.data_as(ctypes.c_void_p), self._s())
+    def prefill(self, ids, lengths=None, logits: bool = True):
+        """Parallel prefill of right-padded prompts (prefillBatch over
+        bodyWithState, BatchGenerate.swift:36-51): ids int [rows, T] (device
+        or host), lengths int [rows] (None: all T).  Continues from the rows'
+        current state; returns the logits [rows, vocab] of each row's last
+        real token (or None), whose argmax becomes the next step's input."""
+        ids = torch.as_tensor(ids, dtype=torch.int32).to("cuda").contiguous()
+        rows, T = ids.shape
+        lens = None
+        if lengths is not None:
+            lens = np.ascontiguousarray(np.asarray(lengths, np.int32))
+            if lens.shape != (rows,):
+                raise ValueError(f"lengths must be [{rows}]")
+        out = torch.empty((rows, self.cfg.vocab), device="cuda", dtype=torch.float32) if logits else None
+        call("rwkv_x070_prefill", self.h, _lib.P(ids.data_ptr()),
+             None if lens is None else lens.ctypes.data_as(ctypes.c_void_p), rows, T,
+             None if out is None else _lib.P(out.data_ptr()), None, self._s())
         return out
+
+    def generateBatch(self, prompts, n_new: int, stopTokens=()):
+        """Greedy generation, host in / host out (BatchGenerate.swift:69-116).
+        prompts: int [rows, T] (equal lengths) -> int32 [rows, n_new], or a
+        list of token lists (ragged, right-padded internally) -> a list of
+        token lists, each ending at its first stop token (kept) or after
+        n_new tokens; stopped rows leave the batch.  State starts from zero."""
+        ragged = not isinstance(prompts, np.ndarray) and (
+            len(prompts) > 0 and not np.isscalar(prompts[0]) and len({len(p) for p in prompts}) > 1)
+        if not ragged and not stopTokens:
+            p = np.ascontiguousarray(np.asarray(prompts, np.int32))
+            rows, T = p.shape
+            self.reset(rows)
+            out = np.zeros((rows, n_new), np.int32)
+            call("rwkv_x070_generate", self.h, p.ctypes.data_as(ctypes.c_void_p), rows, T, n_new,
+                 out.ctypes.data_as(ctypes.c_void_p), self._s())
+            return out
+        rows = len(prompts)
+        lens = np.array([len(p) for p in prompts], np.int32)
+        if rows == 0 or lens.min() < 1:
+            raise ValueError("generateBatch: every prompt needs at least one token")
+        T = int(lens.max())
+        p = np.zeros((rows, T), np.int32)
+        for i, q in enumerate(prompts):
+            p[i, :len(q)] = q
+        stops = np.ascontiguousarray(np.asarray(list(stopTokens), np.int32))
+        out = np.zeros((rows, max(n_new, 1)), np.int32)
+        cnt = np.zeros(rows, np.int32)
+        call("rwkv_x070_generate_batch", self.h, p.ctypes.data_as(ctypes.c_void_p),
+             lens.ctypes.data_as(ctypes.c_void_p), rows, T, n_new,
+             stops.ctypes.data_as(ctypes.c_void_p) if stops.size else None, int(stops.size),
+             out.ctypes.data_as(ctypes.c_void_p), cnt.ctypes.data_as(ctypes.c_void_p), self._s())
+        return [list(out[i, :cnt[i]]) for i in range(rows)]
 
     def generate(self, prompt, n_new: int):
         """Single-row greedy generation (Generate.swift:112-202, argmax sampler)."""
