@@ -256,11 +256,6 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, const uint32_t* v) 
 
 constexpr int TC_JOBS = 4;
 constexpr int TC_BM = 128;
-constexpr int TC_QW = 4;                           // dequant warps per TMEM lane quadrant
-constexpr int TC_DQW = 4 * TC_QW;                  // dequant / epilogue warps
-constexpr int TC_THREADS = 64 + 32 * TC_DQW;       // + producer warp + MMA warp
-constexpr int TC_TMEM_COLS = 512;
-constexpr int TC_A_COL = 256;  // A stages live in TMEM columns [256, 512)
 constexpr int TC_SRING = 4;    // scale / bias prefetch ring (stages)
 constexpr int TC_MAX_SPLIT = 8;  // split-K CTAs of one tile form one cluster
 
@@ -287,31 +282,43 @@ struct TcArgs {
     int* err_host;
 };
 
-template <int FMT, int BN, int GPS, int ST>
+// QW dequant warps per TMEM lane quadrant; TMC TMEM columns: 512 (accumulator
+// in [0, 256), A stages in [256, 512), one CTA per SM) or 256 (accumulator in
+// [0, 64), A stages in [64, 256): BN <= 64, small enough -- with QW = 2 and a
+// ~100 KB stage ring -- that two CTAs fit on an SM, so a launch's CTAs can
+// become resident, and stream their weights, beside its predecessor's).
+template <int FMT, int BN, int GPS, int ST, int QW_ = 4, int TMC_ = 512>
 struct TcCfg {
+    static constexpr int QW = QW_;
+    static constexpr int DQW = 4 * QW;                    // dequant / epilogue warps
+    static constexpr int THREADS = 64 + 32 * DQW;         // + producer warp + MMA warp
+    static constexpr int TMC = TMC_;
+    static constexpr int A_COL = TMC == 512 ? 256 : 64;
+    static_assert(TMC == 512 || (TMC == 256 && BN <= 64), "TMEM layout");
     static constexpr int CROW = FMT == TC_Q4 ? 32 * GPS : 128 * GPS;  // weight bytes per row per stage
     static constexpr int C_BYTES = TC_BM * CROW;
     static constexpr int XBOX = BN * 128;                 // one x box (64 columns)
     static constexpr int X_BYTES = GPS * XBOX;
     static constexpr int STAGE = C_BYTES + X_BYTES;       // multiple of 1024
-    static constexpr int ST_A = (TC_TMEM_COLS - TC_A_COL) / (32 * GPS);
+    static constexpr int ST_A = (TMC - A_COL) / (32 * GPS);
     static constexpr int CPR = 2 * GPS;                   // 16-byte code chunks per row per stage
-    static constexpr int CPW = CPR / TC_QW;               // chunks per dequant warp per stage
+    static constexpr int CPW = CPR / QW;                  // chunks per dequant warp per stage
     static constexpr int SLOT = 8;                        // ring slot: a 4-byte-aligned pair of scales + of biases
-    static constexpr int SR_OFF = ST * STAGE;             // ring: [TC_SRING][32*TC_DQW] slots
-    static constexpr int B_OFF = SR_OFF + (FMT == TC_Q4 ? TC_SRING * 32 * TC_DQW * SLOT : 0);
+    static constexpr int SR_OFF = ST * STAGE;             // ring: [TC_SRING][32*DQW] slots
+    static constexpr int B_OFF = SR_OFF + (FMT == TC_Q4 ? TC_SRING * 32 * DQW * SLOT : 0);
     static constexpr int NBAR = 3 * ST + 2 * ST_A + 1;
     static constexpr int T_OFF = B_OFF + NBAR * 8;
     static constexpr int TOTAL = T_OFF + 16 + 1024;       // + slack for 1024-byte alignment
     static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 needs N % 16 == 0, 16..256");
-    static_assert(BN <= TC_A_COL, "accumulator columns");
+    static_assert(BN <= A_COL, "accumulator columns");
     static constexpr int RP = BN + 4;                     // split-K receive row pitch (floats): 16-byte rows, conflict-free
     static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * RP * 4, "split-K receive buffers reuse the stage buffers");
     static_assert(TOTAL <= 227 * 1024, "shared memory per CTA");
-    static_assert(FMT == TC_F16 || (CPR % TC_QW == 0 && CPW >= 1 && CPW <= 2),
+    static_assert(FMT == TC_F16 || ST_A >= 1, "at least one A stage");
+    static_assert(FMT == TC_F16 || (CPR % QW == 0 && CPW >= 1 && CPW <= 2),
                   "a dequant warp's chunks lie in one group");
-    static_assert(BN % (4 * TC_QW) == 0, "accumulator columns per warp in units of 4");
+    static_assert(BN % (4 * QW) == 0, "accumulator columns per warp in units of 4");
 };
 
 // Byte offset of 16-byte chunk c of row r in a TMA tile with `rb`-byte rows
@@ -321,10 +328,11 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c, uint32_t rb) {
     return off ^ (((off >> 7) & (rb / 16 - 1)) << 4);
 }
 
-template <int FMT, int BN, int GPS, int ST>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int FMT, int BN, int GPS, int ST, int QW = 4, int TMC = 512>
+__global__ void __launch_bounds__(TcCfg<FMT, BN, GPS, ST, QW, TMC>::THREADS, TMC == 512 ? 1 : 2)
 gemm_tc_kernel(const __grid_constant__ TcArgs args) {
-    using C = TcCfg<FMT, BN, GPS, ST>;
+    using C = TcCfg<FMT, BN, GPS, ST, QW, TMC>;
+    constexpr int TC_DQW = C::DQW, TC_QW = C::QW, TC_TMEM_COLS = C::TMC, TC_A_COL = C::A_COL;
     constexpr int ST_A = C::ST_A;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -702,30 +710,34 @@ inline bool tc_job_ok(int FMT, const GemvJob& j) {
            ((uintptr_t)j.scales & 7) == 0 && ((uintptr_t)j.biases & 7) == 0;
 }
 
-// Kernel configurations (tile width BN, groups per stage GPS, stages ST) per
-// weight format; X(BN, GPS, ST) for TC_Q4 then TC_F16.
-#define RWKV_TC_CONFIGS(FMT, X)                                                      \
-    switch (BN) {                                                                   \
-        case 16: return FMT == TC_Q4 ? X(TC_Q4, 16, 4, 6) : X(TC_F16, 16, 1, 8);     \
-        case 32: return FMT == TC_Q4 ? X(TC_Q4, 32, 4, 5) : X(TC_F16, 32, 1, 8);     \
-        case 64: return FMT == TC_Q4 ? X(TC_Q4, 64, 4, 4) : X(TC_F16, 64, 1, 8);     \
-        default: return FMT == TC_Q4 ? X(TC_Q4, 128, 2, 4) : X(TC_F16, 128, 1, 6);   \
+// Kernel configurations (tile width BN, groups per stage GPS, stages ST,
+// dequant warps per quadrant QW, TMEM columns TMC) per weight format;
+// X(FMT, BN, GPS, ST, QW, TMC).  One CTA per SM.  (Two-per-SM variants --
+// 128-deep stages, 8 dequant warps, 256 TMEM columns, so that a launch's CTAs
+// could stream their weights beside its predecessor's -- measured slower on
+// the 1.5B decode step: 64 rows 2.11 -> 2.36 ms.)
+#define RWKV_TC_CONFIGS(FMT, X)                                                                 \
+    switch (BN) {                                                                              \
+        case 16: return FMT == TC_Q4 ? X(TC_Q4, 16, 4, 6, 4, 512) : X(TC_F16, 16, 1, 8, 4, 512);  \
+        case 32: return FMT == TC_Q4 ? X(TC_Q4, 32, 4, 5, 4, 512) : X(TC_F16, 32, 1, 8, 4, 512);  \
+        case 64: return FMT == TC_Q4 ? X(TC_Q4, 64, 4, 4, 4, 512) : X(TC_F16, 64, 1, 8, 4, 512);  \
+        default: return FMT == TC_Q4 ? X(TC_Q4, 128, 2, 4, 4, 512) : X(TC_F16, 128, 1, 6, 4, 512); \
     }
 
 // How many (1, 1, S) clusters of this configuration the GPU holds at once
 // (cached per configuration and S; 0 when the query fails).
-template <int FMT, int BN, int GPS, int ST>
+template <int FMT, int BN, int GPS, int ST, int QW, int TMC>
 inline int tc_max_clusters_t(int S) {
     static int cache[TC_MAX_SPLIT + 1] = {};
     if (S < 1 || S > TC_MAX_SPLIT) return 0;
     if (cache[S]) return cache[S] > 0 ? cache[S] : 0;
-    using C = TcCfg<FMT, BN, GPS, ST>;
-    auto kern = gemm_tc_kernel<FMT, BN, GPS, ST>;
+    using C = TcCfg<FMT, BN, GPS, ST, QW, TMC>;
+    auto kern = gemm_tc_kernel<FMT, BN, GPS, ST, QW, TMC>;
     int n = 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL) == cudaSuccess) {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(1, 1, S);
-        cfg.blockDim = dim3(TC_THREADS);
+        cfg.blockDim = dim3(C::THREADS);
         cfg.dynamicSmemBytes = C::TOTAL;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -742,7 +754,7 @@ inline int tc_max_clusters_t(int S) {
 }
 
 inline int tc_max_clusters(int FMT, int BN, int S) {
-#define X_(F, B, G, T) tc_max_clusters_t<F, B, G, T>(S)
+#define X_(F, B, G, T, Q, M) tc_max_clusters_t<F, B, G, T, Q, M>(S)
     RWKV_TC_CONFIGS(FMT, X_)
 #undef X_
 }
@@ -815,15 +827,15 @@ inline bool encode_tc_maps(int FMT, TcJob& t, const GemvJob& j, int R, int BN, i
     return true;
 }
 
-template <int FMT, int BN, int GPS, int ST>
+template <int FMT, int BN, int GPS, int ST, int QW, int TMC>
 inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, bool pdl, cudaStream_t st) {
-    using C = TcCfg<FMT, BN, GPS, ST>;
-    auto kern = gemm_tc_kernel<FMT, BN, GPS, ST>;
+    using C = TcCfg<FMT, BN, GPS, ST, QW, TMC>;
+    auto kern = gemm_tc_kernel<FMT, BN, GPS, ST, QW, TMC>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.mblocks, a.njobs, p.nnb * a.S);
-    cfg.blockDim = dim3(TC_THREADS);
+    cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = C::TOTAL;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -842,7 +854,7 @@ inline cudaError_t launch_tc_t(const TcArgs& a, const TcPlan& p, bool pdl, cudaS
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    if (a.S > 1 && tc_max_clusters_t<FMT, BN, GPS, ST>(a.S) < 1) return cudaErrorLaunchOutOfResources;
+    if (a.S > 1 && tc_max_clusters_t<FMT, BN, GPS, ST, QW, TMC>(a.S) < 1) return cudaErrorLaunchOutOfResources;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
@@ -861,7 +873,7 @@ inline cudaError_t launch_tc(int FMT, const GemvJobs& jobs, int njobs, int R, co
     a.err = err;
     a.err_host = err_host;
     const int BN = p.BN;
-#define X_(F, B, G, T) launch_tc_t<F, B, G, T>(a, p, pdl, st)
+#define X_(F, B, G, T, Q, M) launch_tc_t<F, B, G, T, Q, M>(a, p, pdl, st)
     RWKV_TC_CONFIGS(FMT, X_)
 #undef X_
 }
