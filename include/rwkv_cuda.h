@@ -391,6 +391,17 @@ int rwkv_x070_inject_wait_error(rwkv_x070_t model, int host_record, rwkv_stream_
  * Stands in for DecodeBench's --step-profile (Sources/DecodeBench/main.swift:146-196). */
 int rwkv_x070_profile_step(rwkv_x070_t model, int rows, float* ms_host, int cap, char* names_host,
                            int names_cap, int* count, rwkv_stream_t stream);
+/* How a decode step runs.  path 1 (the default): for 9..64 rows with fp16
+ * activations and no LoRA adapters, the whole step is ONE cooperative launch
+ * of a persistent kernel (one CTA per SM, phases separated by grid barriers,
+ * weight tiles streamed ahead of their phase); other steps, and every step
+ * with path 0, run the per-kernel sequence captured in a CUDA graph.  The
+ * arithmetic is the same (the tcgen05 path's fp16-dequantised weights above 8
+ * rows); split-K sums may be grouped differently.  rwkv_x070_decode_path
+ * returns 1 when a step on `rows` rows takes the persistent kernel.  No
+ * counterpart in the reference (MLX schedules the reference's kernels). */
+int rwkv_x070_set_decode_path(rwkv_x070_t model, int path);
+int rwkv_x070_decode_path(rwkv_x070_t model, int rows);
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t model);
 int rwkv_x070_launches_per_step(rwkv_x070_t model);
 

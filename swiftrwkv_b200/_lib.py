@@ -75,6 +75,8 @@ _SIGS = {
     "rwkv_x070_status": [P, P],
     "rwkv_x070_inject_wait_error": [P, I, P],
     "rwkv_x070_weight_bytes": [P],
+    "rwkv_x070_set_decode_path": [P, I],
+    "rwkv_x070_decode_path": [P, I],
     "rwkv_x070_launches_per_step": [P],
     "rwkv_state_broadcast": [P, P, I, I, I, P],
     "rwkv_state_grad_sum": [P, P, I, I, I, I, P],

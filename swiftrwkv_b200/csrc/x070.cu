@@ -19,6 +19,7 @@
 #include "gemm_tc.cuh"
 #include "gemm_w4_wide.cuh"
 #include "x070_kernels.cuh"
+#include "x070_persist.cuh"
 
 namespace rwkv {
 
@@ -68,8 +69,23 @@ struct QMat {
     uint32_t* wq = nullptr;
     __half* sc = nullptr;
     __half* bi = nullptr;
+    __half2* sbr = nullptr;  // (scale, bias) repacked per 128-row block and 256-code stage (persistent step)
     int OUT = 0, IN = 0;
 };
+
+// (scale, bias) pairs of an MLX 4-bit group-64 matrix, repacked for the
+// persistent step's 1-D bulk copies: out[((mb * S + st) * 128 + r) * 4 + j] =
+// (scale, bias) of row mb * 128 + r, group 4 st + j  (S = IN / 256).
+__global__ void x070_repack_sb_kernel(const __half* __restrict__ sc, const __half* __restrict__ bi,
+                                      __half2* __restrict__ out, int OUT, int IN) {
+    const int NG = IN / 64, S = IN / 256;
+    const int64_t n = (int64_t)OUT * NG;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int o = (int)(i / NG), gi = (int)(i % NG);
+        const int mb = o / 128, r = o % 128, st = gi / 4, j = gi % 4;
+        out[(((int64_t)mb * S + st) * 128 + r) * 4 + j] = __halves2half2(sc[i], bi[i]);
+    }
+}
 
 // A LoRA adapter on a projection (LoRA.swift:118-127, X070Backbone.swift:
 // 746-752): y = base(x) + scale * (x A^T) B^T with A [rank, IN], B [OUT, rank]
@@ -118,6 +134,7 @@ struct X070 {
     size_t act_bytes;
     std::map<int, cudaGraphExec_t> graphs;
     int64_t weight_bytes = 0;
+    int64_t wver = 0;  // bumped by every weight change (the persistent step's repacked scales follow it)
     // A capture cannot run on the legacy default stream: graph work requested
     // there is forwarded to this stream, ordered by events on both sides.
     cudaStream_t own = nullptr;
@@ -244,6 +261,7 @@ struct X070 {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
+        for (void* p : pk_allocs) cudaFree(p);
         pf_free();
         if (pf_prompt) cudaFree(pf_prompt);
         gflag.release();
@@ -326,6 +344,7 @@ struct X070 {
     }
 
     int set_param(const std::string& name, const float* host, int64_t n) {
+        wver++;
         if (name.compare(0, 10, "head.lora_") == 0) return set_adapter(head_ad, name.substr(10), C, V, false, host, n);
         if (name == "emb.weight") return upload_q(emb, host, n);
         if (name == "head.weight") return upload_q(head, host, n);
@@ -382,6 +401,7 @@ struct X070 {
     // Random init on the device with the x070 recipe (X070Init.swift:79-206):
     // orthogonal matrices are drawn as Gaussians of the same element scale.
     int init_random(uint64_t seed) {
+        wver++;
         const size_t maxn = std::max((size_t)V * C, (size_t)F * C);
         __half* h16 = nullptr;
         if (cudaMalloc(&h16, maxn * 2) != cudaSuccess) return fail(RWKV_E_CUDA, "init: staging allocation failed");
@@ -690,11 +710,267 @@ struct X070 {
         return rc;
     }
 
+    // ----- persistent decode step (x070_persist.cuh): one launch per step
+
+    int decode_path = 1;  // 1: the persistent step where it applies; 0: the per-kernel graph
+    struct PkProgram {
+        int BN = 0, nphases = 0, nitems_max = 0, ntiles_max = 0;
+        pk::Job* jobs = nullptr;
+        pk::Item* items = nullptr;
+        pk::Phase* phases = nullptr;
+        pk::Layer* layers = nullptr;
+        float* ws = nullptr;
+        int* tickets = nullptr;
+    };
+    std::map<int, PkProgram> pk_progs;
+    std::vector<void*> pk_allocs;
+    unsigned int* pk_bar = nullptr;
+    int64_t pk_wver = -1;
+    int pk_occ = -1;  // CTAs of the persistent kernel per SM (cached)
+
+    bool any_adapter() const {
+        if (head_ad.on()) return true;
+        for (const LayerW& w : lw)
+            for (int t = 0; t < AD_N; t++)
+                if (w.ad[t].on()) return true;
+        return false;
+    }
+    // Whether a step on R rows takes the persistent kernel.
+    bool pk_eligible(int R) const {
+        return decode_path == 1 && f16act && R > 8 && R <= 64 && C % 256 == 0 && C <= 4 * pk::WT * 2 &&
+               F % 256 == 0 && V % 128 == 0 && !any_adapter();
+    }
+    template <typename T>
+    T* pk_alloc(size_t n) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)) != cudaSuccess) return nullptr;
+        pk_allocs.push_back(p);
+        return (T*)p;
+    }
+    // Repacked (scale, bias) of every 4-bit matrix, refreshed after weight changes.
+    int pk_repack(cudaStream_t st) {
+        if (pk_wver == wver) return RWKV_OK;
+        std::vector<QMat*> qs = {&head};
+        for (LayerW& w : lw) {
+            QMat* m[6] = {&w.r, &w.k, &w.v, &w.o, &w.key, &w.value};
+            for (QMat* q : m) qs.push_back(q);
+        }
+        for (QMat* q : qs) {
+            if (!q->sbr && !(q->sbr = pk_alloc<__half2>((size_t)q->OUT * q->IN / 64)))
+                return fail(RWKV_E_CUDA, "persistent step: scale repack allocation failed");
+            x070_repack_sb_kernel<<<std::min(ceil_div((int64_t)q->OUT * q->IN / 64, 256), 8 * sm_count), 256, 0, st>>>(
+                q->sc, q->bi, q->sbr, q->OUT, q->IN);
+        }
+        pk_wver = wver;
+        return check_launch("x070_repack_sb_kernel");
+    }
+
+    // The step as a program of phases for R rows (tensor maps, work items).
+    int pk_build(int R, PkProgram& P) {
+        auto enc = tensor_map_encoder();
+        if (!enc) return fail(RWKV_E_CUDA, "persistent step: no tensor-map encoder");
+        const int BN = R <= 16 ? 16 : R <= 32 ? 32 : 64;
+        const int G = sm_count;
+        std::vector<pk::Job> jobs;
+        std::vector<pk::Item> items;
+        std::vector<pk::Phase> phases;
+        bool bad = false;
+        auto xmap = [&](CUtensorMap& m, const void* x, int IN, int xs) {
+            cuuint64_t dims[2] = {(cuuint64_t)IN, (cuuint64_t)R};
+            cuuint64_t strides[1] = {(cuuint64_t)xs * 2};
+            cuuint32_t box[2] = {64, (cuuint32_t)BN};
+            cuuint32_t es[2] = {1, 1};
+            if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)x, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                bad = true;
+        };
+        auto qj = [&](const QMat& q, const void* x, int xs, int act, int out, void* y, int ys,
+                      const float* bias = nullptr) {
+            pk::Job j{};
+            cuuint64_t dims[2] = {(cuuint64_t)(q.IN / 8), (cuuint64_t)q.OUT};
+            cuuint64_t strides[1] = {(cuuint64_t)q.IN / 2};
+            cuuint32_t box[2] = {32, 128};
+            cuuint32_t es[2] = {1, 1};
+            if (enc(&j.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, (void*)q.wq, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                bad = true;
+            xmap(j.xmap, x, q.IN, xs);
+            j.sb = (const unsigned char*)q.sbr;
+            j.g = qjob(q, x, xs, act, out, y, ys, bias);
+            j.fmt = pk::FMT_Q4;
+            j.sb_stages = q.IN / 256;
+            jobs.push_back(j);
+            return (int)jobs.size() - 1;
+        };
+        auto hj = [&](const __half* W, int OUT, int IN, const void* x, int xs, int act, int out, void* y, int ys,
+                      const float* bias = nullptr) {
+            pk::Job j{};
+            cuuint64_t dims[2] = {(cuuint64_t)IN, (cuuint64_t)OUT};
+            cuuint64_t strides[1] = {(cuuint64_t)IN * 2};
+            cuuint32_t box[2] = {64, 128};
+            cuuint32_t es[2] = {1, 1};
+            if (enc(&j.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)W, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                bad = true;
+            xmap(j.xmap, x, IN, xs);
+            j.g = hjob(W, OUT, IN, x, xs, act, out, y, ys, bias);
+            j.fmt = pk::FMT_F16;
+            jobs.push_back(j);
+            return (int)jobs.size() - 1;
+        };
+        // A GEMM phase over jobs js: every 128-row tile split along K so that
+        // the phase has about one work item per CTA (items of a tile adjacent).
+        int max_items = 1, max_tiles = 1;
+        auto gemm = [&](std::initializer_list<int> js, int layer) {
+            auto stages = [&](const pk::Job& j) { return j.fmt == pk::FMT_Q4 ? j.g.IN / 256 : (j.g.IN + 63) / 64; };
+            int64_t T = 0;
+            for (int ji : js) T += (int64_t)((jobs[ji].g.OUT + 127) / 128) * stages(jobs[ji]);
+            const int target = (int)std::max<int64_t>(1, (T + G - 1) / G);
+            pk::Phase ph{pk::PH_GEMM, (int)items.size(), 0, layer};
+            int tile = 0;
+            for (int ji : js) {
+                const int S = stages(jobs[ji]);
+                const int nz = (S + target - 1) / target;
+                for (int m0 = 0; m0 < jobs[ji].g.OUT; m0 += 128, tile++)
+                    for (int z = 0; z < nz; z++) {
+                        const int a = (int)((int64_t)S * z / nz), b = (int)((int64_t)S * (z + 1) / nz);
+                        items.push_back({ji, m0, a, b - a, tile, z, nz, (int)items.size() - ph.i0});
+                    }
+            }
+            ph.i1 = (int)items.size();
+            max_items = std::max(max_items, ph.i1 - ph.i0);
+            max_tiles = std::max(max_tiles, tile);
+            phases.push_back(ph);
+        };
+        __half* mixp = (__half*)mix;
+        __half* hidp = (__half*)hidden;
+        const size_t RC = (size_t)R * C;
+        auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
+        phases.push_back({pk::PH_EMBED, 0, 0, -1});
+        for (int l = 0; l < L; l++) {
+            LayerW& w = lw[l];
+            phases.push_back({pk::PH_TMIX, 0, 0, l});
+            const int jr = qj(w.r, M(0), C, ACT_NONE, OUT_F32, r, C);
+            const int jk = qj(w.k, M(2), C, ACT_NONE, OUT_F32, k, C);
+            const int jv = qj(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
+            const int dw = hj(w.wA, rw, C, M(1), C, ACT_TANH, OUT_F16, hidp, hid);
+            const int da = hj(w.aA, ra, C, M(4), C, ACT_NONE, OUT_F16, hidp + rw, hid);
+            const int dg = hj(w.gA, rg, C, M(5), C, ACT_SIGMOID, OUT_F16, hidp + rw + ra, hid);
+            const int uw = hj(w.wB, C, rw, hidp, hid, ACT_DECAY, OUT_F32, wdec, C, w.wbias);
+            const int ua = hj(w.aB, C, ra, hidp + rw, hid, ACT_SIGMOID_BIAS, OUT_F32, a, C, w.abias);
+            const int ug = hj(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, g, C);
+            if (l > 0) {
+                const int dv = hj(w.vA, rv, C, M(3), C, ACT_NONE, OUT_F16, hidp + rw + ra + rg, hid);
+                const int uv = hj(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
+                gemm({jr, jk, jv, dw, da, dg, dv}, l);
+                gemm({uw, ua, ug, uv}, l);
+            } else {
+                gemm({jr, jk, jv, dw, da, dg}, l);
+                gemm({uw, ua, ug}, l);
+            }
+            phases.push_back({pk::PH_WKV, 0, 0, l});
+            gemm({qj(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C)}, l);
+            phases.push_back({pk::PH_CMIX, 0, 0, l});
+            gemm({qj(w.key, xk, C, ACT_RELU2, OUT_F16, ffn, F)}, l);
+            gemm({qj(w.value, ffn, F, ACT_NONE, OUT_ADD_F32, x, C)}, l);
+        }
+        phases.push_back({pk::PH_LNOUT, 0, 0, -1});
+        gemm({qj(head, lnout, C, ACT_NONE, OUT_F32, logits, V)}, -1);
+        phases.push_back({pk::PH_ARGMAX, 0, 0, -1});
+        phases.push_back({pk::PH_ARGFIN, 0, 0, -1});
+        if (bad) return fail(RWKV_E_CUDA, "persistent step: tensor map encoding failed");
+        std::vector<pk::Layer> layers(L);
+        for (int l = 0; l < L; l++) {
+            const LayerW& w = lw[l];
+            layers[l] = {w.ln1w, w.ln1b, w.ln2w, w.ln2b, w.coef6, w.kkw, w.kaw, w.rkw, w.lnxw, w.lnxb, w.cxk,
+                         wkv + (size_t)l * Rmax * H * 64 * 64, tshift + (size_t)l * Rmax * C, cshift + (size_t)l * Rmax * C};
+        }
+        P.BN = BN;
+        P.nphases = (int)phases.size();
+        P.nitems_max = max_items;
+        P.ntiles_max = max_tiles;
+        P.jobs = pk_alloc<pk::Job>(jobs.size());
+        P.items = pk_alloc<pk::Item>(items.size());
+        P.phases = pk_alloc<pk::Phase>(phases.size());
+        P.layers = pk_alloc<pk::Layer>(layers.size());
+        P.ws = pk_alloc<float>((size_t)max_items * BN * 128);
+        P.tickets = pk_alloc<int>(max_tiles);
+        if (!P.jobs || !P.items || !P.phases || !P.layers || !P.ws || !P.tickets)
+            return fail(RWKV_E_CUDA, "persistent step: program allocation failed");
+        cudaMemcpy(P.jobs, jobs.data(), jobs.size() * sizeof(pk::Job), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.items, items.data(), items.size() * sizeof(pk::Item), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.phases, phases.data(), phases.size() * sizeof(pk::Phase), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.layers, layers.data(), layers.size() * sizeof(pk::Layer), cudaMemcpyHostToDevice);
+        cudaMemset(P.tickets, 0, (size_t)max_tiles * sizeof(int));
+        return check_launch("persistent step: program upload");
+    }
+
+    template <int BN>
+    cudaError_t pk_launch(const pk::Args& a, cudaStream_t st) {
+        auto kern = pk::x070_persist_kernel<BN>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pk::SMEM);
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(sm_count);
+        cfg.blockDim = dim3(pk::THREADS);
+        cfg.dynamicSmemBytes = pk::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once (grid barriers)
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, a);
+    }
+
+    int pk_step(int R, cudaStream_t st) {
+        if (int rc = pk_repack(st)) return rc;
+        if (!pk_bar && !(pk_bar = pk_alloc<unsigned int>(1))) return fail(RWKV_E_CUDA, "persistent step: allocation failed");
+        auto it = pk_progs.find(R);
+        if (it == pk_progs.end()) {
+            PkProgram P;
+            if (int rc = pk_build(R, P)) return rc;
+            it = pk_progs.emplace(R, P).first;
+        }
+        const PkProgram& P = it->second;
+        if (pk_occ < 0) {
+            int n = 0;
+            cudaFuncSetAttribute(pk::x070_persist_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, pk::SMEM);
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pk::x070_persist_kernel<64>, pk::THREADS, pk::SMEM) !=
+                cudaSuccess)
+                n = 0;
+            cudaGetLastError();
+            pk_occ = n;
+        }
+        if (pk_occ < 1) return fail(RWKV_E_UNSUPPORTED, "persistent step: the kernel does not fit on an SM");
+        pk::Args a{};
+        a.jobs = P.jobs; a.items = P.items; a.phases = P.phases; a.layers = P.layers;
+        a.nphases = P.nphases; a.R = R; a.C = C; a.H = H; a.V = V;
+        a.x = x; a.r = r; a.k = k; a.v = v; a.wdec = wdec; a.a = this->a; a.g = g; a.vv = vv; a.vfirst = vfirst;
+        a.logits = logits; a.ws = P.ws;
+        a.mix = (__half*)mix; a.tail = (__half*)tail; a.xk = (__half*)xk; a.lnout = (__half*)lnout;
+        a.ids = ids; a.amax_keys = amax_keys;
+        a.emb_wq = emb.wq; a.emb_sc = emb.sc; a.emb_bi = emb.bi;
+        a.ln0w = ln0w; a.ln0b = ln0b; a.lnow = lnow; a.lnob = lnob;
+        a.tickets = P.tickets; a.bar = pk_bar; a.err = gerr; a.err_host = gflag.host_dev;
+        cudaMemsetAsync(pk_bar, 0, sizeof(unsigned int), st);
+        cudaMemsetAsync(P.tickets, 0, (size_t)P.ntiles_max * sizeof(int), st);
+        const cudaError_t e = P.BN == 16 ? pk_launch<16>(a, st) : P.BN == 32 ? pk_launch<32>(a, st) : pk_launch<64>(a, st);
+        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "x070_persist_kernel: %s", cudaGetErrorString(e));
+        mark("persistent_step");
+        return RWKV_OK;
+    }
+
     int run_step(int R, cudaStream_t st) {
+        if (pk_eligible(R)) return pk_step(R, st);
         return f16act ? step_body<__half>(R, st) : step_body<float>(R, st);
     }
 
     int graph_step(int R, cudaStream_t st) {
+        if (pk_eligible(R)) return run_step(R, st);  // one launch per step: nothing to capture
         auto it = graphs.find(R);
         if (it == graphs.end()) {
             cudaGraph_t gph;
@@ -1217,6 +1493,17 @@ int rwkv_x070_profile_step(rwkv_x070_t h, int rows, float* ms_host, int cap, cha
     X070& m = *reinterpret_cast<X070*>(h);
     RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax, RWKV_E_SHAPE, "rows %d not in 1..%d", rows, m.Rmax);
     return m.profile_step(rows, (cudaStream_t)stream, ms_host, cap, names_host, names_cap, count);
+}
+
+int rwkv_x070_set_decode_path(rwkv_x070_t h, int path) {
+    RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_set_decode_path: NULL handle");
+    RWKV_REQUIRE(path == 0 || path == 1, RWKV_E_SHAPE, "rwkv_x070_set_decode_path: path %d (0 or 1)", path);
+    reinterpret_cast<X070*>(h)->decode_path = path;
+    return ok();
+}
+
+int rwkv_x070_decode_path(rwkv_x070_t h, int rows) {
+    return h && reinterpret_cast<X070*>(h)->pk_eligible(rows) ? 1 : 0;
 }
 
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t h) { return h ? reinterpret_cast<X070*>(h)->weight_bytes : 0; }

@@ -112,3 +112,22 @@ def test_1p5b_width_prefill_matches_oracle(model16, oracle16):
     assert rel_err(got.cpu().numpy(), want) < 2e-3, rel_err(got.cpu().numpy(), want)
     want = oracle16.step(nxt, st)
     assert rel_err(cont.cpu().numpy(), want) < 2e-3, rel_err(cont.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("rows", [16, 32])
+def test_1p5b_width_persistent_tile_widths(model16, oracle16, rows):
+    """The persistent step's 16- and 32-row tiles at the 1.5B width (64 rows
+    is covered above: the default path there)."""
+    from oracle import x070_oracle as XO
+    from swiftrwkv_b200 import _lib
+    assert _lib.lib().rwkv_x070_decode_path(model16.h, rows) == 1
+    ids = XO.splitmix_ids(rows, 2, vocab=V, seed=100 + rows)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        model16.reset(rows)
+        got = [model16.step(torch.from_numpy(ids[:, t]).cuda(), use_graph=True) for t in range(2)]
+    s.synchronize()
+    st = oracle16.new_state(rows)
+    for t in range(2):
+        want = oracle16.step(ids[:, t], st)
+        assert rel_err(got[t].cpu().numpy(), want) < 2e-3, (rows, t)

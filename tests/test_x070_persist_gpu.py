@@ -1,0 +1,92 @@
+"""The persistent decode step (one cooperative launch per step, 9..64 rows,
+fp16 activations) against the decode oracle and against the per-kernel step.
+
+Both paths compute the projections with the fp16-dequantised weight (the
+tcgen05 arithmetic above 8 rows), which the oracle models; they group the
+split-K sums differently, so they agree to fp32 rounding carried through fp16
+activations, not bitwise.  Checked: logits within 2e-3 of the oracle over
+several steps (tiny width, and the 1.5B width at 16/32/64 rows -- the three
+tile widths), greedy ids equal to the per-kernel path's, and the state the
+persistent steps leave behind continues correctly on the per-kernel path.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(rows, n_embd=256, vocab=256, n_layer=2, seed=7, fan_in=False):
+    from oracle import x070_oracle as XO
+    from swiftrwkv_b200.x070 import X070Backbone, X070Config
+    cfg = XO.Cfg(n_layer, n_embd, vocab)
+    w = XO.tiny_weights(cfg, seed, fan_in_scale=fan_in)
+    m = X070Backbone(X070Config(n_layer, n_embd, vocab), max_rows=rows, act="f16").load(w)
+    return m, XO.X070Oracle(cfg, w, act="f16")
+
+
+def _steps(m, ids, path):
+    from swiftrwkv_b200 import _lib
+    _lib.call("rwkv_x070_set_decode_path", m.h, path)
+    rows = ids.shape[0]
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        m.reset(rows)
+        out = [m.step(torch.from_numpy(ids[:, t]).cuda(), use_graph=True) for t in range(ids.shape[1])]
+    s.synchronize()
+    return [o.cpu().numpy() for o in out]
+
+
+@pytest.mark.parametrize("rows", [9, 20, 64])
+def test_persistent_step_matches_oracle(cuda, rows):
+    from oracle import x070_oracle as XO
+    from swiftrwkv_b200 import _lib
+    m, ref = _model(rows)
+    assert _lib.lib().rwkv_x070_decode_path(m.h, rows) == 1
+    ids = XO.splitmix_ids(rows, 4, vocab=256, seed=rows)
+    got = _steps(m, ids, 1)
+    st = ref.new_state(rows)
+    for t in range(ids.shape[1]):
+        want = ref.step(ids[:, t], st)
+        assert rel_err(got[t], want) < 2e-3, (rows, t, rel_err(got[t], want))
+    per_kernel = _steps(m, ids, 0)
+    for t in range(ids.shape[1]):
+        assert rel_err(got[t], per_kernel[t]) < 2e-3
+        assert np.array_equal(np.argmax(got[t], 1), np.argmax(per_kernel[t], 1))
+
+
+def test_persistent_state_continues_on_the_per_kernel_path(cuda):
+    from oracle import x070_oracle as XO
+    from swiftrwkv_b200 import _lib
+    rows = 16
+    m, ref = _model(rows)
+    ids = XO.splitmix_ids(rows, 5, vocab=256, seed=3)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        m.reset(rows)
+        _lib.call("rwkv_x070_set_decode_path", m.h, 1)
+        for t in range(3):
+            m.step(torch.from_numpy(ids[:, t]).cuda(), use_graph=True)
+        _lib.call("rwkv_x070_set_decode_path", m.h, 0)
+        got = [m.step(torch.from_numpy(ids[:, t]).cuda(), use_graph=True) for t in range(3, 5)]
+    s.synchronize()
+    st = ref.new_state(rows)
+    for t in range(5):
+        want = ref.step(ids[:, t], st)
+        if t >= 3:
+            assert rel_err(got[t - 3].cpu().numpy(), want) < 2e-3
+
+
+def test_persistent_step_is_not_taken_outside_its_range(cuda):
+    from swiftrwkv_b200 import _lib
+    m, _ = _model(65)
+    L = _lib.lib()
+    assert L.rwkv_x070_decode_path(m.h, 8) == 0      # exact-GEMV rows
+    assert L.rwkv_x070_decode_path(m.h, 65) == 0     # beyond one 64-row tile
+    assert L.rwkv_x070_decode_path(m.h, 40) == 1
+    _lib.call("rwkv_x070_set_decode_path", m.h, 0)
+    assert L.rwkv_x070_decode_path(m.h, 40) == 0
