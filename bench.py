@@ -385,7 +385,18 @@ class Decode15B:
         self.dev_next = torch.zeros(self.rows, dtype=torch.int32, device=dev)
         self.h2d = self.rows * 4
         self.d2h = self.rows * 4
-        self._family()
+        from swiftrwkv_b200 import _lib
+        self.persistent = bool(_lib.lib().rwkv_x070_decode_path(self.m.h, self.rows))
+        if self.persistent:
+            # one cooperative launch per step: the kernel is the whole step
+            self.launches_per_step = 1
+            self.dom_bytes = self.alg_bytes
+            bn = 16 if self.rows <= 16 else 32 if self.rows <= 32 else 64
+            self.kernel = (f"x070_persist_kernel<{bn}> (the whole decode step in one cooperative launch: "
+                           "24 layers' 4-bit and low-rank projections on tcgen05, WKV step + tail, glue, head, "
+                           "argmax; algorithmic bytes = the step's weights + state read/write + shift rows)")
+        else:
+            self._family()
 
     def _family(self):
         """The dominant kernel family: the 4-bit projection GEMMs of the step
@@ -419,7 +430,17 @@ class Decode15B:
         self.pin_ids.copy_(self.pin_out)
 
     def dominant_ms(self, reps):
-        """Average device time per launch of the GEMM family inside the step."""
+        """Average device time per launch of the dominant kernel family inside
+        the step: the persistent step kernel, or the 4-bit GEMM launches."""
+        if self.persistent:
+            # the step profiler times the kernel's phases (grid barrier to grid barrier)
+            ts = []
+            for _ in range(reps):
+                agg, seq = self.m.profile_step(self.rows)
+                if not seq:
+                    raise RuntimeError("step profiler returned no phases")
+                ts.append(sum(t for _, t in seq))
+            return sum(ts) / len(ts)
         tot, n = 0.0, 0
         for _ in range(reps):
             agg, _ = self.m.profile_step(self.rows)

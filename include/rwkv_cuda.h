@@ -391,16 +391,24 @@ int rwkv_x070_inject_wait_error(rwkv_x070_t model, int host_record, rwkv_stream_
  * Stands in for DecodeBench's --step-profile (Sources/DecodeBench/main.swift:146-196). */
 int rwkv_x070_profile_step(rwkv_x070_t model, int rows, float* ms_host, int cap, char* names_host,
                            int names_cap, int* count, rwkv_stream_t stream);
-/* How a decode step runs.  path 1 (the default): for 9..64 rows with fp16
- * activations and no LoRA adapters, the whole step is ONE cooperative launch
- * of a persistent kernel (one CTA per SM, phases separated by grid barriers,
- * weight tiles streamed ahead of their phase); other steps, and every step
- * with path 0, run the per-kernel sequence captured in a CUDA graph.  The
- * arithmetic is the same (the tcgen05 path's fp16-dequantised weights above 8
- * rows); split-K sums may be grouped differently.  rwkv_x070_decode_path
- * returns 1 when a step on `rows` rows takes the persistent kernel.  No
- * counterpart in the reference (MLX schedules the reference's kernels). */
+/* How a decode step runs.  path 0 (the default): the per-kernel sequence
+ * captured in a CUDA graph.  path 1: for 9..64 rows with fp16 activations and
+ * no LoRA adapters, the whole step is ONE cooperative launch of a persistent
+ * kernel (one CTA per SM, phases separated by grid barriers, weight tiles
+ * streamed ahead of their phase); other steps keep the graph.  The arithmetic
+ * is the same (the tcgen05 path's fp16-dequantised weights above 8 rows);
+ * split-K sums are grouped differently.  On the 1.5B step the persistent
+ * kernel is the slower of the two (64 rows: 2.70 vs 2.11 ms), hence the
+ * default.  rwkv_x070_decode_path returns 1 when a step on `rows` rows takes
+ * the persistent kernel.  No counterpart in the reference (MLX schedules the
+ * reference's kernels). */
 int rwkv_x070_set_decode_path(rwkv_x070_t model, int path);
+/* The raw %globaltimer trace of the last rwkv_x070_profile_step that ran the
+ * persistent kernel (CTA 0: phase boundaries at [0, 1024); per pipeline stage
+ * j < 2048: weight copy issued [1024 + j], activation copy issued
+ * [3072 + j], MMA inputs ready [5120 + j], dequantised [7168 + j]; 0 where
+ * nothing was recorded), up to cap entries into out_host. */
+int rwkv_x070_trace(rwkv_x070_t model, uint64_t* out_host, int cap, int* count);
 int rwkv_x070_decode_path(rwkv_x070_t model, int rows);
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t model);
 int rwkv_x070_launches_per_step(rwkv_x070_t model);

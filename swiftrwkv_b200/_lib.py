@@ -76,6 +76,7 @@ _SIGS = {
     "rwkv_x070_inject_wait_error": [P, I, P],
     "rwkv_x070_weight_bytes": [P],
     "rwkv_x070_set_decode_path": [P, I],
+    "rwkv_x070_trace": [P, P, I, P],
     "rwkv_x070_decode_path": [P, I],
     "rwkv_x070_launches_per_step": [P],
     "rwkv_state_broadcast": [P, P, I, I, I, P],

@@ -712,9 +712,12 @@ struct X070 {
 
     // ----- persistent decode step (x070_persist.cuh): one launch per step
 
-    int decode_path = 1;  // 1: the persistent step where it applies; 0: the per-kernel graph
+    // 0 (default): the per-kernel graph; 1: the persistent step where it
+    // applies (measured slower on the 1.5B step: 2.70 vs 2.11 ms at 64 rows)
+    int decode_path = 0;
     struct PkProgram {
         int BN = 0, nphases = 0, nitems_max = 0, ntiles_max = 0;
+        std::vector<std::string> names;  // per phase, for the step profiler
         pk::Job* jobs = nullptr;
         pk::Item* items = nullptr;
         pk::Phase* phases = nullptr;
@@ -724,7 +727,9 @@ struct X070 {
     };
     std::map<int, PkProgram> pk_progs;
     std::vector<void*> pk_allocs;
-    unsigned int* pk_bar = nullptr;
+    unsigned int* pk_bar = nullptr;    // grid barrier counter
+    unsigned long long* pk_trace = nullptr;  // per-phase timestamps when profiling
+    std::vector<unsigned long long> pk_last_trace;  // the last profiled step's trace (rwkv_x070_trace)
     int64_t pk_wver = -1;
     int pk_occ = -1;  // CTAs of the persistent kernel per SM (cached)
 
@@ -823,36 +828,42 @@ struct X070 {
         };
         // A GEMM phase over jobs js: every 128-row tile split along K so that
         // the phase has about one work item per CTA (items of a tile adjacent).
-        int max_items = 1, max_tiles = 1;
+        int max_items = 1, tiles = 0;  // tiles numbered across the program
         auto gemm = [&](std::initializer_list<int> js, int layer) {
             auto stages = [&](const pk::Job& j) { return j.fmt == pk::FMT_Q4 ? j.g.IN / 256 : (j.g.IN + 63) / 64; };
             int64_t T = 0;
             for (int ji : js) T += (int64_t)((jobs[ji].g.OUT + 127) / 128) * stages(jobs[ji]);
             const int target = (int)std::max<int64_t>(1, (T + G - 1) / G);
             pk::Phase ph{pk::PH_GEMM, (int)items.size(), 0, layer};
-            int tile = 0;
+            int& tile = tiles;
             for (int ji : js) {
                 const int S = stages(jobs[ji]);
-                const int nz = (S + target - 1) / target;
+                const int nz = std::min(16, (S + target - 1) / target);  // the kernel sums at most 16 partials
                 for (int m0 = 0; m0 < jobs[ji].g.OUT; m0 += 128, tile++)
                     for (int z = 0; z < nz; z++) {
                         const int a = (int)((int64_t)S * z / nz), b = (int)((int64_t)S * (z + 1) / nz);
-                        items.push_back({ji, m0, a, b - a, tile, z, nz, (int)items.size() - ph.i0});
+                        pk::Item itm{ji, m0, a, b - a, tile, z, nz, (int)items.size() - ph.i0, jobs[ji].fmt, 0, nullptr};
+                        if (jobs[ji].fmt == pk::FMT_Q4)
+                            itm.sb = jobs[ji].sb + (size_t)(m0 / 128) * jobs[ji].sb_stages * pk::WSB;
+                        items.push_back(itm);
                     }
             }
             ph.i1 = (int)items.size();
             max_items = std::max(max_items, ph.i1 - ph.i0);
-            max_tiles = std::max(max_tiles, tile);
             phases.push_back(ph);
         };
+        std::vector<std::string> names;
+        auto named = [&](const char* n) { names.resize(phases.size() - 1); names.push_back(n); };
         __half* mixp = (__half*)mix;
         __half* hidp = (__half*)hidden;
         const size_t RC = (size_t)R * C;
         auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
         phases.push_back({pk::PH_EMBED, 0, 0, -1});
+        named("embed");
         for (int l = 0; l < L; l++) {
             LayerW& w = lw[l];
             phases.push_back({pk::PH_TMIX, 0, 0, l});
+            named("tmix_in");
             const int jr = qj(w.r, M(0), C, ACT_NONE, OUT_F32, r, C);
             const int jk = qj(w.k, M(2), C, ACT_NONE, OUT_F32, k, C);
             const int jv = qj(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
@@ -866,22 +877,37 @@ struct X070 {
                 const int dv = hj(w.vA, rv, C, M(3), C, ACT_NONE, OUT_F16, hidp + rw + ra + rg, hid);
                 const int uv = hj(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
                 gemm({jr, jk, jv, dw, da, dg, dv}, l);
+                named("gemm_rkv_lowrank_down");
                 gemm({uw, ua, ug, uv}, l);
+                named("gemm_lowrank_up");
             } else {
                 gemm({jr, jk, jv, dw, da, dg}, l);
+                named("gemm_rkv_lowrank_down");
                 gemm({uw, ua, ug}, l);
+                named("gemm_lowrank_up");
             }
             phases.push_back({pk::PH_WKV, 0, 0, l});
+            named("wkv_step_tail");
             gemm({qj(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C)}, l);
+            named("gemm_o");
             phases.push_back({pk::PH_CMIX, 0, 0, l});
+            named("cmix_in");
             gemm({qj(w.key, xk, C, ACT_RELU2, OUT_F16, ffn, F)}, l);
+            named("gemm_key");
             gemm({qj(w.value, ffn, F, ACT_NONE, OUT_ADD_F32, x, C)}, l);
+            named("gemm_value");
         }
         phases.push_back({pk::PH_LNOUT, 0, 0, -1});
+        named("ln_out");
         gemm({qj(head, lnout, C, ACT_NONE, OUT_F32, logits, V)}, -1);
+        named("gemm_head");
         phases.push_back({pk::PH_ARGMAX, 0, 0, -1});
+        named("argmax");
         phases.push_back({pk::PH_ARGFIN, 0, 0, -1});
+        named("argmax_finish");
         if (bad) return fail(RWKV_E_CUDA, "persistent step: tensor map encoding failed");
+        if ((int)phases.size() > pk::MAX_PHASES)
+            return fail(RWKV_E_UNSUPPORTED, "persistent step: %d phases, at most %d", (int)phases.size(), pk::MAX_PHASES);
         std::vector<pk::Layer> layers(L);
         for (int l = 0; l < L; l++) {
             const LayerW& w = lw[l];
@@ -889,22 +915,23 @@ struct X070 {
                          wkv + (size_t)l * Rmax * H * 64 * 64, tshift + (size_t)l * Rmax * C, cshift + (size_t)l * Rmax * C};
         }
         P.BN = BN;
+        P.names = names;
         P.nphases = (int)phases.size();
         P.nitems_max = max_items;
-        P.ntiles_max = max_tiles;
+        P.ntiles_max = std::max(1, tiles);
         P.jobs = pk_alloc<pk::Job>(jobs.size());
         P.items = pk_alloc<pk::Item>(items.size());
         P.phases = pk_alloc<pk::Phase>(phases.size());
         P.layers = pk_alloc<pk::Layer>(layers.size());
         P.ws = pk_alloc<float>((size_t)max_items * BN * 128);
-        P.tickets = pk_alloc<int>(max_tiles);
+        P.tickets = pk_alloc<int>(P.ntiles_max);
         if (!P.jobs || !P.items || !P.phases || !P.layers || !P.ws || !P.tickets)
             return fail(RWKV_E_CUDA, "persistent step: program allocation failed");
         cudaMemcpy(P.jobs, jobs.data(), jobs.size() * sizeof(pk::Job), cudaMemcpyHostToDevice);
         cudaMemcpy(P.items, items.data(), items.size() * sizeof(pk::Item), cudaMemcpyHostToDevice);
         cudaMemcpy(P.phases, phases.data(), phases.size() * sizeof(pk::Phase), cudaMemcpyHostToDevice);
         cudaMemcpy(P.layers, layers.data(), layers.size() * sizeof(pk::Layer), cudaMemcpyHostToDevice);
-        cudaMemset(P.tickets, 0, (size_t)max_tiles * sizeof(int));
+        cudaMemset(P.tickets, 0, (size_t)P.ntiles_max * sizeof(int));
         return check_launch("persistent step: program upload");
     }
 
@@ -928,7 +955,9 @@ struct X070 {
 
     int pk_step(int R, cudaStream_t st) {
         if (int rc = pk_repack(st)) return rc;
-        if (!pk_bar && !(pk_bar = pk_alloc<unsigned int>(1))) return fail(RWKV_E_CUDA, "persistent step: allocation failed");
+        const size_t bar_words = 32;
+        if (!pk_bar && !(pk_bar = pk_alloc<unsigned int>(bar_words)))
+            return fail(RWKV_E_CUDA, "persistent step: allocation failed");
         auto it = pk_progs.find(R);
         if (it == pk_progs.end()) {
             PkProgram P;
@@ -956,11 +985,16 @@ struct X070 {
         a.emb_wq = emb.wq; a.emb_sc = emb.sc; a.emb_bi = emb.bi;
         a.ln0w = ln0w; a.ln0b = ln0b; a.lnow = lnow; a.lnob = lnob;
         a.tickets = P.tickets; a.bar = pk_bar; a.err = gerr; a.err_host = gflag.host_dev;
-        cudaMemsetAsync(pk_bar, 0, sizeof(unsigned int), st);
+        if (profiling) {
+            if (!pk_trace && !(pk_trace = pk_alloc<unsigned long long>(pk::T_END)))
+                return fail(RWKV_E_CUDA, "persistent step: trace allocation failed");
+            if (P.nphases + 1 > 1024) return fail(RWKV_E_UNSUPPORTED, "persistent step: too many phases to trace");
+            a.trace = pk_trace;
+        }
+        cudaMemsetAsync(pk_bar, 0, bar_words * sizeof(unsigned int), st);
         cudaMemsetAsync(P.tickets, 0, (size_t)P.ntiles_max * sizeof(int), st);
         const cudaError_t e = P.BN == 16 ? pk_launch<16>(a, st) : P.BN == 32 ? pk_launch<32>(a, st) : pk_launch<64>(a, st);
         if (e != cudaSuccess) return fail(RWKV_E_CUDA, "x070_persist_kernel: %s", cudaGetErrorString(e));
-        mark("persistent_step");
         return RWKV_OK;
     }
 
@@ -996,6 +1030,7 @@ struct X070 {
     // replayed once: device-side per-launch milliseconds into ms[] (up to
     // cap) and their names, '\n'-separated.
     int profile_step(int R, cudaStream_t st, float* ms, int cap, char* names, int names_cap, int* count) {
+        if (pk_eligible(R)) return profile_persistent(R, st, ms, cap, names, names_cap, count);
         cudaStream_t cs = st ? st : own;
         if (!st) {
             cudaEventRecord(ev_in, st);
@@ -1049,6 +1084,37 @@ struct X070 {
             cudaStreamWaitEvent(st, ev_out, 0);
         }
         return rc;
+    }
+
+    // The persistent step's phases: device milliseconds between CTA 0's
+    // passes through consecutive grid barriers (%globaltimer), one entry per
+    // phase named after what it runs.
+    int profile_persistent(int R, cudaStream_t st, float* ms, int cap, char* names, int names_cap, int* count) {
+        profiling = true;
+        prof_names.clear();
+        int rc = pk_step(R, st);
+        profiling = false;
+        prof_names.clear();
+        if (rc) return rc;
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "profile: persistent step failed");
+        const PkProgram& P = pk_progs.at(R);
+        pk_last_trace.resize(pk::T_END);
+        cudaMemcpy(pk_last_trace.data(), pk_trace, pk::T_END * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        std::vector<unsigned long long> t(P.nphases + 1);
+        cudaMemcpy(t.data(), pk_trace, t.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        std::string all;
+        int n = 0;
+        for (int p = 0; p < P.nphases; p++) {
+            if (n < cap) ms[n++] = (float)((t[p + 1] - t[p]) * 1e-6);
+            all += P.names[p];
+            all += "\n";
+        }
+        *count = n;
+        if (names && names_cap > 0) {
+            strncpy(names, all.c_str(), names_cap - 1);
+            names[names_cap - 1] = 0;
+        }
+        return check_launch("rwkv_x070_profile_step");
     }
 
     // graph_step on any stream, the legacy default stream included.
@@ -1499,6 +1565,15 @@ int rwkv_x070_set_decode_path(rwkv_x070_t h, int path) {
     RWKV_REQUIRE(h, RWKV_E_NULL, "rwkv_x070_set_decode_path: NULL handle");
     RWKV_REQUIRE(path == 0 || path == 1, RWKV_E_SHAPE, "rwkv_x070_set_decode_path: path %d (0 or 1)", path);
     reinterpret_cast<X070*>(h)->decode_path = path;
+    return ok();
+}
+
+int rwkv_x070_trace(rwkv_x070_t h, uint64_t* out_host, int cap, int* count) {
+    RWKV_REQUIRE(h && out_host && count, RWKV_E_NULL, "rwkv_x070_trace: NULL argument");
+    const auto& t = reinterpret_cast<X070*>(h)->pk_last_trace;
+    const int n = std::min<int>(cap, (int)t.size());
+    for (int i = 0; i < n; i++) out_host[i] = t[i];
+    *count = n;
     return ok();
 }
 

@@ -15,7 +15,7 @@
 //   ARGFIN
 //
 // Weights do not depend on the activations, so the TMA producer of each CTA
-// streams the weight tiles of its GEMM work items into an 8-slot ring ahead of
+// streams the weight tiles of its GEMM work items into a 6-slot ring ahead of
 // the phase they belong to -- across barriers, glue phases and layers -- and
 // issues a tile's activation loads only once its phase has begun.  Only the
 // activation loads, the dequantisation of weights already in shared memory,
@@ -46,20 +46,22 @@ namespace pk {
 constexpr int WORKERS = 8;                    // worker warps 2..9
 constexpr int THREADS = 64 + 32 * WORKERS;    // 320
 constexpr int WT = 32 * WORKERS;              // 256 worker threads
-constexpr int WST = 8;                        // weight ring slots
+constexpr int WST = 6;                        // weight ring slots
 constexpr int WCODE = 128 * 128;              // 4-bit stage: 128 rows x 256 codes; fp16 stage: 128 rows x 64
 constexpr int WSB = 128 * 16;                 // 4-bit stage: per row 4 x (scale, bias) fp16
 constexpr int WSLOT = WCODE + WSB;            // 18 KB (multiple of 1024)
-constexpr int XST = 2;                        // activation ring slots
+constexpr int XST = 3;                        // activation ring slots
 constexpr int XSLOT = 4 * 64 * 128;           // 4 boxes of 64 rows x 64 fp16 (128-byte rows)
 constexpr int TMEM_COLS = 512;                // acc b: [64 b, 64 b + 64); A stage a: [256 + 128 a, +128)
 constexpr int A_COL = 256;
 constexpr int NACC = 2, NA = 2;
 constexpr int GLUE_SMEM = 2 * 12 * 64 * 4 + 64;  // two WKV half-groups' vectors + reduction scratch
+constexpr int MAX_PHASES = 256;               // phase table copied into shared memory
 constexpr int W_OFF = 0;
 constexpr int X_OFF = W_OFF + WST * WSLOT;
 constexpr int G_OFF = X_OFF + XST * XSLOT;
-constexpr int B_OFF = G_OFF + GLUE_SMEM;
+constexpr int P_OFF = G_OFF + GLUE_SMEM;
+constexpr int B_OFF = P_OFF + MAX_PHASES * 16;
 constexpr int NBAR = 2 * WST + 2 * XST + 2 * NA + 2 * NACC + 1;
 constexpr int T_OFF = B_OFF + NBAR * 8;
 constexpr int SMEM = T_OFF + 32 + 1024;       // + slack for 1024-byte alignment
@@ -80,10 +82,13 @@ struct alignas(128) Job {
 };
 
 // A work item: job, m-block, K stages [s0, s0 + nst) (256 codes per 4-bit
-// stage, 64 per fp16 stage), split z of nz of tile `tile`; its partial (if nz
-// > 1) is workspace slot `slot` (the tile's splits are slots slot - z ..).
-struct Item {
+// stage, 64 per fp16 stage), split z of nz of tile `tile` (numbered across the
+// whole program: one ticket per tile per step); its partial (if nz > 1) is
+// workspace slot `slot` of the phase (the tile's splits are slots slot - z ..).
+struct alignas(16) Item {
     int job, m0, s0, nst, tile, z, nz, slot;
+    int fmt, pad;
+    const unsigned char* sb;  // 4-bit: the m-block's repacked (scale, bias) stages
 };
 
 struct Phase {
@@ -109,11 +114,21 @@ struct Args {
     const uint32_t* emb_wq;
     const __half *emb_sc, *emb_bi;
     const float *ln0w, *ln0b, *lnow, *lnob;
-    int* tickets;
+    int* tickets;       // one per split tile of the program (zeroed before each launch)
     unsigned int* bar;  // grid barrier counter (zeroed before each launch)
     int* err;
     int* err_host;
+    // nullable (step profiler): %globaltimer of CTA 0 at the start and after
+    // each phase's barrier [0, 1024); per pipeline stage j < 2048 of CTA 0:
+    // weight copy issued [T_W + j], activation copy issued [T_X + j], MMA
+    // inputs ready [T_M + j], dequantised into TMEM [T_D + j]
+    unsigned long long* trace;
 };
+// per work item k < 512 of CTA 0: [T_E + 4 k + 0] accumulator ready, +1 drained,
+// +2 output or partial written (and counted), +3 its split tile reduced
+// per phase p < 256 and CTA c < 160: [T_C + 160 p + c] the CTA's workers done
+constexpr int T_W = 1024, T_X = T_W + 2048, T_M = T_X + 2048, T_D = T_M + 2048, T_E = T_D + 2048,
+              T_C = T_E + 4 * 512, T_END = T_C + 160 * 256;
 
 // ------------------------------------------------------------------ helpers
 
@@ -136,12 +151,14 @@ __device__ __forceinline__ float wsum(float v, float* sh, int wt) {
 // ordered before the meeting), counts itself in and spins with acquire loads
 // until every CTA has; the workers meet again.  Returns false (to every
 // worker, through *flag) when the error flag is set or the wait expires.
-__device__ __forceinline__ bool grid_barrier(unsigned int* bar, unsigned int target, int* err, int wt, int* flag) {
+__device__ __forceinline__ bool grid_barrier(unsigned int* bar, unsigned int gen, int* err, int wt, int* flag) {
     wbar(1, WT);
     if (wt == 0) {
+        // acq_rel: releases this CTA's writes (ordered before it by the
+        // meeting), and the polling acquire takes every other CTA's
         bool ok = true;
-        __threadfence();
-        atomicAdd(bar, 1u);
+        const unsigned int target = gen * gridDim.x;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const uint64_t t0 = tc::gtime();
         for (uint32_t it = 0;; it++) {
             unsigned int v;
@@ -156,7 +173,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* bar, unsigned int tar
                 }
             }
         }
-        __threadfence();
         *flag = ok;
     }
     wbar(1, WT);
@@ -172,10 +188,10 @@ __device__ __forceinline__ void ld4(float4* d, const float* __restrict__ p, int 
     }
 }
 
-// Two-pass LayerNorm (eps 1e-5) over the worker threads, in place.
+// Two-pass LayerNorm (eps 1e-5) over the worker threads, in place; w4 / b4:
+// the weight and bias columns, loaded by the caller with everything else.
 template <int GV>
-__device__ __forceinline__ void ln4(float4* v, const float* __restrict__ w, const float* __restrict__ b, int C,
-                                    float* sh, int wt) {
+__device__ __forceinline__ void ln4(float4* v, const float4* w4, const float4* b4, int C, float* sh, int wt) {
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < GV; i++)
@@ -191,13 +207,10 @@ __device__ __forceinline__ void ln4(float4* v, const float* __restrict__ w, cons
     const float den = sqrtf(wsum(q, sh, wt) / (float)C + 1e-5f);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
-        const int c = 4 * (wt + WT * i);
-        if (c >= C) continue;
-        const float4 ww = *reinterpret_cast<const float4*>(w + c), bb = *reinterpret_cast<const float4*>(b + c);
-        v[i].x = (v[i].x - mean) / den * ww.x + bb.x;
-        v[i].y = (v[i].y - mean) / den * ww.y + bb.y;
-        v[i].z = (v[i].z - mean) / den * ww.z + bb.z;
-        v[i].w = (v[i].w - mean) / den * ww.w + bb.w;
+        v[i].x = (v[i].x - mean) / den * w4[i].x + b4[i].x;
+        v[i].y = (v[i].y - mean) / den * w4[i].y + b4[i].y;
+        v[i].z = (v[i].z - mean) / den * w4[i].z + b4[i].z;
+        v[i].w = (v[i].w - mean) / den * w4[i].w + b4[i].w;
     }
 }
 
@@ -223,7 +236,10 @@ __device__ void do_embed(const Args& A, int n, float* sh, int wt) {
         }
         v[i] = make_float4(e[0], e[1], e[2], e[3]);
     }
-    ln4<GV>(v, A.ln0w, A.ln0b, C, sh, wt);
+    float4 w4[GV], b4[GV];
+    ld4<GV>(w4, A.ln0w, C, wt);
+    ld4<GV>(b4, A.ln0b, C, wt);
+    ln4<GV>(v, w4, b4, C, sh, wt);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
         const int c = 4 * (wt + WT * i);
@@ -235,10 +251,15 @@ __device__ void do_embed(const Args& A, int n, float* sh, int wt) {
 template <int GV>
 __device__ void do_tmix(const Args& A, const Layer& L, int n, float* sh, int wt) {
     const int C = A.C, R = A.R;
-    float4 v[GV], sv[GV];
+    // every load first: one round trip
+    float4 v[GV], sv[GV], w4[GV], b4[GV], cf[6][GV];
     ld4<GV>(v, A.x + (int64_t)n * C, C, wt);
     ld4<GV>(sv, L.tshift + (int64_t)n * C, C, wt);
-    ln4<GV>(v, L.ln1w, L.ln1b, C, sh, wt);
+    ld4<GV>(w4, L.ln1w, C, wt);
+    ld4<GV>(b4, L.ln1b, C, wt);
+#pragma unroll
+    for (int m = 0; m < 6; m++) ld4<GV>(cf[m], L.coef6 + m * C, C, wt);
+    ln4<GV>(v, w4, b4, C, sh, wt);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
         const int c = 4 * (wt + WT * i);
@@ -247,8 +268,7 @@ __device__ void do_tmix(const Args& A, const Layer& L, int n, float* sh, int wt)
         const float4 xx = sub4(sv[i], v[i]);
         *reinterpret_cast<float4*>(L.tshift + o) = v[i];
 #pragma unroll
-        for (int m = 0; m < 6; m++)
-            st_act4(A.mix + (int64_t)m * R * C + o, lerp4(v[i], xx, *reinterpret_cast<const float4*>(L.coef6 + m * C + c)));
+        for (int m = 0; m < 6; m++) st_act4(A.mix + (int64_t)m * R * C + o, lerp4(v[i], xx, cf[m][i]));
     }
 }
 
@@ -256,26 +276,31 @@ __device__ void do_tmix(const Args& A, const Layer& L, int n, float* sh, int wt)
 template <int GV>
 __device__ void do_cmix(const Args& A, const Layer& L, int n, float* sh, int wt) {
     const int C = A.C;
-    float4 v[GV], sv[GV];
+    float4 v[GV], sv[GV], w4[GV], b4[GV], cf[GV];
     ld4<GV>(v, A.x + (int64_t)n * C, C, wt);
     ld4<GV>(sv, L.cshift + (int64_t)n * C, C, wt);
-    ln4<GV>(v, L.ln2w, L.ln2b, C, sh, wt);
+    ld4<GV>(w4, L.ln2w, C, wt);
+    ld4<GV>(b4, L.ln2b, C, wt);
+    ld4<GV>(cf, L.cxk, C, wt);
+    ln4<GV>(v, w4, b4, C, sh, wt);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
         const int c = 4 * (wt + WT * i);
         if (c >= C) continue;
         const int64_t o = (int64_t)n * C + c;
         *reinterpret_cast<float4*>(L.cshift + o) = v[i];
-        st_act4(A.xk + o, lerp4(v[i], sub4(sv[i], v[i]), *reinterpret_cast<const float4*>(L.cxk + c)));
+        st_act4(A.xk + o, lerp4(v[i], sub4(sv[i], v[i]), cf[i]));
     }
 }
 
 template <int GV>
 __device__ void do_lnout(const Args& A, int n, float* sh, int wt) {
     const int C = A.C;
-    float4 v[GV];
+    float4 v[GV], w4[GV], b4[GV];
     ld4<GV>(v, A.x + (int64_t)n * C, C, wt);
-    ln4<GV>(v, A.lnow, A.lnob, C, sh, wt);
+    ld4<GV>(w4, A.lnow, C, wt);
+    ld4<GV>(b4, A.lnob, C, wt);
+    ln4<GV>(v, w4, b4, C, sh, wt);
 #pragma unroll
     for (int i = 0; i < GV; i++) {
         const int c = 4 * (wt + WT * i);
@@ -283,9 +308,45 @@ __device__ void do_lnout(const Args& A, int n, float* sh, int wt) {
     }
 }
 
+// This thread's 16 state rows x 4 columns of (row, head) rh (t = 0..127).
+__device__ __forceinline__ void wkv_load(const Layer& L, int rh, int t, float4* s) {
+    constexpr int N = 64, RPW = 16;
+    const int warp = t >> 5, lane = t & 31;
+    const float* hp = L.state + (size_t)rh * N * N + (size_t)(RPW * warp + (lane >> 4)) * N + 4 * (lane & 15);
+#pragma unroll
+    for (int p = 0; p < RPW / 2; p++) s[p] = __ldcg(reinterpret_cast<const float4*>(hp + (size_t)2 * p * N));
+}
+
+// The per-column vectors of (row, head) rh this thread needs (t < 64: column
+// t of k, a, r, w, k_k, k_a, v, v_first, v-gate; t >= 64: column t - 64 of
+// r_k, ln_x weight / bias, gate), loaded one item ahead.
+__device__ __forceinline__ void wkv_vec_load(const Args& A, const Layer& L, int rh, int layer0, int t, float* f) {
+    constexpr int N = 64;
+    const size_t vb = (size_t)rh * N, hb = (size_t)(rh % A.H) * N;
+    if (t < N) {
+        f[0] = A.k[vb + t];
+        f[1] = A.a[vb + t];
+        f[2] = A.r[vb + t];
+        f[3] = A.wdec[vb + t];
+        f[4] = L.kkw[hb + t];
+        f[5] = L.kaw[hb + t];
+        f[6] = A.v[vb + t];
+        f[7] = layer0 ? 0.f : A.vfirst[vb + t];
+        f[8] = layer0 ? 0.f : A.vv[vb + t];
+    } else {
+        const int c = t - N;
+        f[0] = L.rkw[hb + c];
+        f[1] = L.lnxw[hb + c];
+        f[2] = L.lnxb[hb + c];
+        f[3] = A.g[vb + c];
+    }
+}
+
 // WKV step + tail of (row, head) rh by a half-group of 4 warps (t = 0..127),
-// x070_wkv_kernel's arithmetic; sv: this half-group's 11 x 64 floats + 2.
-__device__ void do_wkv(const Args& A, const Layer& L, int rh, int layer0, float* sv, int t, int half) {
+// x070_wkv_kernel's arithmetic, from the state rows s (wkv_load) and the
+// vectors f (wkv_vec_load); sv: this half-group's 11 x 64 floats + 2.
+__device__ void do_wkv(const Args& A, const Layer& L, int rh, int layer0, float* sv, int t, int half, float4* s,
+                       const float* f) {
     constexpr int N = 64, RPW = 16;
     float *r_s = sv, *w_s = sv + 64, *kp_s = sv + 128, *aw_s = sv + 192, *bw_s = sv + 256, *v_s = sv + 320;
     float *y_s = sv + 384, *rk_s = sv + 448, *lw_s = sv + 512, *lb_s = sv + 576, *g_s = sv + 640, *red = sv + 704;
@@ -295,25 +356,21 @@ __device__ void do_wkv(const Args& A, const Layer& L, int rh, int layer0, float*
     const int hlf = lane >> 4, c0 = 4 * (lane & 15);
     const size_t vb = (size_t)rh * N, hb = (size_t)hi * N;
     float* hp = L.state + (size_t)rh * N * N + (size_t)(RPW * warp + hlf) * N + c0;
-    float4 s[RPW / 2];
-#pragma unroll
-    for (int p = 0; p < RPW / 2; p++) s[p] = *reinterpret_cast<const float4*>(hp + (size_t)2 * p * N);
     if (t < N) {
         const int c = t;
-        const float kr = A.k[vb + c], aa = A.a[vb + c];
-        const float kk = kr * L.kkw[hb + c];
+        const float kr = f[0], aa = f[1];
+        const float kk = kr * f[4];
         const float ss = warp_sum(kk * kk);
         if ((c & 31) == 0) red[c >> 5] = ss;
-        r_s[c] = A.r[vb + c];
-        w_s[c] = A.wdec[vb + c];
-        const float kp = kr * (1.0f + (aa - 1.0f) * L.kaw[hb + c]);
+        r_s[c] = f[2];
+        w_s[c] = f[3];
+        const float kp = kr * (1.0f + (aa - 1.0f) * f[5]);
         kp_s[c] = kp;
-        float vd = A.v[vb + c];
+        float vd = f[6];
         if (layer0) {
             A.vfirst[vb + c] = vd;
         } else {
-            const float f = A.vfirst[vb + c];
-            vd = vd + (f - vd) * A.vv[vb + c];
+            vd = vd + (f[7] - vd) * f[8];
         }
         v_s[c] = vd;
         wbar(4 + half, 64);
@@ -323,10 +380,10 @@ __device__ void do_wkv(const Args& A, const Layer& L, int rh, int layer0, float*
         bw_s[c] = kn * aa;
     } else {
         const int c = t - N;
-        rk_s[c] = L.rkw[hb + c];
-        lw_s[c] = L.lnxw[hb + c];
-        lb_s[c] = L.lnxb[hb + c];
-        g_s[c] = A.g[vb + c];
+        rk_s[c] = f[0];
+        lw_s[c] = f[1];
+        lb_s[c] = f[2];
+        g_s[c] = f[3];
     }
     wbar(2 + half, 128);
     const float4 aw = *reinterpret_cast<const float4*>(aw_s + c0);
@@ -382,6 +439,7 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
     uint64_t* accempty = accfull + NACC;
     uint64_t* mdone = accempty + NACC;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + T_OFF);
+    Phase* phs = reinterpret_cast<Phase*>(smem + P_OFF);
     int* last_flag = reinterpret_cast<int*>(smem + T_OFF + 16);
     float* glue = reinterpret_cast<float*>(smem + G_OFF);
 
@@ -389,6 +447,7 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
     const int G = gridDim.x, cta = blockIdx.x;
     int* err = A.err;
 
+    for (int p = tid; p < A.nphases; p += THREADS) phs[p] = A.phases[p];
     if (tid == 0) {
         for (int s = 0; s < WST; s++) {
             tc::mbar_init(wfull + s, 1);
@@ -427,11 +486,11 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
             int px = 0, ix = -1, sx = 0, nx = 0;  // activation cursor
             bool wdone = false, xdone = false;
             int started = 0;                      // phases known to have begun (phase 0 at launch)
-            // next GEMM item of this CTA at or after (p, i): returns false at the end
+            // next GEMM item of this CTA after (p, i): false at the end
             auto next_item = [&](int& p, int& i) {
                 for (;;) {
                     if (p >= A.nphases) return false;
-                    const Phase ph = A.phases[p];
+                    const Phase ph = phs[p];
                     if (ph.type == PH_GEMM) {
                         const int ni = i < 0 ? ph.i0 + cta : i + G;
                         if (ni < ph.i1) {
@@ -443,67 +502,70 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                     i = -1;
                 }
             };
+            Item wi{}, xi{};  // the cursors' items, read once each
             wdone = !next_item(pw, iw);
+            if (!wdone) wi = A.items[iw];
             xdone = !next_item(px, ix);
-            const uint64_t t_start = tc::gtime();
-            uint64_t t_last = t_start;
+            if (!xdone) xi = A.items[ix];
+            uint64_t t_last = tc::gtime();
             for (uint32_t spin = 0; (!wdone || !xdone) && ok; spin++) {
                 bool prog = false;
                 if (!wdone && (nw < WST || tc::mbar_try(wempty + (nw % WST), ((nw / WST) - 1) & 1))) {
-                    const Item it = A.items[iw];
-                    const Job& jb = A.jobs[it.job];
+                    const CUtensorMap* wm = &A.jobs[wi.job].wmap;
                     const int s = nw % WST;
                     unsigned char* dst = smem + W_OFF + s * WSLOT;
-                    const int st = it.s0 + sw;
-                    if (jb.fmt == FMT_Q4) {
+                    const int st = wi.s0 + sw;
+                    if (wi.fmt == FMT_Q4) {
                         tc::mbar_expect_tx(wfull + s, WCODE + WSB);
-                        tc::tma_2d(dst, &jb.wmap, wfull + s, 32 * st, it.m0);
-                        const unsigned char* src = jb.sb + ((size_t)(it.m0 / 128) * jb.sb_stages + st) * WSB;
+                        tc::tma_2d(dst, wm, wfull + s, 32 * st, wi.m0);
                         asm volatile(
                             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                                 tc::saddr(dst + WCODE)),
-                            "l"(src), "r"(WSB), "r"(tc::saddr(wfull + s))
+                            "l"(wi.sb + (size_t)st * WSB), "r"(WSB), "r"(tc::saddr(wfull + s))
                             : "memory");
                     } else {
                         tc::mbar_expect_tx(wfull + s, WCODE);
-                        tc::tma_2d(dst, &jb.wmap, wfull + s, 64 * st, it.m0);
+                        tc::tma_2d(dst, wm, wfull + s, 64 * st, wi.m0);
                     }
+                    if (A.trace && cta == 0 && nw < 2048) A.trace[T_W + nw] = tc::gtime();
                     nw++;
-                    if (++sw == it.nst) {
+                    if (++sw == wi.nst) {
                         sw = 0;
                         wdone = !next_item(pw, iw);
+                        if (!wdone) wi = A.items[iw];
                     }
                     prog = true;
                 }
-                if (!xdone && px > started && (spin & 7) == 0) {
-                    // has phase px begun?  (every CTA has passed the barrier ending px - 1;
-                    // the acquire orders the other CTAs' writes of px's inputs before the loads)
+                if (!xdone && px > started) {
+                    // has phase px begun?  (every CTA has passed the barrier ending
+                    // px - 1; the acquire orders the other CTAs' writes of px's inputs
+                    // before the loads)
                     unsigned int v;
                     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.bar) : "memory");
-                    const int done_phases = (int)(v / (unsigned)G);
-                    if (done_phases > started) {
-                        started = done_phases;
+                    if ((int)(v / (unsigned)G) > started) {
+                        started = (int)(v / (unsigned)G);
                         asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes -> TMA reads
                     }
                 }
                 if (!xdone && px <= started && (nx < XST || tc::mbar_try(xempty + (nx % XST), ((nx / XST) - 1) & 1))) {
-                    const Item it = A.items[ix];
-                    const Job& jb = A.jobs[it.job];
+                    const CUtensorMap* xm = &A.jobs[xi.job].xmap;
                     const int s = nx % XST;
                     unsigned char* dst = smem + X_OFF + s * XSLOT;
-                    const int st = it.s0 + sx;
-                    if (jb.fmt == FMT_Q4) {
+                    const int st = xi.s0 + sx;
+                    if (xi.fmt == FMT_Q4) {
                         tc::mbar_expect_tx(xfull + s, 4 * BN * 128);
 #pragma unroll
-                        for (int q = 0; q < 4; q++) tc::tma_2d(dst + q * BN * 128, &jb.xmap, xfull + s, 256 * st + 64 * q, 0);
+                        for (int q = 0; q < 4; q++) tc::tma_2d(dst + q * BN * 128, xm, xfull + s, 256 * st + 64 * q, 0);
                     } else {
                         tc::mbar_expect_tx(xfull + s, BN * 128);
-                        tc::tma_2d(dst, &jb.xmap, xfull + s, 64 * st, 0);
+                        tc::tma_2d(dst, xm, xfull + s, 64 * st, 0);
                     }
+                    if (A.trace && cta == 0 && nx < 2048) A.trace[T_X + nx] = tc::gtime();
                     nx++;
-                    if (++sx == it.nst) {
+                    if (++sx == xi.nst) {
                         sx = 0;
                         xdone = !next_item(px, ix);
+                        if (!xdone) xi = A.items[ix];
                     }
                     prog = true;
                 }
@@ -529,11 +591,11 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
             constexpr uint32_t IDESC = tc::idesc_f16(128, BN);
             int nw = 0, na = 0, nacc = 0;
             for (int p = 0; p < A.nphases && ok; p++) {
-                const Phase ph = A.phases[p];
+                const Phase ph = phs[p];
                 if (ph.type != PH_GEMM) continue;
                 for (int i = ph.i0 + cta; i < ph.i1 && ok; i += G) {
                     const Item it = A.items[i];
-                    const int fmt = A.jobs[it.job].fmt;
+                    const int fmt = it.fmt;
                     const int b = nacc % NACC;
                     if (nacc >= NACC && !tc::mbar_wait(accempty + b, ((nacc / NACC) - 1) & 1, err)) { ok = false; break; }
                     const uint32_t dacc = tmem + 64 * b;
@@ -545,6 +607,7 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                         }
                         const int as = na % NA;
                         if (fmt == FMT_Q4 && !tc::mbar_wait(afull + as, (na / NA) & 1, err)) { ok = false; break; }
+                        if (A.trace && cta == 0 && nw < 2048) A.trace[T_M + nw] = tc::gtime();
                         tc::tc_after();
                         const uint32_t xsa = tc::saddr(smem + X_OFF + xs * XSLOT);
                         if (fmt == FMT_Q4) {
@@ -585,9 +648,9 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
         const int R = A.R;
         constexpr int GV = 2;                       // C <= 2048: two 16-byte column groups per thread
         int nw = 0, na = 0, nacc = 0;
-        unsigned int bars = 0;
+        if (A.trace && cta == 0 && wt == 0) A.trace[0] = tc::gtime();
         for (int p = 0; p < A.nphases; p++) {
-            const Phase ph = A.phases[p];
+            const Phase ph = phs[p];
             if (ok) {
                 const Layer* L = ph.layer >= 0 ? A.layers + ph.layer : nullptr;
                 switch (ph.type) {
@@ -604,9 +667,27 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                         for (int n = cta; n < R; n += G) do_lnout<GV>(A, n, sh, wt);
                         break;
                     case PH_WKV: {
-                        const int half = wt >> 7, t = wt & 127;
-                        for (int rh = 2 * cta + half; rh < R * A.H; rh += 2 * G)
-                            do_wkv(A, *L, rh, ph.layer == 0, glue + half * 12 * 64, t, half);
+                        // two (row, head) items at a time; the next item's state is
+                        // loaded while the current one is updated
+                        const int half = wt >> 7, t = wt & 127, RH = R * A.H, l0 = ph.layer == 0;
+                        float4 s[8], sn[8];
+                        float f[9], fn[9];
+                        int rh = 2 * cta + half;
+                        if (rh < RH) {
+                            wkv_load(*L, rh, t, s);
+                            wkv_vec_load(A, *L, rh, l0, t, f);
+                        }
+                        for (; rh < RH; rh += 2 * G) {
+                            if (rh + 2 * G < RH) {
+                                wkv_load(*L, rh + 2 * G, t, sn);
+                                wkv_vec_load(A, *L, rh + 2 * G, l0, t, fn);
+                            }
+                            do_wkv(A, *L, rh, l0, glue + half * 12 * 64, t, half, s, f);
+#pragma unroll
+                            for (int q = 0; q < 8; q++) s[q] = sn[q];
+#pragma unroll
+                            for (int q = 0; q < 9; q++) f[q] = fn[q];
+                        }
                         break;
                     }
                     case PH_ARGMAX: {
@@ -628,11 +709,12 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                             A.amax_keys[n] = 0ull;
                         }
                         break;
-                    case PH_GEMM:
+                    case PH_GEMM: {
+                        const int nacc0 = nacc;
                         for (int i = ph.i0 + cta; i < ph.i1 && ok; i += G) {
                             const Item it = A.items[i];
                             const Job& jb = A.jobs[it.job];
-                            if (jb.fmt == FMT_Q4) {
+                            if (it.fmt == FMT_Q4) {
                                 // dequantise each stage into a TMEM A stage
                                 for (int s = 0; s < it.nst; s++, nw++, na++) {
                                     const int ws = nw % WST, as = na % NA;
@@ -658,6 +740,7 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                                     tc::tmem_st_wait();
                                     tc::tc_before();
                                     tc::mbar_arrive(afull + as);
+                                    if (A.trace && cta == 0 && wt == 0 && nw < 2048) A.trace[T_D + nw] = tc::gtime();
                                 }
                             } else {
                                 nw += it.nst;
@@ -666,6 +749,8 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                             // drain the accumulator: row rl, columns [h CW, (h+1) CW)
                             const int b = nacc % NACC;
                             if (!tc::mbar_wait(accfull + b, (nacc / NACC) & 1, err)) { ok = false; break; }
+                            const bool tr = A.trace && cta == 0 && wt == 0 && nacc < 512;
+                            if (tr) A.trace[T_E + 4 * nacc] = tc::gtime();
                             tc::tc_after();
                             uint32_t acc[CW];
 #pragma unroll
@@ -673,6 +758,8 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                             tc::tmem_ld_wait();
                             tc::tc_before();
                             tc::mbar_arrive(accempty + b);
+                            if (tr) A.trace[T_E + 4 * nacc + 1] = tc::gtime();
+                            const int item_no = nacc;
                             nacc++;
                             const GemvJob g = jb.g;
                             const int o = it.m0 + rl;
@@ -685,42 +772,73 @@ __global__ void __launch_bounds__(THREADS, 1) x070_persist_kernel(const __grid_c
                                     }
                                 }
                             } else {
-                                // split-K: this item's partial, then the last of the tile reduces
+                                // split-K: publish this item's partial (release by one thread
+                                // after the workers meet), then count it in the tile's ticket
                                 float* part = A.ws + (size_t)it.slot * BN * 128;
 #pragma unroll
                                 for (int c = 0; c < CW; c++) part[(h * CW + c) * 128 + rl] = __uint_as_float(acc[c]);
-                                // the partial is published (release by one thread after the
-                                // meeting) before the ticket; the last item acquires them all
                                 wbar(1, WT);
-                                if (wt == 0) {
-                                    __threadfence();
-                                    *last_flag = atomicAdd(A.tickets + it.tile, 1) == it.nz - 1;
-                                    __threadfence();
-                                }
-                                wbar(1, WT);
-                                if (*last_flag) {
-                                    const float* base = A.ws + (size_t)(it.slot - it.z) * BN * 128;
-                                    if (o < g.OUT) {
-#pragma unroll 4
-                                        for (int c = 0; c < CW; c++) {
-                                            const int n = h * CW + c;
-                                            if (n >= R) continue;
-                                            float v = 0.f;
-                                            for (int z = 0; z < it.nz; z++) v += __ldcg(base + ((size_t)z * BN + n) * 128 + rl);
-                                            epilogue(g, o, n, v);
+                                if (wt == 0)
+                                    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(A.tickets + it.tile) : "memory");
+                            }
+                            if (tr) A.trace[T_E + 4 * item_no + 2] = tc::gtime();
+                        }
+                        // split tiles: once all of a tile's partials are in, item z sums
+                        // rows [128 z / nz, 128 (z + 1) / nz) of it over the splits, in
+                        // split order.  Every item of every CTA has published its partial
+                        // before any CTA waits here, so the waits cannot form a cycle.
+                        for (int i = ph.i0 + cta; i < ph.i1 && ok; i += G) {
+                            const Item it = A.items[i];
+                            if (it.nz == 1) continue;
+                            if (wt == 0) {
+                                int complete = 0;
+                                const uint64_t t0 = tc::gtime();
+                                for (uint32_t sp = 0;; sp++) {
+                                    int v;
+                                    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(A.tickets + it.tile) : "memory");
+                                    if (v >= it.nz) { complete = 1; break; }
+                                    if ((sp & 15) == 15) {
+                                        if (*(volatile int*)err) break;
+                                        if (tc::gtime() - t0 > tc::WAIT_LIMIT_NS) {
+                                            atomicExch(err, 1);
+                                            break;
                                         }
                                     }
-                                    if (wt == 0) A.tickets[it.tile] = 0;  // re-armed for the next use
                                 }
-                                wbar(1, WT);
+                                *last_flag = complete;
                             }
+                            wbar(1, WT);
+                            if (!*last_flag) { ok = false; break; }
+                            const GemvJob g = A.jobs[it.job].g;
+                            const int q0 = 32 * it.z / it.nz, q1 = 32 * (it.z + 1) / it.nz;  // row quads
+                            const int nq = q1 - q0;
+                            const float* base = A.ws + (size_t)(it.slot - it.z) * BN * 128;
+                            for (int task = wt; task < R * nq; task += WT) {
+                                const int n = task / nq, rq = 4 * (q0 + task % nq);
+                                float4 v = __ldcg(reinterpret_cast<const float4*>(base + (size_t)n * 128 + rq));
+                                for (int z = 1; z < it.nz; z++) {
+                                    const float4 u = __ldcg(reinterpret_cast<const float4*>(base + ((size_t)z * BN + n) * 128 + rq));
+                                    v.x += u.x;
+                                    v.y += u.y;
+                                    v.z += u.z;
+                                    v.w += u.w;
+                                }
+                                const float vv4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                                for (int j = 0; j < 4; j++)
+                                    if (it.m0 + rq + j < g.OUT) epilogue(g, it.m0 + rq + j, n, vv4[j]);
+                            }
+                            const int k = nacc0 + (i - ph.i0 - cta) / G;
+                            if (A.trace && cta == 0 && wt == 0 && k < 512) A.trace[T_E + 4 * k + 3] = tc::gtime();
                         }
                         break;
+                    }
                 }
             }
             // phase boundary
-            bars += G;
-            if (!grid_barrier(A.bar, bars, err, wt, last_flag + 1)) ok = false;
+            if (A.trace && wt == 0 && cta < 160 && p < 256) A.trace[T_C + 160 * p + cta] = tc::gtime();
+            if (!grid_barrier(A.bar, (unsigned int)(p + 1), err, wt, last_flag + 1)) ok = false;
+            if (A.trace && cta == 0 && wt == 0) A.trace[p + 1] = tc::gtime();
         }
     }
 

@@ -114,12 +114,13 @@ def test_1p5b_width_prefill_matches_oracle(model16, oracle16):
     assert rel_err(cont.cpu().numpy(), want) < 2e-3, rel_err(cont.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("rows", [16, 32])
-def test_1p5b_width_persistent_tile_widths(model16, oracle16, rows):
-    """The persistent step's 16- and 32-row tiles at the 1.5B width (64 rows
-    is covered above: the default path there)."""
+@pytest.mark.parametrize("rows", [16, 32, 64])
+def test_1p5b_width_persistent_step(model16, oracle16, rows):
+    """The persistent decode step (rwkv_x070_set_decode_path 1) at the 1.5B
+    width, at each of its tile widths (16, 32, 64 rows)."""
     from oracle import x070_oracle as XO
     from swiftrwkv_b200 import _lib
+    _lib.call("rwkv_x070_set_decode_path", model16.h, 1)
     assert _lib.lib().rwkv_x070_decode_path(model16.h, rows) == 1
     ids = XO.splitmix_ids(rows, 2, vocab=V, seed=100 + rows)
     s = torch.cuda.Stream()
@@ -127,6 +128,7 @@ def test_1p5b_width_persistent_tile_widths(model16, oracle16, rows):
         model16.reset(rows)
         got = [model16.step(torch.from_numpy(ids[:, t]).cuda(), use_graph=True) for t in range(2)]
     s.synchronize()
+    _lib.call("rwkv_x070_set_decode_path", model16.h, 0)
     st = oracle16.new_state(rows)
     for t in range(2):
         want = oracle16.step(ids[:, t], st)

@@ -6,7 +6,8 @@ tcgen05 arithmetic above 8 rows), which the oracle models; they group the
 split-K sums differently, so they agree to fp32 rounding carried through fp16
 activations, not bitwise.  Checked: logits within 2e-3 of the oracle over
 several steps (tiny width, and the 1.5B width at 16/32/64 rows -- the three
-tile widths), greedy ids equal to the per-kernel path's, and the state the
+tile widths), greedy ids equal to the per-kernel path's where the top two
+logits are not a near tie, and the state the
 persistent steps leave behind continues correctly on the per-kernel path.
 """
 from __future__ import annotations
@@ -46,6 +47,7 @@ def test_persistent_step_matches_oracle(cuda, rows):
     from oracle import x070_oracle as XO
     from swiftrwkv_b200 import _lib
     m, ref = _model(rows)
+    _lib.call("rwkv_x070_set_decode_path", m.h, 1)
     assert _lib.lib().rwkv_x070_decode_path(m.h, rows) == 1
     ids = XO.splitmix_ids(rows, 4, vocab=256, seed=rows)
     got = _steps(m, ids, 1)
@@ -56,7 +58,10 @@ def test_persistent_step_matches_oracle(cuda, rows):
     per_kernel = _steps(m, ids, 0)
     for t in range(ids.shape[1]):
         assert rel_err(got[t], per_kernel[t]) < 2e-3
-        assert np.array_equal(np.argmax(got[t], 1), np.argmax(per_kernel[t], 1))
+        # greedy ids agree wherever the top two logits are not a near tie
+        top2 = np.sort(per_kernel[t], 1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 1e-2 * np.abs(per_kernel[t]).max()
+        assert np.array_equal(np.argmax(got[t], 1)[clear], np.argmax(per_kernel[t], 1)[clear])
 
 
 def test_persistent_state_continues_on_the_per_kernel_path(cuda):
@@ -85,6 +90,8 @@ def test_persistent_step_is_not_taken_outside_its_range(cuda):
     from swiftrwkv_b200 import _lib
     m, _ = _model(65)
     L = _lib.lib()
+    assert L.rwkv_x070_decode_path(m.h, 40) == 0     # the per-kernel graph by default
+    _lib.call("rwkv_x070_set_decode_path", m.h, 1)
     assert L.rwkv_x070_decode_path(m.h, 8) == 0      # exact-GEMV rows
     assert L.rwkv_x070_decode_path(m.h, 65) == 0     # beyond one 64-row tile
     assert L.rwkv_x070_decode_path(m.h, 40) == 1
