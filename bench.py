@@ -713,6 +713,65 @@ def wkv_prefill_line(torch, dev, args, peaks, flush_l2):
             "gpu_launches": pw.launches_per_step * args.steps, "_wl": pw}
 
 
+def config3_line(torch, dev, args, peaks):
+    """random-init x070 0.1B (L=12, C=768, H=12, vocab
+    65536) over a dense bf16 base with bf16 activations; a 1024-token prefill
+    (uniform ids) at batch 1, then 256 greedy decode steps.  Weights (0.19 GB)
+    exceed L2 only with the head; timed as the workload runs (no flush)."""
+    from swiftrwkv_b200.x070 import X070Backbone, X070Config
+    L, C, V, T, NEW = 12, 768, 65536, 1024, 256
+    m = X070Backbone(X070Config(L, C, V), max_rows=1, act="bf16", base="bf16").init_random(seed=SEED)
+    rng = np.random.default_rng(SEED + 3)
+    prompt = rng.integers(0, V, (1, T), dtype=np.int32)
+    dprompt = torch.from_numpy(prompt).to(dev)
+    st = torch.cuda.current_stream()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def prefill():
+        m.reset(1)
+        m.prefill(dprompt, logits=False)
+
+    def decode():
+        for _ in range(NEW):
+            m.step_greedy(1, None, use_graph=True)
+
+    for _ in range(max(args.warmup, 3)):
+        prefill()
+        decode()
+    torch.cuda.synchronize()
+    pf, dc = [], []
+    for _ in range(max(3, min(args.steps, 10))):
+        a, b, c = ev(), ev(), ev()
+        a.record(st)
+        prefill()
+        b.record(st)
+        decode()
+        c.record(st)
+        torch.cuda.synchronize()
+        pf.append(a.elapsed_time(b))
+        dc.append(b.elapsed_time(c))
+    pf_ms, dc_ms = statistics.median(pf), statistics.median(dc)
+    # end to end through generate (host prompt in, host tokens out, per-token sync)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    m.reset(1)
+    out = m.generateBatch(prompt, NEW)
+    e2e_s = time.perf_counter() - t0
+    H = C // 64
+    step_bytes = m.weight_bytes + L * H * 64 * 64 * 4 * 2 + L * C * 4 * 2 * 2
+    gbs = step_bytes / (dc_ms / NEW / 1e3) / 1e9
+    m.close()
+    return {"metric": "x070 0.1B bf16 (config 3): 1024-token prefill tok/s and greedy decode tok/s, batch 1",
+            "prefill_tok_s": T / (pf_ms / 1e3), "prefill_ms": pf_ms,
+            "decode_tok_s": NEW / (dc_ms / 1e3), "decode_ms_per_token": dc_ms / NEW,
+            "dtype": "bf16", "data": "synthetic (random init, uniform ids)",
+            "decode_roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                "frac": gbs / peaks["hbm_gbs"], "alg_bytes_per_token": step_bytes,
+                                "peak_src": peaks["src"]},
+            "e2e": {"value": (T + NEW) / e2e_s, "unit": "tok/s (prompt + generated, wall clock, generate API)",
+                    "tokens_out": int(out.size)}}
+
+
 def make_workload(args):
     if args.workload == "decode":
         return Decode15B(args.rows or 64, args.prompt)
@@ -819,6 +878,7 @@ def main():
                                  "prompt": wl.PROMPT, "base": "MLX affine 4-bit g64"})
     if wl.name == "decode" and world == 1:
         result["prefill"] = wkv_prefill_line(torch, dev, args, peaks, flush_l2)
+        result["config3"] = config3_line(torch, dev, args, peaks)
     if rank == 0 and world == 1:
         from oracle import oracle as O
         O.build()

@@ -87,6 +87,13 @@ def tiny_weights(cfg: Cfg, seed: int = 42, fan_in_scale: bool = False):
     return w
 
 
+def to_bf16(x):
+    """Round float32 values to bfloat16 (nearest, ties to even), as float32."""
+    u = np.ascontiguousarray(np.asarray(x, np.float32)).view(np.uint32)
+    r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return r.astype(np.uint32).view(np.float32)
+
+
 def splitmix_ids(B, T, vocab=64, seed=1):
     """TinyBackbone.ids: SplitMix64 stream, ids = next() % vocab, [B, T] int32."""
     mask = (1 << 64) - 1
@@ -117,9 +124,14 @@ class X070Oracle:
     GEMV_MAX_ROWS = 8
 
     def __init__(self, cfg: Cfg, weights: dict, act="f16", quant_bits=4, group=64):
+        """quant_bits 4: the big matrices in the 4-bit container (used
+        dequantised); quant_bits 0: a dense bf16 base.  The low-rank and
+        adapter matrices are stored fp16, or bf16 with a bf16 model (the
+        runtime's storage)."""
         self.cfg, self.act = cfg, act
         self.w = {}
         self.w16 = {}
+        lr_bf16 = act == "bf16" or (quant_bits == 0 and act != "f16")
         for k, v in weights.items():
             v = np.asarray(v, np.float32)
             if quant_bits and v.ndim == 2 and _is_quant(k):
@@ -128,8 +140,10 @@ class X070Oracle:
                 v = O.affine_dequant(wq, sc, bi, group, quant_bits)
                 if act == "f16" and k != "emb.weight":
                     self.w16[k] = v.astype(np.float16).astype(np.float64)
-            elif v.ndim == 2:          # dense low-rank branches: fp16 storage
-                v = v.astype(np.float16).astype(np.float32)
+            elif not quant_bits and v.ndim == 2 and _is_quant(k):
+                v = to_bf16(v)          # dense bf16 base
+            elif v.ndim == 2:          # dense low-rank branches: 16-bit storage
+                v = to_bf16(v) if lr_bf16 else v.astype(np.float16).astype(np.float32)
             self.w[k] = v.astype(np.float64)
 
     def new_state(self, rows):
@@ -142,6 +156,8 @@ class X070Oracle:
         """Round a matmul input to the activation dtype."""
         if self.act == "f16":
             return x.astype(np.float16).astype(np.float64)
+        if self.act == "bf16":
+            return to_bf16(x).astype(np.float64)
         return x.astype(np.float32).astype(np.float64)
 
     def _mm(self, x, key):

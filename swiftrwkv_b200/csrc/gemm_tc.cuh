@@ -129,9 +129,10 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     return d;
 }
 
-// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
-    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// kind::f16 instruction descriptor: D f32, A and B f16 (bf16 = true: both
+// bf16, format 1 in bits 7-9 and 10-12), both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16 = false) {
+    return (1u << 4) | (bf16 ? (1u << 7) | (1u << 10) : 0u) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]^T
@@ -260,8 +261,9 @@ constexpr int TC_SRING = 4;    // scale / bias prefetch ring (stages)
 constexpr int TC_MAX_SPLIT = 8;  // split-K CTAs of one tile form one cluster
 
 // Weight formats: TC_Q4 = MLX affine 4-bit group-64 codes (dequantised into
-// TMEM), TC_F16 = dense fp16 [OUT, IN] (read by the MMA straight from shared memory).
-enum : int { TC_Q4 = 0, TC_F16 = 1 };
+// TMEM), TC_F16 / TC_BF16 = dense fp16 / bf16 [OUT, IN] (read by the MMA
+// straight from shared memory; activations of the same type).
+enum : int { TC_Q4 = 0, TC_F16 = 1, TC_BF16 = 2 };
 
 struct alignas(64) TcJob {
     CUtensorMap wmap;  // TC_Q4: codes {IN/8, OUT} u32, box {8*GPS, 128}, swizzled;
@@ -315,8 +317,8 @@ struct TcCfg {
     static constexpr int RP = BN + 4;                     // split-K receive row pitch (floats): 16-byte rows, conflict-free
     static_assert(ST * STAGE >= (TC_BM + TC_MAX_SPLIT) * RP * 4, "split-K receive buffers reuse the stage buffers");
     static_assert(TOTAL <= 227 * 1024, "shared memory per CTA");
-    static_assert(FMT == TC_F16 || ST_A >= 1, "at least one A stage");
-    static_assert(FMT == TC_F16 || (CPR % QW == 0 && CPW >= 1 && CPW <= 2),
+    static_assert(FMT != TC_Q4 || ST_A >= 1, "at least one A stage");
+    static_assert(FMT != TC_Q4 || (CPR % QW == 0 && CPW >= 1 && CPW <= 2),
                   "a dequant warp's chunks lie in one group");
     static_assert(BN % (4 * QW) == 0, "accumulator columns per warp in units of 4");
 };
@@ -438,7 +440,7 @@ gemm_tc_kernel(const __grid_constant__ TcArgs args) {
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
-            constexpr uint32_t IDESC = tc::idesc_f16(TC_BM, BN);
+            constexpr uint32_t IDESC = tc::idesc_f16(TC_BM, BN, FMT == TC_BF16);
             for (int i = 0; i < (skip ? 0 : nst); i++) {
                 const int s = i % ST, a = i % ST_A;
                 if (!tc::mbar_wait(wfull + s, (i / ST) & 1, err) || !tc::mbar_wait(xfull + s, (i / ST) & 1, err) ||
@@ -705,7 +707,7 @@ struct TcPlan {
 inline bool tc_job_ok(int FMT, const GemvJob& j) {
     const bool common = j.OUT >= 1 && j.x_stride % 8 == 0 && ((uintptr_t)j.x & 15) == 0 &&
                         ((uintptr_t)j.w & 15) == 0;
-    if (FMT == TC_F16) return common && j.IN >= 8 && j.IN % 8 == 0;
+    if (FMT != TC_Q4) return common && j.IN >= 8 && j.IN % 8 == 0;
     return common && j.IN % 256 == 0 && j.IN >= 256 && j.scales && j.biases &&
            ((uintptr_t)j.scales & 7) == 0 && ((uintptr_t)j.biases & 7) == 0;
 }
@@ -718,10 +720,14 @@ inline bool tc_job_ok(int FMT, const GemvJob& j) {
 // the 1.5B decode step: 64 rows 2.11 -> 2.36 ms.)
 #define RWKV_TC_CONFIGS(FMT, X)                                                                 \
     switch (BN) {                                                                              \
-        case 16: return FMT == TC_Q4 ? X(TC_Q4, 16, 4, 6, 4, 512) : X(TC_F16, 16, 1, 8, 4, 512);  \
-        case 32: return FMT == TC_Q4 ? X(TC_Q4, 32, 4, 5, 4, 512) : X(TC_F16, 32, 1, 8, 4, 512);  \
-        case 64: return FMT == TC_Q4 ? X(TC_Q4, 64, 4, 4, 4, 512) : X(TC_F16, 64, 1, 8, 4, 512);  \
-        default: return FMT == TC_Q4 ? X(TC_Q4, 128, 2, 4, 4, 512) : X(TC_F16, 128, 1, 6, 4, 512); \
+        case 16: return FMT == TC_Q4 ? X(TC_Q4, 16, 4, 6, 4, 512) : FMT == TC_F16 ? X(TC_F16, 16, 1, 8, 4, 512)     \
+                                                                   : X(TC_BF16, 16, 1, 8, 4, 512);                   \
+        case 32: return FMT == TC_Q4 ? X(TC_Q4, 32, 4, 5, 4, 512) : FMT == TC_F16 ? X(TC_F16, 32, 1, 8, 4, 512)     \
+                                                                   : X(TC_BF16, 32, 1, 8, 4, 512);                   \
+        case 64: return FMT == TC_Q4 ? X(TC_Q4, 64, 4, 4, 4, 512) : FMT == TC_F16 ? X(TC_F16, 64, 1, 8, 4, 512)     \
+                                                                   : X(TC_BF16, 64, 1, 8, 4, 512);                   \
+        default: return FMT == TC_Q4 ? X(TC_Q4, 128, 2, 4, 4, 512) : FMT == TC_F16 ? X(TC_F16, 128, 1, 6, 4, 512)  \
+                                                                    : X(TC_BF16, 128, 1, 6, 4, 512);                 \
     }
 
 // How many (1, 1, S) clusters of this configuration the GPU holds at once
@@ -759,13 +765,14 @@ inline int tc_max_clusters(int FMT, int BN, int S) {
 #undef X_
 }
 
-inline int tc_gps(int FMT, int BN) { return FMT == TC_F16 ? 1 : BN <= 64 ? 4 : 2; }
+inline int tc_gps(int FMT, int BN) { return FMT != TC_Q4 ? 1 : BN <= 64 ? 4 : 2; }
 
 inline TcPlan plan_tc(int FMT, const GemvJobs& jobs, int njobs, int R, int sm_count) {
     TcPlan p{};
     // decode batches (R <= 256) and prefill token blocks (R up to 64 Ki rows,
     // 128-row n-blocks, no split-K once the n-blocks fill the GPU)
-    if (R <= 8 || R > 65536 || njobs < 1 || njobs > TC_JOBS) return p;
+    // (bf16 dense weights take it at any row count: no exact-GEMV numerics to keep)
+    if ((R <= 8 && FMT != TC_BF16) || R < 1 || R > 65536 || njobs < 1 || njobs > TC_JOBS) return p;
     for (int i = 0; i < njobs; i++)
         if (!tc_job_ok(FMT, jobs.j[i])) return p;
     p.BN = R <= 16 ? 16 : R <= 32 ? 32 : R <= 64 ? 64 : 128;
@@ -809,8 +816,8 @@ inline bool encode_tc_maps(int FMT, TcJob& t, const GemvJob& j, int R, int BN, i
         cuuint64_t strides[1] = {(cuuint64_t)j.IN * 2};
         cuuint32_t box[2] = {64, (cuuint32_t)TC_BM};
         cuuint32_t es[2] = {1, 1};
-        if (enc(&t.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)j.w, dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        if (enc(&t.wmap, FMT == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                (void*)j.w, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
     }
@@ -819,8 +826,8 @@ inline bool encode_tc_maps(int FMT, TcJob& t, const GemvJob& j, int R, int BN, i
         cuuint64_t strides[1] = {(cuuint64_t)j.x_stride * 2};
         cuuint32_t box[2] = {64, (cuuint32_t)BN};
         cuuint32_t es[2] = {1, 1};
-        if (enc(&t.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)j.x, dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        if (enc(&t.xmap, FMT == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                (void*)j.x, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
     }

@@ -70,7 +70,7 @@ enum Act : int {
     ACT_SIGMOID_BIAS = 5,  // sigmoid(v + bias)                  (a / v branches, up)
     ACT_SCALE = 6,         // alpha * v                          (LoRA adapter, down)
 };
-enum Out : int { OUT_F32 = 0, OUT_F16 = 1, OUT_ADD_F32 = 2 };
+enum Out : int { OUT_F32 = 0, OUT_F16 = 1, OUT_ADD_F32 = 2, OUT_BF16 = 3 };
 
 __device__ __forceinline__ void epilogue(const GemvJob& jb, int o, int n, float v) {
     switch (jb.act) {
@@ -87,6 +87,8 @@ __device__ __forceinline__ void epilogue(const GemvJob& jb, int o, int n, float 
         ((float*)jb.y)[idx] = v;
     else if (jb.out == OUT_F16)
         ((__half*)jb.y)[idx] = __float2half_rn(v);
+    else if (jb.out == OUT_BF16)
+        ((__nv_bfloat16*)jb.y)[idx] = __float2bfloat16_rn(v);
     else
         ((float*)jb.y)[idx] += v;
 }

@@ -33,6 +33,9 @@ int launch_wkv7_chunk_fwd(int, const void*, const void*, const void*, const void
 // buffers stay bounded whatever the prompt length.
 constexpr int PF_TOKENS = 8192;
 
+// weight formats of the runtime's matrices
+enum : int { WF_Q4 = 0, WF_F16 = 1, WF_BF16 = 2 };
+
 // -------------------------------------------------------- device init helpers
 
 __device__ __forceinline__ uint64_t splitmix(uint64_t z) {
@@ -43,7 +46,8 @@ __device__ __forceinline__ uint64_t splitmix(uint64_t z) {
 }
 
 // mode 0: uniform(lo, hi); mode 1: normal(0, lo); counter-based, seeded.
-__global__ void fill_f16_kernel(__half* out, int64_t n, int mode, float lo, float hi, uint64_t seed) {
+template <typename T>
+__global__ void fill_kernel(T* out, int64_t n, int mode, float lo, float hi, uint64_t seed) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const uint64_t z = splitmix(seed ^ splitmix((uint64_t)i));
         const float u1 = ((z >> 40) + 0.5f) * (1.0f / 16777216.0f);
@@ -54,21 +58,24 @@ __global__ void fill_f16_kernel(__half* out, int64_t n, int mode, float lo, floa
             const float u2 = (((z >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
             v = lo * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
         }
-        out[i] = __float2half_rn(v);
+        out[i] = from_f<T>(v);
     }
 }
 
-__global__ void f32_to_f16_kernel(const float* in, __half* out, int64_t n) {
+template <typename T>
+__global__ void f32_to_kernel(const float* in, T* out, int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = __float2half_rn(in[i]);
+        out[i] = from_f<T>(in[i]);
 }
 
 // ------------------------------------------------------------------- model
 
+// A base matrix: the MLX 4-bit group-64 container, or dense bf16 (`dense`).
 struct QMat {
     uint32_t* wq = nullptr;
     __half* sc = nullptr;
     __half* bi = nullptr;
+    __nv_bfloat16* dense = nullptr;
     __half2* sbr = nullptr;  // (scale, bias) repacked per 128-row block and 256-code stage (persistent step)
     int OUT = 0, IN = 0;
 };
@@ -116,7 +123,10 @@ struct X070 {
     rwkv_x070_config cfg{};
     int L, C, H, V, F, Rmax;
     int rw, ra, rv, rg, hid;  // low-rank sizes and hidden width
-    bool f16act;
+    bool f16act;   // 16-bit activations (fp16 or bf16): the tensor-core GEMM path
+    bool bf16act;  // bf16 activations (with the dense bf16 base)
+    bool dense;    // dense bf16 base instead of the 4-bit container
+    int base_wf, lr_wf;  // weight formats (WF_*) of the base and the low-rank / adapter matrices
     std::vector<void*> allocs;
     std::vector<LayerW> lw;
     QMat emb, head;
@@ -187,6 +197,11 @@ struct X070 {
         QMat q;
         q.OUT = OUT;
         q.IN = IN;
+        if (dense) {
+            q.dense = alloc<__nv_bfloat16>((size_t)OUT * IN);
+            weight_bytes += (int64_t)OUT * IN * 2;
+            return q;
+        }
         q.wq = alloc<uint32_t>((size_t)OUT * IN / 8);
         q.sc = alloc<__half>((size_t)OUT * IN / 64);
         q.bi = alloc<__half>((size_t)OUT * IN / 64);
@@ -202,7 +217,11 @@ struct X070 {
         L = c.n_layer; C = c.n_embd; H = C / c.head_size; V = c.vocab; F = c.ffn; Rmax = c.max_rows;
         rw = c.rank_w; ra = c.rank_a; rv = c.rank_v; rg = c.rank_g;
         hid = rw + ra + rv + rg;
-        f16act = c.act_dtype == RWKV_F16;
+        f16act = c.act_dtype == RWKV_F16 || c.act_dtype == RWKV_BF16;
+        bf16act = c.act_dtype == RWKV_BF16;
+        dense = c.quant_bits == 0;
+        base_wf = dense ? WF_BF16 : WF_Q4;
+        lr_wf = bf16act || (dense && !f16act) ? WF_BF16 : WF_F16;
         act_bytes = f16act ? 2 : 4;
         emb = qmat(V, C);
         head = qmat(V, C);
@@ -278,12 +297,21 @@ struct X070 {
     int upload_q(QMat& q, const float* host, int64_t n) {
         RWKV_REQUIRE(n == (int64_t)q.OUT * q.IN, RWKV_E_SHAPE, "matrix size %lld, expected %d x %d",
                      (long long)n, q.OUT, q.IN);
+        if (dense) {
+            float* t32 = nullptr;
+            if (cudaMalloc(&t32, n * 4) != cudaSuccess) return fail(RWKV_E_CUDA, "set_param: staging allocation failed");
+            cudaMemcpy(t32, host, n * 4, cudaMemcpyHostToDevice);
+            f32_to_kernel<__nv_bfloat16><<<1024, 256>>>(t32, q.dense, n);
+            cudaDeviceSynchronize();
+            cudaFree(t32);
+            return check_launch("f32_to_kernel");
+        }
         float* tmp = nullptr;
         __half* h16 = nullptr;
         if (cudaMalloc(&tmp, n * 4) != cudaSuccess || cudaMalloc(&h16, n * 2) != cudaSuccess)
             return fail(RWKV_E_CUDA, "set_param: staging allocation failed");
         cudaMemcpy(tmp, host, n * 4, cudaMemcpyHostToDevice);
-        f32_to_f16_kernel<<<1024, 256>>>(tmp, h16, n);
+        f32_to_kernel<__half><<<1024, 256>>>(tmp, h16, n);
         int rc = launch_q_quantize(RWKV_F16, h16, q.wq, q.sc, q.bi, q.OUT, q.IN, 64, 4, 0);
         cudaDeviceSynchronize();
         cudaFree(tmp);
@@ -296,10 +324,12 @@ struct X070 {
         float* tmp = nullptr;
         if (cudaMalloc(&tmp, n * 4) != cudaSuccess) return fail(RWKV_E_CUDA, "set_param: staging allocation failed");
         cudaMemcpy(tmp, host, n * 4, cudaMemcpyHostToDevice);
-        f32_to_f16_kernel<<<1024, 256>>>(tmp, dst, n);
+        // 16-bit storage in the low-rank format: fp16, or bf16 beside bf16 activations
+        if (lr_wf == WF_BF16) f32_to_kernel<__nv_bfloat16><<<1024, 256>>>(tmp, (__nv_bfloat16*)dst, n);
+        else f32_to_kernel<__half><<<1024, 256>>>(tmp, dst, n);
         cudaDeviceSynchronize();
         cudaFree(tmp);
-        return check_launch("f32_to_f16_kernel");
+        return check_launch("f32_to_kernel");
     }
     int upload_f(float* dst, int64_t expect, const float* host, int64_t n) {
         RWKV_REQUIRE(n == expect, RWKV_E_SHAPE, "vector size %lld, expected %lld", (long long)n, (long long)expect);
@@ -406,11 +436,19 @@ struct X070 {
         __half* h16 = nullptr;
         if (cudaMalloc(&h16, maxn * 2) != cudaSuccess) return fail(RWKV_E_CUDA, "init: staging allocation failed");
         uint64_t salt = 0;
+        // low-rank matrices in their storage format (fp16, or bf16 beside bf16 activations)
         auto fill = [&](__half* dst, int64_t n, int mode, float a, float b) {
-            fill_f16_kernel<<<2048, 256>>>(dst, n, mode, a, b, seed * 0x9E3779B97F4A7C15ull + (++salt));
+            const uint64_t sd = seed * 0x9E3779B97F4A7C15ull + (++salt);
+            if (lr_wf == WF_BF16) fill_kernel<__nv_bfloat16><<<2048, 256>>>((__nv_bfloat16*)dst, n, mode, a, b, sd);
+            else fill_kernel<__half><<<2048, 256>>>(dst, n, mode, a, b, sd);
         };
         auto qfill = [&](QMat& q, int mode, float a, float b) {
-            fill(h16, (int64_t)q.OUT * q.IN, mode, a, b);
+            const uint64_t sd = seed * 0x9E3779B97F4A7C15ull + (++salt);
+            if (dense) {
+                fill_kernel<__nv_bfloat16><<<2048, 256>>>(q.dense, (int64_t)q.OUT * q.IN, mode, a, b, sd);
+                return check_launch("fill_kernel");
+            }
+            fill_kernel<__half><<<2048, 256>>>(h16, (int64_t)q.OUT * q.IN, mode, a, b, sd);
             return launch_q_quantize(RWKV_F16, h16, q.wq, q.sc, q.bi, q.OUT, q.IN, 64, 4, 0);
         };
         const float s = 0.5f / sqrtf((float)C);
@@ -488,14 +526,18 @@ struct X070 {
         return pdl_check(e, name);
     }
 
+    // fmt 0: the base matrices (4-bit, or dense bf16); 1: the low-rank / adapter matrices
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
+        const int wf = fmt == 0 ? base_wf : lr_wf;
         if (f16act) {
-            const int tfmt = fmt == 0 ? TC_Q4 : TC_F16;
+            const int tfmt = wf == WF_Q4 ? TC_Q4 : wf == WF_F16 ? TC_F16 : TC_BF16;
             const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
             if (tp.ok) {
                 cudaError_t e = launch_tc(tfmt, jobs, nj, R, tp, gerr, gflag.host_dev, st, /*pdl=*/true);
                 return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm_tc: %s", cudaGetErrorString(e));
             }
+            if (wf == WF_BF16)
+                return fail(RWKV_E_UNSUPPORTED, "gemm: bf16 matrices take the tensor-core path only (16-byte rows)");
             GemmPlan p = plan_any(jobs, nj, R, sm_count);
             if (p.ws_floats > gws_floats || p.tickets > gtickets_n)
                 return fail(RWKV_E_WORKSPACE, "gemm: split-K plan exceeds the workspace");
@@ -507,20 +549,26 @@ struct X070 {
         int maxo = 0;
         for (int i = 0; i < nj; i++) maxo = std::max(maxo, jobs.j[i].OUT);
         dim3 grid((maxo + 7) / 8, nj, (R + 7) / 8);
-        if (fmt == 0) gemv_cc_kernel<0><<<grid, 256, 0, st>>>(jobs, R);
-        else gemv_cc_kernel<1><<<grid, 256, 0, st>>>(jobs, R);
+        if (wf == WF_Q4) gemv_cc_kernel<0><<<grid, 256, 0, st>>>(jobs, R);
+        else if (wf == WF_F16) gemv_cc_kernel<1><<<grid, 256, 0, st>>>(jobs, R);
+        else gemv_cc_kernel<2><<<grid, 256, 0, st>>>(jobs, R);
         return check_launch("gemv_cc_kernel");
     }
 
     // whether gemv() takes the tensor-core path for these jobs
     bool tc_path(int fmt, const GemvJobs& jobs, int nj, int R) const {
-        return f16act && plan_tc(fmt == 0 ? TC_Q4 : TC_F16, jobs, nj, R, sm_count).ok;
+        const int wf = fmt == 0 ? base_wf : lr_wf;
+        return f16act && plan_tc(wf == WF_Q4 ? TC_Q4 : wf == WF_F16 ? TC_F16 : TC_BF16, jobs, nj, R, sm_count).ok;
     }
+    // output type of an activation-typed GEMM result
+    int aout() const { return !f16act ? OUT_F32 : bf16act ? OUT_BF16 : OUT_F16; }
 
     static GemvJob qjob(const QMat& q, const void* x, int xs, int act, int out, void* y, int ys,
                         const float* bias = nullptr) {
         GemvJob j{};
-        j.w = q.wq; j.scales = q.sc; j.biases = q.bi; j.x = x; j.x_stride = xs;
+        if (q.dense) j.w = q.dense;
+        else j.w = q.wq;
+        j.scales = q.sc; j.biases = q.bi; j.x = x; j.x_stride = xs;
         j.OUT = q.OUT; j.IN = q.IN; j.act = act; j.out = out; j.y = y; j.y_stride = ys; j.bias = bias;
         return j;
     }
@@ -554,7 +602,7 @@ struct X070 {
             const Adapter& ad = *lj[i].ad;
             if (!ad.on()) continue;
             A* z = (A*)zbuf + (size_t)nd * zrows * LORA_MAX_RANK;
-            GemvJob d = hjob(ad.A, ad.rank_a, lj[i].IN, lj[i].x, lj[i].xs, ACT_SCALE, f16act ? OUT_F16 : OUT_F32, z,
+            GemvJob d = hjob(ad.A, ad.rank_a, lj[i].IN, lj[i].x, lj[i].xs, ACT_SCALE, aout(), z,
                              ad.rank_a);
             d.alpha = ad.scale;
             D.j[nd] = d;
@@ -574,12 +622,12 @@ struct X070 {
     template <typename A>
     int step_body(int R, cudaStream_t st) {
         const size_t RC = (size_t)R * C;
-        const int aout = f16act ? OUT_F16 : OUT_F32;
+        const int aout = this->aout();
         A* mixp = (A*)mix;
         A* hidp = (A*)hidden;
         int rc;
         if ((rc = pdl_check(launch_pdl(x070_embed_kernel, R, GLUE_T, 0, st, (const int32_t*)ids, (const uint32_t*)emb.wq,
-                                       (const __half*)emb.sc, (const __half*)emb.bi, (const __half*)nullptr,
+                                       (const __half*)emb.sc, (const __half*)emb.bi, (const __nv_bfloat16*)emb.dense,
                                        (const float*)ln0w, (const float*)ln0b, x, C, V), "x070_embed_kernel")))
             return rc;
         mark("embed");
@@ -742,7 +790,7 @@ struct X070 {
     }
     // Whether a step on R rows takes the persistent kernel.
     bool pk_eligible(int R) const {
-        return decode_path == 1 && f16act && R > 8 && R <= 64 && C % 256 == 0 && C <= 4 * pk::WT * 2 &&
+        return decode_path == 1 && f16act && !bf16act && !dense && R > 8 && R <= 64 && C % 256 == 0 && C <= 4 * pk::WT * 2 &&
                F % 256 == 0 && V % 128 == 0 && !any_adapter();
     }
     template <typename T>
@@ -1000,7 +1048,7 @@ struct X070 {
 
     int run_step(int R, cudaStream_t st) {
         if (pk_eligible(R)) return pk_step(R, st);
-        return f16act ? step_body<__half>(R, st) : step_body<float>(R, st);
+        return bf16act ? step_body<__nv_bfloat16>(R, st) : f16act ? step_body<__half>(R, st) : step_body<float>(R, st);
     }
 
     int graph_step(int R, cudaStream_t st) {
@@ -1203,11 +1251,11 @@ struct X070 {
     int prefill_block_body(const int32_t* prompt, int T, int rows, int p0, int Ts, cudaStream_t st) {
         const int N = rows * Ts;
         const size_t NC = (size_t)N * C;
-        const int aout = f16act ? OUT_F16 : OUT_F32;
+        const int aout = this->aout();
         A* mixp = (A*)pf_mix;
         A* hidp = (A*)pf_hidden;
         x070_pf_ids_kernel<<<(N + 255) / 256, 256, 0, st>>>(prompt, T, p0, Ts, rows, pf_ids);
-        x070_embed_kernel<<<N, GLUE_T, 0, st>>>(pf_ids, emb.wq, emb.sc, emb.bi, nullptr, ln0w, ln0b, pf_x, C, V);
+        x070_embed_kernel<<<N, GLUE_T, 0, st>>>(pf_ids, emb.wq, emb.sc, emb.bi, emb.dense, ln0w, ln0b, pf_x, C, V);
         int rc = check_launch("x070 prefill embed");
         if (rc) return rc;
         auto rows_launch = [&](auto&& f, const char* name) { return row_launch(f, name); };
@@ -1315,8 +1363,9 @@ struct X070 {
         if (int rc = ensure_prefill(rows * Ts, Ts, rows)) return rc;
         cudaMemcpyAsync(pf_len, lens.data(), rows * sizeof(int32_t), cudaMemcpyHostToDevice, st);
         for (int p0 = 0; p0 < maxlen; p0 += Ts) {
-            const int rc = f16act ? prefill_block_body<__half>(prompt, T, rows, p0, Ts, st)
-                                  : prefill_block_body<float>(prompt, T, rows, p0, Ts, st);
+            const int rc = bf16act ? prefill_block_body<__nv_bfloat16>(prompt, T, rows, p0, Ts, st)
+                           : f16act ? prefill_block_body<__half>(prompt, T, rows, p0, Ts, st)
+                                    : prefill_block_body<float>(prompt, T, rows, p0, Ts, st);
             if (rc) return rc;
         }
         // the head over the rows' hidden states, then greedy ids: the decode step's tail
@@ -1326,7 +1375,9 @@ struct X070 {
         if (rc) return rc;
         {
             const LoraJob lj[1] = {{&head_ad, lnout, C, C, V, logits, V}};
-            if ((rc = f16act ? lora_apply<__half>(lj, 1, rows, st) : lora_apply<float>(lj, 1, rows, st))) return rc;
+            if ((rc = bf16act ? lora_apply<__nv_bfloat16>(lj, 1, rows, st)
+                      : f16act ? lora_apply<__half>(lj, 1, rows, st) : lora_apply<float>(lj, 1, rows, st)))
+                return rc;
         }
         x070_argmax_kernel<<<dim3((V + ARGMAX_SLICE - 1) / ARGMAX_SLICE, rows), GLUE_T, 0, st>>>(logits, V, amax_keys);
         x070_argmax_finish_kernel<<<(rows + 127) / 128, 128, 0, st>>>(amax_keys, ids, rows);
@@ -1394,9 +1445,14 @@ int rwkv_x070_create(const rwkv_x070_config* cfg, rwkv_x070_t* out) {
     RWKV_REQUIRE(c.ffn % 64 == 0, RWKV_E_UNSUPPORTED, "rwkv_x070_create: ffn %d must be a multiple of 64", c.ffn);
     RWKV_REQUIRE(c.rank_w % 16 == 0 && c.rank_a % 16 == 0 && c.rank_v % 16 == 0 && c.rank_g % 16 == 0,
                  RWKV_E_UNSUPPORTED, "rwkv_x070_create: low-rank sizes must be multiples of 16");
-    RWKV_REQUIRE(c.quant_bits == 4 && c.quant_group == 64, RWKV_E_UNSUPPORTED,
-                 "rwkv_x070_create: the base must be 4-bit group-64");
-    RWKV_REQUIRE(c.act_dtype == RWKV_F16 || c.act_dtype == RWKV_F32, RWKV_E_DTYPE, "rwkv_x070_create: act dtype");
+    RWKV_REQUIRE((c.quant_bits == 4 && c.quant_group == 64) || c.quant_bits == 0, RWKV_E_UNSUPPORTED,
+                 "rwkv_x070_create: the base must be 4-bit group-64 (quant_bits 4) or dense bf16 (quant_bits 0)");
+    RWKV_REQUIRE(c.act_dtype == RWKV_F16 || c.act_dtype == RWKV_F32 || c.act_dtype == RWKV_BF16, RWKV_E_DTYPE,
+                 "rwkv_x070_create: act dtype");
+    // a tensor-core product takes both operands in one type: the 4-bit base is
+    // dequantised into fp16, the dense base is bf16
+    RWKV_REQUIRE(c.act_dtype == RWKV_F32 || (c.quant_bits == 4) == (c.act_dtype == RWKV_F16), RWKV_E_DTYPE,
+                 "rwkv_x070_create: fp16 activations go with the 4-bit base, bf16 with the dense bf16 base");
     X070* m = new X070(c);
     if (m->alloc_failed) {
         delete m;

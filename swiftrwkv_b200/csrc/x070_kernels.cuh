@@ -62,11 +62,11 @@ __device__ __forceinline__ void ln_regs(float v[GLUE_PER], int C, const float* _
 }
 
 // ids -> x = ln0(emb[id]).  Embedding in the 4-bit group-64 container
-// (emb_wq != NULL) or dense fp16.
+// (emb_wq != NULL) or dense bf16.
 __global__ void __launch_bounds__(GLUE_T)
 x070_embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ emb_wq,
                   const __half* __restrict__ emb_sc, const __half* __restrict__ emb_bi,
-                  const __half* __restrict__ emb_dense, const float* __restrict__ lnw,
+                  const __nv_bfloat16* __restrict__ emb_dense, const float* __restrict__ lnw,
                   const float* __restrict__ lnb, float* __restrict__ x, int C, int vocab) {
     pdl_wait();  // launched as a programmatic dependent: predecessor outputs first
     pdl_trigger();
@@ -86,7 +86,7 @@ x070_embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ 
                 const int64_t gi = (int64_t)id * (C / 64) + c / 64;
                 v[i] = q * __half2float(emb_sc[gi]) + __half2float(emb_bi[gi]);
             } else {
-                v[i] = __half2float(emb_dense[(int64_t)id * C + c]);
+                v[i] = __bfloat162float(emb_dense[(int64_t)id * C + c]);
             }
         }
     }
@@ -614,10 +614,18 @@ gemv_cc_kernel(const GemvJobs jobs, int R) {
             for (int n = 0; n < 8; n++)
                 if (n < Rz) acc[n] = fmaf(wv, x[(int64_t)n * jb.x_stride + c], acc[n]);
         }
-    } else {
+    } else if (FMT == 1) {
         const __half* W = (const __half*)jb.w + (int64_t)o * jb.IN;
         for (int c = lane; c < jb.IN; c += 32) {
             const float wv = __half2float(W[c]);
+#pragma unroll
+            for (int n = 0; n < 8; n++)
+                if (n < Rz) acc[n] = fmaf(wv, x[(int64_t)n * jb.x_stride + c], acc[n]);
+        }
+    } else {
+        const __nv_bfloat16* W = (const __nv_bfloat16*)jb.w + (int64_t)o * jb.IN;
+        for (int c = lane; c < jb.IN; c += 32) {
+            const float wv = __bfloat162float(W[c]);
 #pragma unroll
             for (int n = 0; n < 8; n++)
                 if (n < Rz) acc[n] = fmaf(wv, x[(int64_t)n * jb.x_stride + c], acc[n]);

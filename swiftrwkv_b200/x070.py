@@ -14,7 +14,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import F16, F32, call
+from ._lib import BF16, F16, F32, call
 
 
 def lora_ranks(D: int):
@@ -49,16 +49,22 @@ class _Cfg(ctypes.Structure):
 
 
 class X070Backbone:
-    """x070 model over a 4-bit group-64 QLoRA base, decoded recurrently.
+    """x070 model, decoded recurrently and prefilled in parallel.
 
-    act="f16" feeds the projections fp16 activations (tensor-core GEMVs);
-    act="f32" keeps activations fp32 end to end (the parity path)."""
+    base="q4": a 4-bit group-64 QLoRA base (LoRA.swift:28-91); act="f16"
+    feeds the projections fp16 activations (tensor-core GEMMs), act="f32"
+    keeps activations fp32 end to end (the parity path).
+    base="bf16": a dense bf16 base (the reference's bf16 model, BASELINE
+    config 3); act="bf16" (tensor-core GEMMs) or "f32"."""
 
-    def __init__(self, cfg: X070Config, max_rows: int = 1, act: str = "f16"):
+    def __init__(self, cfg: X070Config, max_rows: int = 1, act: str = "f16", base: str = "q4"):
         self.cfg = cfg
+        if base not in ("q4", "bf16"):
+            raise ValueError(f"base {base!r}: 'q4' or 'bf16'")
         r = lora_ranks(cfg.nEmbd)
+        adt = {"f16": F16, "f32": F32, "bf16": BF16}[act]
         c = _Cfg(cfg.nLayer, cfg.nEmbd, cfg.headSize, cfg.vocab, cfg.ffn, r["w"], r["a"], r["v"],
-                 r["g"], 4, 64, F16 if act == "f16" else F32, max_rows)
+                 r["g"], 4 if base == "q4" else 0, 64, adt, max_rows)
         h = ctypes.c_void_p()
         call("rwkv_x070_create", ctypes.byref(c), ctypes.byref(h))
         self.h = h
