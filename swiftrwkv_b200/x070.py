@@ -91,6 +91,30 @@ class X070Backbone:
                  a.size)
         return self
 
+    def load_rwkvq(self, path: str, weights: dict | None = None):
+        """The projection matrices, embedding and head found in a `.rwkvq`
+        file (swiftrwkv_b200.rwkvq; world names mapped as RwkvqNaming does),
+        dequantised on the GPU -- sb6 and sym by the reference's dequant
+        kernels' arithmetic (RwkvqDequant.swift) -- into this model's base:
+        rounded once into bf16 for the dense base (the reference's
+        dequantise-then-matmul path), re-quantised into the 4-bit container
+        otherwise (lossy: sb6 / sym are not 4-bit group 64).  Tensors without
+        an x070 name are skipped; `weights` (reference names) supplies the
+        rest of the model.  Returns the x070 names loaded."""
+        from .rwkvq import RwkvqFile, x070_key
+        f = RwkvqFile(path)
+        done = []
+        for wk in f.keys():
+            key = x070_key(wk) if f.naming == "world" else wk
+            if key is None:
+                continue
+            w = f.dequantize(wk, torch.float32).cpu().numpy()
+            call("rwkv_x070_set_param", self.h, key.encode(), w.ctypes.data_as(ctypes.c_void_p), w.size)
+            done.append(key)
+        if weights:
+            self.load(weights)
+        return done
+
     def init_random(self, seed: int = 0):
         """Device-side random init with the x070 recipe (X070Init.weights)."""
         call("rwkv_x070_init_random", self.h, ctypes.c_uint64(seed))
