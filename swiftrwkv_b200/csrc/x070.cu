@@ -157,6 +157,8 @@ struct X070 {
     // split-K partials and tickets of the tensor-core GEMMs
     float* gws = nullptr;
     int* gtickets = nullptr;
+    float* gws_side = nullptr;   // the same for launches on `side` (the low-rank branch)
+    int* gtickets_side = nullptr;
     int* gerr = nullptr;  // set by a tensor-core GEMM wait that gave up
     TcWaitFlag gflag;     // gerr and its mapped host record
     size_t gws_floats = 0, gtickets_n = 0;
@@ -267,6 +269,8 @@ struct X070 {
         gws = alloc<float>(gws_floats);
         gtickets = alloc<int>(gtickets_n + 1);
         gerr = gtickets + gtickets_n;
+        gws_side = alloc<float>(gws_floats);
+        gtickets_side = alloc<int>(gtickets_n);
         if (!alloc_failed && !gflag.init(gerr)) alloc_failed = true;
         cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking);
         cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
@@ -542,7 +546,11 @@ struct X070 {
             if (p.ws_floats > gws_floats || p.tickets > gtickets_n)
                 return fail(RWKV_E_WORKSPACE, "gemm: split-K plan exceeds the workspace");
             GemmArgs ga{};
-            ga.jobs = jobs; ga.njobs = nj; ga.R = R; ga.ws = gws; ga.tickets = gtickets;
+            // the side stream runs beside the main one: its own split-K workspace
+            const bool on_side = st == side;
+            ga.jobs = jobs; ga.njobs = nj; ga.R = R;
+            ga.ws = on_side ? gws_side : gws;
+            ga.tickets = on_side ? gtickets_side : gtickets;
             cudaError_t e = fmt == 0 ? launch_any<0>(ga, p, st, true) : launch_any<1>(ga, p, st, true);
             return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "gemm: %s", cudaGetErrorString(e));
         }
@@ -662,10 +670,9 @@ struct X070 {
             U.j[nu++] = hjob(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, g, C);
             if (l > 0) U.j[nu++] = hjob(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
             // the low-rank branch reads only tmix_in's mixes and writes only
-            // w/a/g/v': beside the r/k/v GEMM when neither needs the shared
-            // split-K workspace (the step profiler keeps one stream)
-            const bool fork = side && !profiling && tc_path(0, J, 3, R) && tc_path(1, D, nd, R) &&
-                              tc_path(1, U, nu, R);
+            // w/a/g/v': beside the r/k/v GEMM (launches on `side` have their
+            // own split-K workspace; the step profiler keeps one stream)
+            const bool fork = side && !profiling;
             cudaStream_t sb = fork ? side : st;
             if (fork) {
                 cudaEventRecord(ev_fork, st);

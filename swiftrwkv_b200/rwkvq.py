@@ -283,7 +283,7 @@ class RwkvqFile:
         from . import quant as Q
         t = self.tensor(key)
         dtype = dtype or torch.float32
-        dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        dev = lambda x: torch.from_numpy(np.array(x, copy=True)).cuda()
         if t["kind"] == "dense":
             d = t["dense"]
             dt = self.box.entries[f"{key}::dense"][0]
