@@ -352,9 +352,10 @@ class Decode15B:
     unit = "tok/s"
     L, C, V, PROMPT = 24, 2048, 65536, 128
 
-    def __init__(self, rows=64, prompt=128):
+    def __init__(self, rows=64, prompt=128, decode_path="launches"):
         self.rows = rows
         self.PROMPT = prompt
+        self.decode_path = decode_path
         self.metric = (f"x070 1.5B 4-bit decode tok/s (generateBatch greedy, {rows} rows/GPU, "
                        "fp16 activations)")
 
@@ -363,6 +364,7 @@ class Decode15B:
         self.torch = torch
         cfg = X070Config(self.L, self.C, self.V)
         self.m = X070Backbone(cfg, max_rows=self.rows, act="f16").init_random(seed=SEED)
+        self.m.set_decode_path(1 if self.decode_path == "persistent" else 0)
         self.stream = torch.cuda.Stream(device=dev)
         torch.cuda.set_stream(self.stream)
         rng = np.random.default_rng(SEED)
@@ -385,8 +387,7 @@ class Decode15B:
         self.dev_next = torch.zeros(self.rows, dtype=torch.int32, device=dev)
         self.h2d = self.rows * 4
         self.d2h = self.rows * 4
-        from swiftrwkv_b200 import _lib
-        self.persistent = bool(_lib.lib().rwkv_x070_decode_path(self.m.h, self.rows))
+        self.persistent = bool(self.m.decode_path(self.rows))
         if self.persistent:
             # one cooperative launch per step: the kernel is the whole step
             self.launches_per_step = 1
@@ -434,12 +435,17 @@ class Decode15B:
         the step: the persistent step kernel, or the 4-bit GEMM launches."""
         if self.persistent:
             # the step profiler times the kernel's phases (grid barrier to grid barrier)
-            ts = []
+            ts, ph = [], {}
             for _ in range(reps):
                 agg, seq = self.m.profile_step(self.rows)
                 if not seq:
                     raise RuntimeError("step profiler returned no phases")
                 ts.append(sum(t for _, t in seq))
+                for name, (c, t) in agg.items():
+                    pc, pt = ph.get(name, (0, 0.0))
+                    ph[name] = (pc + c, pt + t)
+            # per phase kind: phases per step and average microseconds per phase
+            self.phases = {k: {"per_step": c // reps, "avg_us": 1e3 * t / c} for k, (c, t) in ph.items()}
             return sum(ts) / len(ts)
         tot, n = 0.0, 0
         for _ in range(reps):
@@ -774,7 +780,7 @@ def config3_line(torch, dev, args, peaks):
 
 def make_workload(args):
     if args.workload == "decode":
-        return Decode15B(args.rows or 64, args.prompt)
+        return Decode15B(args.rows or 64, args.prompt, args.decode_path)
     if args.workload == "gemv":
         return GemvSuite(args.rows or 1)
     if args.workload == "statetune":
@@ -791,6 +797,9 @@ def main():
     ap.add_argument("--rows", type=int, default=None,
                     help="decode rows per GPU (default 64) / GEMV activation rows (default 1)")
     ap.add_argument("--prompt", type=int, default=128, help="decode prompt tokens per row")
+    ap.add_argument("--decode-path", default="launches", choices=["launches", "persistent"],
+                    help="decode: one graph of per-op launches (default) or the persistent one-launch step "
+                         "(9..64 rows, fp16 activations, 4-bit base)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -858,7 +867,8 @@ def main():
         "config": {"workload": wl.name, "l2": l2_note, "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "traffic": measured_traffic(wl),
+                     # the committed captures cover the per-op launches, not the persistent step
+                     "traffic": None if getattr(wl, "persistent", False) else measured_traffic(wl),
                      "peak_src": peaks["src"], "kernel": kernel, "kernel_ms": dom_ms},
         "step_roofline": {"alg_bytes": wl.alg_bytes, "achieved": step_gbs,
                           "frac": step_gbs / peaks["hbm_gbs"], "unit": "GB/s"},
@@ -872,7 +882,10 @@ def main():
                                  "rows_per_gpu": wl.B, "global_batch": wl.B * world,
                                  "parallelism": f"dp{world} (NCCL allreduce of state gradients)",
                                  "inputs": f"{wl.NSETS} distinct per-layer sets cycled over 32 layers"})
+    if getattr(wl, "phases", None):
+        result["roofline"]["phases"] = wl.phases
     if wl.name == "decode":
+        result["config"]["decode_path"] = "persistent" if wl.persistent else "launches"
         result["config"].update({"model": "x070 1.5B (L=24 C=2048 H=32 V=65536 FFN=8192)",
                                  "rows_per_gpu": wl.rows, "global_batch": wl.rows * world,
                                  "prompt": wl.PROMPT, "base": "MLX affine 4-bit g64"})

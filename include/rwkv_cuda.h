@@ -294,7 +294,7 @@ int rwkv_sym_rows(const int32_t* ids, int n_ids, const uint8_t* codes, const uin
 
 /* --------------------------------------------- x070 recurrent decode runtime
  * The host side of X070Backbone's decode over the kernels above, for a 4-bit
- * group-64 QLoRA base: embedding -> per layer (ln1, token shift, r/k/v
+ * group-64 QLoRA base or a dense bf16 base: embedding -> per layer (ln1, token shift, r/k/v
  * GEMVs, low-rank w/a/v/g branches, WKV step + tail, o GEMV, ln2, cmix
  * key/value GEMVs) -> ln_out -> head GEMV -> greedy argmax.  Each row of a
  * batch carries its own state; one step is captured into a CUDA graph per
@@ -309,8 +309,12 @@ typedef struct rwkv_x070* rwkv_x070_t;
 typedef struct {
     int n_layer, n_embd, head_size, vocab, ffn; /* X070Config (X070Backbone.swift:24-37) */
     int rank_w, rank_a, rank_v, rank_g;         /* low-rank sizes (X070Init.swift:46-52) */
-    int quant_bits, quant_group;                /* 4, 64 (LoRA.swift:28-91) */
-    int act_dtype;  /* RWKV_F16: fp16 activations, tensor-core GEMVs; RWKV_F32: fp32 path */
+    int quant_bits, quant_group;                /* 4, 64 (LoRA.swift:28-91); or 0: dense bf16 base */
+    /* 4-bit base: RWKV_F16 (fp16 activations, tensor-core GEMMs) or RWKV_F32;
+     * dense bf16 base: RWKV_BF16 (bf16 activations, tensor-core GEMMs) or
+     * RWKV_F32.  Other pairings return RWKV_E_DTYPE: a tensor-core product
+     * takes both operands in one type. */
+    int act_dtype;
     int max_rows;   /* rows (batch) the state and workspace are sized for */
 } rwkv_x070_config;
 

@@ -128,6 +128,17 @@ class X070Backbone:
     def launches_per_step(self) -> int:
         return int(_lib.lib().rwkv_x070_launches_per_step(self.h))
 
+    def set_decode_path(self, path: int):
+        """0: one captured graph of per-op launches per step (default);
+        1: the persistent one-launch step where it applies (9..64 rows, fp16
+        activations, 4-bit base), the per-op graph elsewhere."""
+        call("rwkv_x070_set_decode_path", self.h, int(path))
+        return self
+
+    def decode_path(self, rows: int) -> int:
+        """The path a step of `rows` rows takes now (0 or 1)."""
+        return int(_lib.lib().rwkv_x070_decode_path(self.h, rows))
+
     # ----------------------------------------------------------------- decode
     @staticmethod
     def _s():
