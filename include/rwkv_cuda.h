@@ -219,6 +219,31 @@ int rwkv_q_gemm_status(rwkv_stream_t stream);
  * device fault.  No counterpart in the reference. */
 int rwkv_q_gemm_inject_wait_error(int host_record, rwkv_stream_t stream);
 
+/* Projection backward through a frozen base: the VJP X070Backbone gives a
+ * base projection y = x W^T (baseMatmul, Sources/RWKVGen/X070Backbone.swift:
+ * 337-356: matmul(cotangent.asType(bf16), weight(bf16)), a bf16 result cast
+ * to the primal's type):
+ *     dX[n, i] = bf16( sum_o dY[n, o] * Wb[o, i] )     (fp32 accumulation)
+ * dY [rows, OUT] bf16 (the host casts the cotangent, as the reference does);
+ * dX [rows, IN] in dx_dtype F32 / BF16 / F16 (the bf16-rounded sum, widened
+ * or narrowed: F16 rounds twice, like the reference's asType); accumulate != 0
+ * adds into an F32 dX (gradients of one input summed over its projections).
+ * rwkv_gemm_dx: Wb a dense bf16 [OUT, IN] (a dense target, or a base
+ * dequantised to bf16 by rwkv_q_dequant / rwkv_sb6_dequant / rwkv_sym_dequant
+ * as the reference's rwkvqWeight does, X070Backbone.swift:669-672).
+ * rwkv_q_gemm_dx: Wb = bf16(float(q) * scale + bias) of the MLX affine 4-bit
+ * group-64 container (fp16 scales), dequantised inside the kernel; bitwise
+ * the same as rwkv_q_dequant to bf16 followed by rwkv_gemm_dx.
+ * IN % 128 == 0, OUT % 64 == 0, dY / W / wq 16-byte aligned.  tcgen05 tensor
+ * cores; shares rwkv_q_gemm's wait-error record (rwkv_q_gemm_status).  The
+ * reference's optional fp32 backward (rwkvqBackwardDType = .float32) is not
+ * provided. */
+int rwkv_gemm_dx(int dy_dtype, const void* dy, int w_dtype, const void* w, int dx_dtype, void* dx, int rows,
+                 int OUT, int IN, int accumulate, rwkv_stream_t stream);
+int rwkv_q_gemm_dx(int dy_dtype, const void* dy, const uint32_t* wq, const void* scales, const void* biases,
+                   int sdtype, int dx_dtype, void* dx, int rows, int OUT, int IN, int group, int bits,
+                   int accumulate, rwkv_stream_t stream);
+
 /* Dense W [OUT, IN] in odtype: float(q)*float(scale) + float(bias), one
  * rounding.  Replaces MLX `dequantized` as used at
  * Sources/RWKVGen/X070Backbone.swift:759-766 and RwkvqModelTests. */

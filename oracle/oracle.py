@@ -216,6 +216,20 @@ def affine_gemv(x, wq, scales, biases, group=64, bits=4, exact=False):
     return y
 
 
+def base_matmul_vjp(dy, W):
+    """The bf16 backward of a frozen base projection y = x W^T, restated from
+    X070Backbone.baseMatmul's VJP (Sources/RWKVGen/X070Backbone.swift:337-356):
+    matmul(dy.asType(bf16), W.asType(bf16)), a bf16 result.  dy [rows, OUT],
+    W [OUT, IN] (fp32 values; both rounded to bf16 here).  Returns
+    (dx, exact): dx the bf16-rounded sum widened to fp32, exact the float64
+    sum of the bf16 operands (a kernel's fp32 sum lies within fp32 rounding of
+    it, so its bf16 rounding equals dx except at near-ties)."""
+    dyb = bf16_bits_to_f32(f32_to_bf16_bits(dy)).astype(np.float64)
+    Wb = bf16_bits_to_f32(f32_to_bf16_bits(W)).astype(np.float64)
+    exact = dyb @ Wb
+    return bf16_bits_to_f32(f32_to_bf16_bits(exact.astype(np.float32))), exact
+
+
 # ------------------------------------------------------------------ .rwkvq sb6
 
 def sb6_dequant(qblk, qsqm, ddm, OUT, IN, xbits):

@@ -41,6 +41,8 @@ int launch_wkv7_bwd_seq(int, const void*, const void*, const void*, const void*,
 int launch_q_gemm(int, const void*, const uint32_t*, const void*, const void*, int, int, void*,
                   int, int, int, int, int, cudaStream_t);
 int q_gemm_status(cudaStream_t);
+int launch_gemm_dx_any(int, const void*, const void*, const uint32_t*, const void*, const void*, int, void*, int,
+                       int, int, int, cudaStream_t);
 int q_gemm_inject_wait_error(int, cudaStream_t);
 int launch_q_dequant(const uint32_t*, const void*, const void*, int, int, void*, const int32_t*,
                      int, int, int, int, int, cudaStream_t);
@@ -264,6 +266,44 @@ int rwkv_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* scale
     RWKV_REQUIRE(al16(x) && al16(wq), RWKV_E_UNSUPPORTED, "rwkv_q_gemm: x / wq not 16-byte aligned");
     return launch_q_gemm(xdtype, x, wq, scales, biases, sdtype, ydtype, y, rows, OUT, IN, group,
                          bits, (cudaStream_t)stream);
+}
+
+static int check_dx(int dy_dtype, const void* dy, int dx_dtype, void* dx, int rows, int OUT, int IN,
+                    int accumulate, const char* fn) {
+    RWKV_REQUIRE(dy && dx, RWKV_E_NULL, "%s: NULL argument", fn);
+    RWKV_REQUIRE(dy_dtype == RWKV_BF16, RWKV_E_DTYPE,
+                 "%s: dY dtype %d; the backward takes the cotangent in bf16 (cast it first)", fn, dy_dtype);
+    RWKV_REQUIRE(dx_dtype == RWKV_F32 || dx_dtype == RWKV_BF16 || dx_dtype == RWKV_F16, RWKV_E_DTYPE,
+                 "%s: dX dtype %d", fn, dx_dtype);
+    RWKV_REQUIRE(accumulate == 0 || dx_dtype == RWKV_F32, RWKV_E_DTYPE, "%s: accumulate needs an fp32 dX", fn);
+    RWKV_REQUIRE(rows >= 1 && OUT >= 1 && IN >= 1, RWKV_E_SHAPE, "%s: rows=%d OUT=%d IN=%d", fn, rows, OUT, IN);
+    RWKV_REQUIRE(IN % 128 == 0 && OUT % 64 == 0, RWKV_E_UNSUPPORTED,
+                 "%s: IN=%d must be a multiple of 128 and OUT=%d of 64", fn, IN, OUT);
+    RWKV_REQUIRE(al16(dy), RWKV_E_UNSUPPORTED, "%s: dY not 16-byte aligned", fn);
+    return RWKV_OK;
+}
+
+int rwkv_gemm_dx(int dy_dtype, const void* dy, int w_dtype, const void* w, int dx_dtype, void* dx, int rows,
+                 int OUT, int IN, int accumulate, rwkv_stream_t stream) {
+    if (int rc = check_dx(dy_dtype, dy, dx_dtype, dx, rows, OUT, IN, accumulate, "rwkv_gemm_dx")) return rc;
+    RWKV_REQUIRE(w, RWKV_E_NULL, "rwkv_gemm_dx: NULL weight");
+    RWKV_REQUIRE(w_dtype == RWKV_BF16, RWKV_E_DTYPE, "rwkv_gemm_dx: weight dtype %d (bf16 only)", w_dtype);
+    RWKV_REQUIRE(al16(w), RWKV_E_UNSUPPORTED, "rwkv_gemm_dx: weight not 16-byte aligned");
+    return launch_gemm_dx_any(DX_BF16, dy, w, nullptr, nullptr, nullptr, dx_dtype, dx, rows, OUT, IN, accumulate,
+                              (cudaStream_t)stream);
+}
+
+int rwkv_q_gemm_dx(int dy_dtype, const void* dy, const uint32_t* wq, const void* scales, const void* biases,
+                   int sdtype, int dx_dtype, void* dx, int rows, int OUT, int IN, int group, int bits,
+                   int accumulate, rwkv_stream_t stream) {
+    if (int rc = check_dx(dy_dtype, dy, dx_dtype, dx, rows, OUT, IN, accumulate, "rwkv_q_gemm_dx")) return rc;
+    RWKV_REQUIRE(wq && scales && biases, RWKV_E_NULL, "rwkv_q_gemm_dx: NULL weight buffer");
+    RWKV_REQUIRE(group == 64 && bits == 4 && sdtype == RWKV_F16, RWKV_E_UNSUPPORTED,
+                 "rwkv_q_gemm_dx: group=%d bits=%d scale dtype %d (4-bit group 64, fp16 scales)", group, bits,
+                 sdtype);
+    RWKV_REQUIRE(al16(wq), RWKV_E_UNSUPPORTED, "rwkv_q_gemm_dx: wq not 16-byte aligned");
+    return launch_gemm_dx_any(DX_Q4, dy, nullptr, wq, scales, biases, dx_dtype, dx, rows, OUT, IN, accumulate,
+                              (cudaStream_t)stream);
 }
 
 int rwkv_q_gemm_status(rwkv_stream_t stream) { return q_gemm_status((cudaStream_t)stream); }

@@ -136,4 +136,8 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// Base-weight formats of the projection backward (gemm_dx.cuh): dense bf16,
+// or the MLX affine 4-bit group-64 container dequantised on the fly.
+enum : int { DX_BF16 = 0, DX_Q4 = 1 };
+
 }  // namespace rwkv

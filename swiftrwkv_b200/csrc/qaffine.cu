@@ -17,6 +17,7 @@
 #include <mutex>
 #include <unordered_map>
 
+#include "gemm_dx.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_w4_wide.cuh"
 
@@ -394,6 +395,33 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
             });
         });
     });
+}
+
+// Projection backward dX = bf16(bf16(dY) W_bf16) (gemm_dx.cuh).  wfmt DX_BF16:
+// `w` dense bf16 [OUT, IN]; DX_Q4: the 4-bit group-64 container (fp16 scales).
+// Shares rwkv_q_gemm's wait-error record.  Arguments are checked by the caller.
+int launch_gemm_dx_any(int wfmt, const void* dy, const void* w, const uint32_t* wq, const void* scales,
+                       const void* biases, int dx_dtype, void* dx, int rows, int OUT, int IN, int accumulate,
+                       cudaStream_t st) {
+    GemmScratch* sc = gemm_scratch();
+    if (!sc) return fail(RWKV_E_CUDA, "rwkv_gemm_dx: workspace allocation failed");
+    if (sc->flag.take(st))
+        return fail(RWKV_E_TIMEOUT, "rwkv_gemm_dx: a tensor-core GEMM wait of an earlier call gave up; "
+                                    "its outputs are not valid (flag cleared, nothing launched)");
+    DxArgs a{};
+    a.scales = (const __half*)scales;
+    a.biases = (const __half*)biases;
+    a.dx = dx;
+    a.dx_dtype = dx_dtype;
+    a.accumulate = accumulate;
+    a.rows = rows;
+    a.OUT = OUT;
+    a.IN = IN;
+    a.err = sc->err;
+    a.err_host = sc->flag.host_dev;
+    cudaError_t e = launch_gemm_dx(wfmt, a, dy, w, wq, sc->sm_count, st);
+    if (e != cudaSuccess) return fail(RWKV_E_CUDA, "gemm_dx_kernel: %s", cudaGetErrorString(e));
+    return ok();
 }
 
 int q_gemm_status(cudaStream_t st) {

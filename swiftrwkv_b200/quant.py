@@ -2,7 +2,8 @@
 
 * MLX affine container (the QLoRA base): `quantized`, `dequantized`,
   `quantizedMM` with MLX's argument names (called at Sources/RWKVGen/
-  LoRA.swift:68 and X070Backbone.swift:678-681, 759-766), plus `QuantBase`.
+  LoRA.swift:68 and X070Backbone.swift:678-681, 759-766), plus `QuantBase`;
+  `baseMatmulVJP`, the bf16 backward of a frozen base projection.
 * .rwkvq sb6 / sym (Sources/RWKVQuant): `rwkvqDequantDense`, `rwkvqSb6GEMV`,
   `rwkvqDequantSym`, `rwkvqSymGEMV`, `symGEMVFused`, `RwkvqSymRowTable`,
   `nativeAffine`, with the reference's `...Applies` predicates.  GEMV entry
@@ -95,6 +96,39 @@ def quantizedMM(x, wq, scales, biases, transpose=True, groupSize=64, bits=4, out
     call("rwkv_q_gemm", _DT[x2.dtype], _p(x2), _p(wq), _p(scales), _p(biases), _DT[scales.dtype],
          _DT[ydt], _p(y), rows, OUT, IN, groupSize, bits, _s())
     return y.reshape(*lead, OUT)
+
+
+def baseMatmulVJP(cotangent, weight=None, q: QuantBase | None = None, primal_dtype=None, out=None):
+    """The backward of a frozen base projection y = x W^T, the VJP
+    X070Backbone gives baseMatmul (X070Backbone.swift:337-356, bf16 backward):
+    dX = matmul(cotangent.asType(bf16), W_bf16), a bf16 result cast to the
+    primal's dtype (`primal_dtype`, default the cotangent's).  `weight`: the
+    dense bf16 [OUT, IN] (a dense target, or a base dequantised to bf16);
+    `q`: the 4-bit group-64 container, dequantised inside the kernel.  With
+    `out` (an fp32 [..., IN] tensor) the result is added into it instead."""
+    if (weight is None) == (q is None):
+        raise ValueError("baseMatmulVJP: give exactly one of weight / q")
+    OUT = cotangent.shape[-1]
+    lead = cotangent.shape[:-1]
+    dy = cotangent.reshape(-1, OUT).to(torch.bfloat16).contiguous()
+    rows = dy.shape[0]
+    IN = weight.shape[1] if weight is not None else q.inFeatures
+    if out is not None:
+        if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != rows * IN:
+            raise ValueError("baseMatmulVJP: out must be a contiguous fp32 tensor of [..., IN]")
+        dx, acc = out, 1
+    else:
+        dt = primal_dtype or cotangent.dtype
+        if dt not in _DT:
+            dt = torch.float32
+        dx, acc = torch.empty((rows, IN), device=dy.device, dtype=dt), 0
+    if weight is not None:
+        w = weight.to(torch.bfloat16).contiguous()
+        call("rwkv_gemm_dx", BF16, _p(dy), BF16, _p(w), _DT[dx.dtype], _p(dx), rows, OUT, IN, acc, _s())
+    else:
+        call("rwkv_q_gemm_dx", BF16, _p(dy), _p(q.wq), _p(q.scales), _p(q.biases), _DT[q.scales.dtype],
+             _DT[dx.dtype], _p(dx), rows, OUT, IN, q.groupSize, q.bits, acc, _s())
+    return dx.reshape(*lead, IN)
 
 
 def quantized_rows(ids, q: QuantBase, dtype=torch.float16):

@@ -102,3 +102,25 @@ def test_wkv7_step_api_validates_shapes_before_any_launch():
         K.wkv7Steps(*(x3 for _ in range(6)))
     with pytest.raises(ValueError, match="every input"):
         K.wkv7Steps(torch.zeros(1, 3, 2, 64), *(torch.zeros(1, 2, 2, 64) for _ in range(5)))
+
+
+def test_projection_backward_validates_before_any_launch():
+    """rwkv_gemm_dx / rwkv_q_gemm_dx: bf16 cotangent only, fp32 dX for
+    accumulation, IN % 128 and OUT % 64, 4-bit group 64 with fp16 scales."""
+    s = _lib.status
+    F32, BF16, F16 = _lib.F32, _lib.BF16, _lib.F16
+    dense = lambda dyt=BF16, wt=BF16, dxt=F32, rows=16, OUT=256, IN=256, acc=0: s(
+        "rwkv_gemm_dx", dyt, FAKE, wt, FAKE, dxt, FAKE, rows, OUT, IN, acc, None)
+    assert dense(dyt=F32) == _lib.E_DTYPE          # the host casts the cotangent to bf16
+    assert dense(wt=F16) == _lib.E_DTYPE
+    assert dense(dxt=BF16, acc=1) == _lib.E_DTYPE  # accumulation into fp32 only
+    assert dense(dxt=9) == _lib.E_DTYPE
+    assert dense(rows=0) == _lib.E_SHAPE
+    assert dense(IN=200) == _lib.E_UNSUPPORTED
+    assert dense(OUT=96) == _lib.E_UNSUPPORTED
+    assert s("rwkv_gemm_dx", BF16, None, BF16, FAKE, F32, FAKE, 1, 64, 128, 0, None) == _lib.E_NULL
+    q = lambda group=64, bits=4, sdt=F16: s("rwkv_q_gemm_dx", BF16, FAKE, FAKE, FAKE, FAKE, sdt, F32, FAKE,
+                                          8, 256, 256, group, bits, 0, None)
+    assert q(group=32) == _lib.E_UNSUPPORTED
+    assert q(bits=8) == _lib.E_UNSUPPORTED
+    assert q(sdt=BF16) == _lib.E_UNSUPPORTED
