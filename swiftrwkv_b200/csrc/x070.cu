@@ -20,6 +20,7 @@
 #include "gemm_w4_wide.cuh"
 #include "x070_kernels.cuh"
 #include "x070_persist.cuh"
+#include "x070_small.cuh"
 
 namespace rwkv {
 
@@ -1053,13 +1054,209 @@ struct X070 {
         return RWKV_OK;
     }
 
+    // ----- persistent decode step for 1..8 rows (x070_small.cuh)
+
+    bool sp_eligible(int R) const {
+        return decode_path == 1 && f16act && !bf16act && !dense && R >= 1 && R <= 8 && C % 128 == 0 &&
+               C <= 4 * pk::WT * 2 && F % 128 == 0 && !any_adapter();
+    }
+    struct SpProgram {
+        int nphases = 0;
+        std::vector<std::string> names;
+        sp::Job* jobs = nullptr;
+        sp::Item* items = nullptr;
+        int* ofs = nullptr;
+        sp::Phase* phases = nullptr;
+        pk::Layer* layers = nullptr;
+    };
+    std::map<int, SpProgram> sp_progs;
+    int sp_occ = -1;
+
+    int sp_build(int R, SpProgram& P) {
+        const int G = sm_count;
+        std::vector<sp::Job> jobs;
+        std::vector<sp::Item> items;
+        std::vector<int> ofs;
+        std::vector<sp::Phase> phases;
+        std::vector<std::string> names;
+        auto named = [&](const char* n) { names.resize(phases.size() - 1); names.push_back(n); };
+        auto qj = [&](const QMat& q, const void* xx, int xs, int act, int out, void* y, int ys, const float* bias = nullptr) {
+            jobs.push_back({qjob(q, xx, xs, act, out, y, ys, bias), sp::FMT_Q4, 0});
+            return (int)jobs.size() - 1;
+        };
+        auto hj = [&](const __half* W, int OUT, int IN, const void* xx, int xs, int act, int out, void* y, int ys,
+                      const float* bias = nullptr) {
+            jobs.push_back({hjob(W, OUT, IN, xx, xs, act, out, y, ys, bias), sp::FMT_F16, 0});
+            return (int)jobs.size() - 1;
+        };
+        // A GEMV phase over jobs js: 16-row tiles, each cut along K into pieces
+        // (4-bit: 2048 codes, fp16: 512 columns); whole tiles go to CTAs in
+        // order so that every CTA gets about the same number of pieces.
+        auto gemv = [&](std::initializer_list<int> js, int layer, const char* name) {
+            struct Tile { int job, o0, np; };
+            std::vector<Tile> tiles;
+            int64_t T = 0;
+            for (int ji : js) {
+                const int KP = jobs[ji].fmt == sp::FMT_Q4 ? 2048 : 512;
+                const int np = (jobs[ji].g.IN + KP - 1) / KP;
+                for (int o0 = 0; o0 < jobs[ji].g.OUT; o0 += sp::TR) {
+                    tiles.push_back({ji, o0, np});
+                    T += np;
+                }
+            }
+            phases.push_back({pk::PH_GEMM, (int)ofs.size(), layer, 0});
+            named(name);
+            size_t ti = 0;
+            int64_t done = 0;
+            for (int c = 0; c < G; c++) {
+                ofs.push_back((int)items.size());
+                const int64_t until = T * (c + 1) / G;
+                while (ti < tiles.size() && done < until) {
+                    const Tile& t = tiles[ti++];
+                    const int KP = jobs[t.job].fmt == sp::FMT_Q4 ? 2048 : 512, IN = jobs[t.job].g.IN;
+                    for (int q = 0; q < t.np; q++) {
+                        const int k0 = q * KP;
+                        items.push_back({t.job, t.o0, k0, std::min(KP, IN - k0), q == t.np - 1, 0, 0, 0});
+                    }
+                    done += t.np;
+                }
+            }
+            ofs.push_back((int)items.size());
+        };
+        __half* mixp = (__half*)mix;
+        __half* hidp = (__half*)hidden;
+        const size_t RC = (size_t)R * C;
+        auto M = [&](int m) { return (const void*)(mixp + (size_t)m * RC); };
+        phases.push_back({pk::PH_EMBED, 0, -1, 0});
+        named("embed");
+        for (int l = 0; l < L; l++) {
+            LayerW& w = lw[l];
+            phases.push_back({pk::PH_TMIX, 0, l, 0});
+            named("tmix_in");
+            const int jr = qj(w.r, M(0), C, ACT_NONE, OUT_F32, r, C);
+            const int jk = qj(w.k, M(2), C, ACT_NONE, OUT_F32, k, C);
+            const int jv = qj(w.v, M(3), C, ACT_NONE, OUT_F32, v, C);
+            const int dw = hj(w.wA, rw, C, M(1), C, ACT_TANH, OUT_F16, hidp, hid);
+            const int da = hj(w.aA, ra, C, M(4), C, ACT_NONE, OUT_F16, hidp + rw, hid);
+            const int dg = hj(w.gA, rg, C, M(5), C, ACT_SIGMOID, OUT_F16, hidp + rw + ra, hid);
+            const int uw = hj(w.wB, C, rw, hidp, hid, ACT_DECAY, OUT_F32, wdec, C, w.wbias);
+            const int ua = hj(w.aB, C, ra, hidp + rw, hid, ACT_SIGMOID_BIAS, OUT_F32, a, C, w.abias);
+            const int ug = hj(w.gB, C, rg, hidp + rw + ra, hid, ACT_NONE, OUT_F32, g, C);
+            if (l > 0) {
+                const int dv = hj(w.vA, rv, C, M(3), C, ACT_NONE, OUT_F16, hidp + rw + ra + rg, hid);
+                const int uv = hj(w.vB, C, rv, hidp + rw + ra + rg, hid, ACT_SIGMOID_BIAS, OUT_F32, vv, C, w.vbias);
+                gemv({jr, jk, jv, dw, da, dg, dv}, l, "gemm_rkv_lowrank_down");
+                gemv({uw, ua, ug, uv}, l, "gemm_lowrank_up");
+            } else {
+                gemv({jr, jk, jv, dw, da, dg}, l, "gemm_rkv_lowrank_down");
+                gemv({uw, ua, ug}, l, "gemm_lowrank_up");
+            }
+            phases.push_back({pk::PH_WKV, 0, l, 0});
+            named("wkv_step_tail");
+            gemv({qj(w.o, tail, C, ACT_NONE, OUT_ADD_F32, x, C)}, l, "gemm_o");
+            phases.push_back({pk::PH_CMIX, 0, l, 0});
+            named("cmix_in");
+            gemv({qj(w.key, xk, C, ACT_RELU2, OUT_F16, ffn, F)}, l, "gemm_key");
+            gemv({qj(w.value, ffn, F, ACT_NONE, OUT_ADD_F32, x, C)}, l, "gemm_value");
+        }
+        phases.push_back({pk::PH_LNOUT, 0, -1, 0});
+        named("ln_out");
+        gemv({qj(head, lnout, C, ACT_NONE, OUT_F32, logits, V)}, -1, "gemm_head");
+        phases.push_back({pk::PH_ARGMAX, 0, -1, 0});
+        named("argmax");
+        phases.push_back({pk::PH_ARGFIN, 0, -1, 0});
+        named("argmax_finish");
+        if ((int)phases.size() > pk::MAX_PHASES)
+            return fail(RWKV_E_UNSUPPORTED, "small-row persistent step: %d phases, at most %d", (int)phases.size(),
+                        pk::MAX_PHASES);
+        std::vector<pk::Layer> layers(L);
+        for (int l = 0; l < L; l++) {
+            const LayerW& w = lw[l];
+            layers[l] = {w.ln1w, w.ln1b, w.ln2w, w.ln2b, w.coef6, w.kkw, w.kaw, w.rkw, w.lnxw, w.lnxb, w.cxk,
+                         wkv + (size_t)l * Rmax * H * 64 * 64, tshift + (size_t)l * Rmax * C, cshift + (size_t)l * Rmax * C};
+        }
+        P.names = names;
+        P.nphases = (int)phases.size();
+        P.jobs = pk_alloc<sp::Job>(jobs.size());
+        P.items = pk_alloc<sp::Item>(items.size());
+        P.ofs = pk_alloc<int>(ofs.size());
+        P.phases = pk_alloc<sp::Phase>(phases.size());
+        P.layers = pk_alloc<pk::Layer>(layers.size());
+        if (!P.jobs || !P.items || !P.ofs || !P.phases || !P.layers)
+            return fail(RWKV_E_CUDA, "small-row persistent step: program allocation failed");
+        cudaMemcpy(P.jobs, jobs.data(), jobs.size() * sizeof(sp::Job), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.items, items.data(), items.size() * sizeof(sp::Item), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.ofs, ofs.data(), ofs.size() * sizeof(int), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.phases, phases.data(), phases.size() * sizeof(sp::Phase), cudaMemcpyHostToDevice);
+        cudaMemcpy(P.layers, layers.data(), layers.size() * sizeof(pk::Layer), cudaMemcpyHostToDevice);
+        return check_launch("small-row persistent step: program upload");
+    }
+
+    int sp_step(int R, cudaStream_t st) {
+        const size_t bar_words = 32;
+        if (!pk_bar && !(pk_bar = pk_alloc<unsigned int>(bar_words)))
+            return fail(RWKV_E_CUDA, "small-row persistent step: allocation failed");
+        auto it = sp_progs.find(R);
+        if (it == sp_progs.end()) {
+            SpProgram P;
+            if (int rc = sp_build(R, P)) return rc;
+            it = sp_progs.emplace(R, P).first;
+        }
+        const SpProgram& P = it->second;
+        auto kern = sp::x070_small_kernel<2>;
+        if (sp_occ < 0) {
+            int n = 0;
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sp::SMEM);
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, sp::THREADS, sp::SMEM) != cudaSuccess) n = 0;
+            cudaGetLastError();
+            sp_occ = n;
+        }
+        if (sp_occ < 1) return fail(RWKV_E_UNSUPPORTED, "small-row persistent step: the kernel does not fit on an SM");
+        sp::Args sa{};
+        pk::Args& a = sa.g;
+        a.layers = P.layers;
+        a.nphases = P.nphases; a.R = R; a.C = C; a.H = H; a.V = V;
+        a.x = x; a.r = r; a.k = k; a.v = v; a.wdec = wdec; a.a = this->a; a.g = g; a.vv = vv; a.vfirst = vfirst;
+        a.logits = logits;
+        a.mix = (__half*)mix; a.tail = (__half*)tail; a.xk = (__half*)xk; a.lnout = (__half*)lnout;
+        a.ids = ids; a.amax_keys = amax_keys;
+        a.emb_wq = emb.wq; a.emb_sc = emb.sc; a.emb_bi = emb.bi;
+        a.ln0w = ln0w; a.ln0b = ln0b; a.lnow = lnow; a.lnob = lnob;
+        a.bar = pk_bar; a.err = gerr; a.err_host = gflag.host_dev;
+        if (profiling) {
+            if (!pk_trace && !(pk_trace = pk_alloc<unsigned long long>(pk::T_END)))
+                return fail(RWKV_E_CUDA, "small-row persistent step: trace allocation failed");
+            if (P.nphases + 1 > 1024) return fail(RWKV_E_UNSUPPORTED, "small-row persistent step: too many phases to trace");
+            a.trace = pk_trace;
+        }
+        sa.jobs = P.jobs; sa.items = P.items; sa.ofs = P.ofs; sa.phases = P.phases; sa.nphases = P.nphases;
+        cudaMemsetAsync(pk_bar, 0, bar_words * sizeof(unsigned int), st);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(sm_count);
+        cfg.blockDim = dim3(sp::THREADS);
+        cfg.dynamicSmemBytes = sp::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once (grid barriers)
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, sa);
+        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "x070_small_kernel: %s", cudaGetErrorString(e));
+        return RWKV_OK;
+    }
+
+    // Whether a step on R rows is one persistent launch, and that launch.
+    bool persist_eligible(int R) const { return pk_eligible(R) || sp_eligible(R); }
+    int persist_step(int R, cudaStream_t st) { return sp_eligible(R) ? sp_step(R, st) : pk_step(R, st); }
+
     int run_step(int R, cudaStream_t st) {
-        if (pk_eligible(R)) return pk_step(R, st);
+        if (persist_eligible(R)) return persist_step(R, st);
         return bf16act ? step_body<__nv_bfloat16>(R, st) : f16act ? step_body<__half>(R, st) : step_body<float>(R, st);
     }
 
     int graph_step(int R, cudaStream_t st) {
-        if (pk_eligible(R)) return run_step(R, st);  // one launch per step: nothing to capture
+        if (persist_eligible(R)) return run_step(R, st);  // one launch per step: nothing to capture
         auto it = graphs.find(R);
         if (it == graphs.end()) {
             cudaGraph_t gph;
@@ -1085,7 +1282,7 @@ struct X070 {
     // replayed once: device-side per-launch milliseconds into ms[] (up to
     // cap) and their names, '\n'-separated.
     int profile_step(int R, cudaStream_t st, float* ms, int cap, char* names, int names_cap, int* count) {
-        if (pk_eligible(R)) return profile_persistent(R, st, ms, cap, names, names_cap, count);
+        if (persist_eligible(R)) return profile_persistent(R, st, ms, cap, names, names_cap, count);
         cudaStream_t cs = st ? st : own;
         if (!st) {
             cudaEventRecord(ev_in, st);
@@ -1147,21 +1344,23 @@ struct X070 {
     int profile_persistent(int R, cudaStream_t st, float* ms, int cap, char* names, int names_cap, int* count) {
         profiling = true;
         prof_names.clear();
-        int rc = pk_step(R, st);
+        int rc = persist_step(R, st);
         profiling = false;
         prof_names.clear();
         if (rc) return rc;
         if (cudaStreamSynchronize(st) != cudaSuccess) return fail(RWKV_E_CUDA, "profile: persistent step failed");
-        const PkProgram& P = pk_progs.at(R);
+        const bool small = sp_eligible(R);
+        const int nph = small ? sp_progs.at(R).nphases : pk_progs.at(R).nphases;
+        const std::vector<std::string>& pnames = small ? sp_progs.at(R).names : pk_progs.at(R).names;
         pk_last_trace.resize(pk::T_END);
         cudaMemcpy(pk_last_trace.data(), pk_trace, pk::T_END * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
-        std::vector<unsigned long long> t(P.nphases + 1);
+        std::vector<unsigned long long> t(nph + 1);
         cudaMemcpy(t.data(), pk_trace, t.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
         std::string all;
         int n = 0;
-        for (int p = 0; p < P.nphases; p++) {
+        for (int p = 0; p < nph; p++) {
             if (n < cap) ms[n++] = (float)((t[p + 1] - t[p]) * 1e-6);
-            all += P.names[p];
+            all += pnames[p];
             all += "\n";
         }
         *count = n;
@@ -1641,7 +1840,7 @@ int rwkv_x070_trace(rwkv_x070_t h, uint64_t* out_host, int cap, int* count) {
 }
 
 int rwkv_x070_decode_path(rwkv_x070_t h, int rows) {
-    return h && reinterpret_cast<X070*>(h)->pk_eligible(rows) ? 1 : 0;
+    return h && reinterpret_cast<X070*>(h)->persist_eligible(rows) ? 1 : 0;
 }
 
 int64_t rwkv_x070_weight_bytes(rwkv_x070_t h) { return h ? reinterpret_cast<X070*>(h)->weight_bytes : 0; }

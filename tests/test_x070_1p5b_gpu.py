@@ -114,10 +114,12 @@ def test_1p5b_width_prefill_matches_oracle(model16, oracle16):
     assert rel_err(cont.cpu().numpy(), want) < 2e-3, rel_err(cont.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("rows", [16, 32, 64])
+@pytest.mark.parametrize("rows", [1, 8, 16, 32, 64])
 def test_1p5b_width_persistent_step(model16, oracle16, rows):
     """The persistent decode step (rwkv_x070_set_decode_path 1) at the 1.5B
-    width, at each of its tile widths (16, 32, 64 rows)."""
+    width: the 1..8-row kernel (exact-code GEMVs, the 8192-wide value matrix
+    in two staged activation windows) and the 9..64-row kernel at each of its
+    tile widths (16, 32, 64 rows)."""
     from oracle import x070_oracle as XO
     from swiftrwkv_b200 import _lib
     _lib.call("rwkv_x070_set_decode_path", model16.h, 1)

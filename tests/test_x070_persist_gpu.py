@@ -1,14 +1,16 @@
-"""The persistent decode step (one cooperative launch per step, 9..64 rows,
-fp16 activations) against the decode oracle and against the per-kernel step.
+"""The persistent decode steps (one cooperative launch per step: the 1..8-row
+kernel with exact-code GEMVs and the 9..64-row tcgen05 kernel, fp16
+activations) against the decode oracle and against the per-kernel step.
 
-Both paths compute the projections with the fp16-dequantised weight (the
-tcgen05 arithmetic above 8 rows), which the oracle models; they group the
-split-K sums differently, so they agree to fp32 rounding carried through fp16
+Each persistent kernel computes the projections with the per-kernel path's
+arithmetic for its row count (up to 8 rows the exact dequantised weight,
+above 8 the fp16-dequantised weight), which the oracle models; the sums are
+grouped differently, so they agree to fp32 rounding carried through fp16
 activations, not bitwise.  Checked: logits within 2e-3 of the oracle over
-several steps (tiny width, and the 1.5B width at 16/32/64 rows -- the three
-tile widths), greedy ids equal to the per-kernel path's where the top two
-logits are not a near tie, and the state the
-persistent steps leave behind continues correctly on the per-kernel path.
+several steps (tiny width; the 1.5B width is in test_x070_1p5b_gpu.py),
+greedy ids equal to the per-kernel path's where the top two logits are not a
+near tie, and the state the persistent steps leave behind continues
+correctly on the per-kernel path.
 """
 from __future__ import annotations
 
@@ -42,7 +44,7 @@ def _steps(m, ids, path):
     return [o.cpu().numpy() for o in out]
 
 
-@pytest.mark.parametrize("rows", [9, 20, 64])
+@pytest.mark.parametrize("rows", [1, 3, 8, 9, 20, 64])
 def test_persistent_step_matches_oracle(cuda, rows):
     from oracle import x070_oracle as XO
     from swiftrwkv_b200 import _lib
@@ -91,8 +93,10 @@ def test_persistent_step_is_not_taken_outside_its_range(cuda):
     m, _ = _model(65)
     L = _lib.lib()
     assert L.rwkv_x070_decode_path(m.h, 40) == 0     # the per-kernel graph by default
+    assert L.rwkv_x070_decode_path(m.h, 1) == 0
     _lib.call("rwkv_x070_set_decode_path", m.h, 1)
-    assert L.rwkv_x070_decode_path(m.h, 8) == 0      # exact-GEMV rows
+    assert L.rwkv_x070_decode_path(m.h, 1) == 1      # the 1..8-row kernel
+    assert L.rwkv_x070_decode_path(m.h, 8) == 1
     assert L.rwkv_x070_decode_path(m.h, 65) == 0     # beyond one 64-row tile
     assert L.rwkv_x070_decode_path(m.h, 40) == 1
     _lib.call("rwkv_x070_set_decode_path", m.h, 0)
