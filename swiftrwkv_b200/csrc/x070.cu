@@ -78,6 +78,7 @@ struct QMat {
     __half* bi = nullptr;
     __nv_bfloat16* dense = nullptr;
     __half2* sbr = nullptr;  // (scale, bias) repacked per 128-row block and 256-code stage (persistent step)
+    __half* sbs = nullptr;   // (scale, bias) blocks per 16-row tile and 2048-code piece (1..8-row persistent step)
     int OUT = 0, IN = 0;
 };
 
@@ -1070,7 +1071,31 @@ struct X070 {
         pk::Layer* layers = nullptr;
     };
     std::map<int, SpProgram> sp_progs;
-    int sp_occ = -1;
+    int sp_occ[4] = {-1, -1, -1, -1};
+    int64_t sp_wver = -1;
+
+    // The (scale, bias) blocks of every 4-bit matrix, refreshed after weight changes.
+    int sp_repack(cudaStream_t st) {
+        if (sp_wver == wver) return RWKV_OK;
+        std::vector<QMat*> qs = {&head};
+        for (LayerW& w : lw) {
+            QMat* m[6] = {&w.r, &w.k, &w.v, &w.o, &w.key, &w.value};
+            for (QMat* q : m) qs.push_back(q);
+        }
+        for (QMat* q : qs) {
+            const size_t n = (size_t)ceil_div(q->OUT, sp::TR) * ceil_div(q->IN, sp::KPQ) * (sp::SBB / 2);
+            if (!q->sbs && !(q->sbs = pk_alloc<__half>(n)))
+                return fail(RWKV_E_CUDA, "small-row persistent step: scale repack allocation failed");
+            x070_repack_sb_small_kernel_launch(q, st);
+        }
+        sp_wver = wver;
+        return check_launch("x070_repack_sb_small_kernel");
+    }
+    void x070_repack_sb_small_kernel_launch(QMat* q, cudaStream_t st) {
+        const int64_t n = (int64_t)ceil_div(q->OUT, sp::TR) * ceil_div(q->IN, sp::KPQ) * (sp::SBB / 2);
+        sp::x070_repack_sb_small_kernel<<<(int)std::min<int64_t>(ceil_div(n, 256), 8 * sm_count), 256, 0, st>>>(
+            q->sc, q->bi, q->sbs, q->OUT, q->IN);
+    }
 
     int sp_build(int R, SpProgram& P) {
         const int G = sm_count;
@@ -1081,12 +1106,12 @@ struct X070 {
         std::vector<std::string> names;
         auto named = [&](const char* n) { names.resize(phases.size() - 1); names.push_back(n); };
         auto qj = [&](const QMat& q, const void* xx, int xs, int act, int out, void* y, int ys, const float* bias = nullptr) {
-            jobs.push_back({qjob(q, xx, xs, act, out, y, ys, bias), sp::FMT_Q4, 0});
+            jobs.push_back({qjob(q, xx, xs, act, out, y, ys, bias), q.sbs, sp::FMT_Q4, ceil_div(q.IN, sp::KPQ)});
             return (int)jobs.size() - 1;
         };
         auto hj = [&](const __half* W, int OUT, int IN, const void* xx, int xs, int act, int out, void* y, int ys,
                       const float* bias = nullptr) {
-            jobs.push_back({hjob(W, OUT, IN, xx, xs, act, out, y, ys, bias), sp::FMT_F16, 0});
+            jobs.push_back({hjob(W, OUT, IN, xx, xs, act, out, y, ys, bias), nullptr, sp::FMT_F16, ceil_div(IN, sp::KPH)});
             return (int)jobs.size() - 1;
         };
         // A GEMV phase over jobs js: 16-row tiles, each cut along K into pieces
@@ -1097,7 +1122,7 @@ struct X070 {
             std::vector<Tile> tiles;
             int64_t T = 0;
             for (int ji : js) {
-                const int KP = jobs[ji].fmt == sp::FMT_Q4 ? 2048 : 512;
+                const int KP = jobs[ji].fmt == sp::FMT_Q4 ? sp::KPQ : sp::KPH;
                 const int np = (jobs[ji].g.IN + KP - 1) / KP;
                 for (int o0 = 0; o0 < jobs[ji].g.OUT; o0 += sp::TR) {
                     tiles.push_back({ji, o0, np});
@@ -1113,7 +1138,7 @@ struct X070 {
                 const int64_t until = T * (c + 1) / G;
                 while (ti < tiles.size() && done < until) {
                     const Tile& t = tiles[ti++];
-                    const int KP = jobs[t.job].fmt == sp::FMT_Q4 ? 2048 : 512, IN = jobs[t.job].g.IN;
+                    const int KP = jobs[t.job].fmt == sp::FMT_Q4 ? sp::KPQ : sp::KPH, IN = jobs[t.job].g.IN;
                     for (int q = 0; q < t.np; q++) {
                         const int k0 = q * KP;
                         items.push_back({t.job, t.o0, k0, std::min(KP, IN - k0), q == t.np - 1, 0, 0, 0});
@@ -1192,7 +1217,36 @@ struct X070 {
         return check_launch("small-row persistent step: program upload");
     }
 
+    template <int RB>
+    int sp_launch(const sp::Args& sa, cudaStream_t st) {
+        auto kern = sp::x070_small_kernel<2, RB>;
+        constexpr int SM = sp::Cfg<RB>::SMEM;
+        const int ri = RB == 1 ? 0 : RB == 2 ? 1 : RB == 4 ? 2 : 3;
+        if (sp_occ[ri] < 0) {
+            int n = 0;
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM);
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, sp::THREADS, SM) != cudaSuccess) n = 0;
+            cudaGetLastError();
+            sp_occ[ri] = n;
+        }
+        if (sp_occ[ri] < 1) return fail(RWKV_E_UNSUPPORTED, "small-row persistent step: the kernel does not fit on an SM");
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(sm_count);
+        cfg.blockDim = dim3(sp::THREADS);
+        cfg.dynamicSmemBytes = SM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once (grid barriers)
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, sa);
+        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "x070_small_kernel: %s", cudaGetErrorString(e));
+        return RWKV_OK;
+    }
+
     int sp_step(int R, cudaStream_t st) {
+        if (int rc = sp_repack(st)) return rc;
         const size_t bar_words = 32;
         if (!pk_bar && !(pk_bar = pk_alloc<unsigned int>(bar_words)))
             return fail(RWKV_E_CUDA, "small-row persistent step: allocation failed");
@@ -1203,15 +1257,6 @@ struct X070 {
             it = sp_progs.emplace(R, P).first;
         }
         const SpProgram& P = it->second;
-        auto kern = sp::x070_small_kernel<2>;
-        if (sp_occ < 0) {
-            int n = 0;
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sp::SMEM);
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, sp::THREADS, sp::SMEM) != cudaSuccess) n = 0;
-            cudaGetLastError();
-            sp_occ = n;
-        }
-        if (sp_occ < 1) return fail(RWKV_E_UNSUPPORTED, "small-row persistent step: the kernel does not fit on an SM");
         sp::Args sa{};
         pk::Args& a = sa.g;
         a.layers = P.layers;
@@ -1231,19 +1276,8 @@ struct X070 {
         }
         sa.jobs = P.jobs; sa.items = P.items; sa.ofs = P.ofs; sa.phases = P.phases; sa.nphases = P.nphases;
         cudaMemsetAsync(pk_bar, 0, bar_words * sizeof(unsigned int), st);
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(sm_count);
-        cfg.blockDim = dim3(sp::THREADS);
-        cfg.dynamicSmemBytes = sp::SMEM;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once (grid barriers)
-        attr[0].val.cooperative = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, sa);
-        if (e != cudaSuccess) return fail(RWKV_E_CUDA, "x070_small_kernel: %s", cudaGetErrorString(e));
-        return RWKV_OK;
+        return R <= 1 ? sp_launch<1>(sa, st) : R <= 2 ? sp_launch<2>(sa, st) : R <= 4 ? sp_launch<4>(sa, st)
+                                                                            : sp_launch<8>(sa, st);
     }
 
     // Whether a step on R rows is one persistent launch, and that launch.

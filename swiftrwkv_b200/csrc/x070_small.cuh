@@ -38,33 +38,42 @@ namespace sp {
 
 constexpr int THREADS = pk::THREADS;          // 320: producer warp, idle warp, 8 worker warps
 constexpr int WT = pk::WT;                    // 256 worker threads
-constexpr int RB = 8;                         // activation rows of the MMA tile (n = 8)
 constexpr int TR = 16;                        // weight rows per tile
+constexpr int KPQ = 2048, KPH = 512;          // K per piece: 4-bit codes / fp16 columns
 constexpr int WROWB = 1056;                   // slot row pitch: 2048 codes or 512 fp16 + 32 B
-constexpr int SB_OFF = TR * WROWB;            // per slot: scales [16][32], biases [16][32] (fp16)
-constexpr int SLOT = SB_OFF + 2 * TR * 32 * 2;  // 18944 B
-constexpr int NS = 7;                         // ring slots
+constexpr int SBB = 2 * TR * 32 * 2;          // a piece's (scale, bias) block: [2][16][32] fp16
+constexpr int SB_OFF = TR * WROWB;
+constexpr int SLOT = SB_OFF + SBB;            // 18944 B
 constexpr int KW = 4096;                      // activation window (columns) staged at a time
 constexpr int XROW = KW + 8;                  // staged activation row pitch (fp16)
-constexpr int W_OFF = 0;
-constexpr int X_OFF = W_OFF + NS * SLOT;
-constexpr int G_OFF = X_OFF + RB * XROW * 2;
-constexpr int RED_OFF = G_OFF + pk::GLUE_SMEM;          // warp partials [8][16][8] fp32
-constexpr int P_OFF = RED_OFF + 8 * TR * RB * 4;
-constexpr int B_OFF = P_OFF + pk::MAX_PHASES * 16;
-constexpr int NBAR = 2 * NS;
-constexpr int T_OFF = B_OFF + NBAR * 8;
-constexpr int SMEM = T_OFF + 32;
-static_assert(SLOT % 16 == 0 && X_OFF % 16 == 0 && G_OFF % 16 == 0 && B_OFF % 8 == 0, "alignment");
-static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+
+// Shared-memory layout for RB staged activation rows (RB >= the step's rows):
+// the weight ring takes what the activation window leaves.
+template <int RB>
+struct Cfg {
+    static constexpr int X_OFF = 0;
+    static constexpr int G_OFF = X_OFF + RB * XROW * 2;
+    static constexpr int RED_OFF = G_OFF + pk::GLUE_SMEM;       // warp partials [8][16][8] fp32
+    static constexpr int P_OFF = RED_OFF + 8 * TR * 8 * 4;
+    static constexpr int T_OFF = P_OFF + pk::MAX_PHASES * 16;
+    static constexpr int W_OFF = (T_OFF + 32 + 127) & ~127;
+    static constexpr int NS = (227 * 1024 - W_OFF - 16 * 8 - 128) / SLOT;  // ring slots
+    static constexpr int B_OFF = W_OFF + NS * SLOT;
+    static constexpr int SMEM = B_OFF + 2 * NS * 8;
+    static_assert(NS >= 4 && SMEM <= 227 * 1024, "shared memory per CTA");
+    static_assert(G_OFF % 16 == 0 && W_OFF % 128 == 0 && SLOT % 128 == 0, "alignment");
+};
 
 enum : int { FMT_Q4 = 0, FMT_F16 = 1 };
 
-// One matrix of a GEMV phase: the runtime's job (weights, activations, epilogue).
+// One matrix of a GEMV phase: the runtime's job (weights, activations,
+// epilogue); 4-bit: sbp = its (scale, bias) blocks, one SBB-byte block per
+// (16-row tile, piece), in that order (x070_repack_sb_small_kernel).
 struct Job {
     GemvJob g;
+    const __half* sbp;
     int fmt;
-    int pad;
+    int np;  // pieces per tile
 };
 
 // A piece: rows [o0, o0 + 16) of job `job`, K columns [k0, k0 + kn); `last`:
@@ -90,29 +99,21 @@ struct Args {
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-template <int BYTES>
-__device__ __forceinline__ void cp_async(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], %2;" ::"r"(dst), "l"(src), "n"(BYTES) : "memory");
-}
-template <>
-__device__ __forceinline__ void cp_async<4>(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-// The arrive-on of barrier `bar` fires once this thread's earlier cp.async
-// copies have landed (the barrier's count includes this arrival).
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(saddr(bar)) : "memory");
+// 16-byte-multiple global -> shared copy counted on mbarrier `bar` (tx bytes).
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(saddr(bar))
+                 : "memory");
 }
 
-
-// ---- producer (warp 0): this CTA's pieces of every GEMV phase, in program
-// order, each into ring slot seq % NS once the workers have released it.  Lane
-// l copies every 32nd 16-byte chunk (4-bit: codes, and the rows' scale / bias
-// pairs in 4-byte chunks); the slot's mbarrier counts the 32 lanes' arrivals,
-// each fired when that lane's copies have landed.
-__device__ void produce(const Args& A, const Phase* phs, unsigned char* smem, uint64_t* full, uint64_t* empty,
+// ---- producer (one thread of warp 0): this CTA's pieces of every GEMV phase,
+// in program order, each into ring slot seq % NS once the workers have
+// released it: one bulk copy per weight row (the row's K range of the piece)
+// and, for 4-bit pieces, one for the piece's (scale, bias) block.
+template <int NS>
+__device__ void produce(const Args& A, const Phase* phs, unsigned char* ring, uint64_t* full, uint64_t* empty,
                         int* err, bool& ok) {
-    const int lane = threadIdx.x & 31, G = gridDim.x, cta = blockIdx.x;
+    const int G = gridDim.x, cta = blockIdx.x;
     int seq = 0;
     for (int p = 0; p < A.nphases && ok; p++) {
         const Phase ph = phs[p];
@@ -127,65 +128,74 @@ __device__ void produce(const Args& A, const Phase* phs, unsigned char* smem, ui
                 ok = false;
                 break;
             }
-            const uint32_t dst = saddr(smem + W_OFF + s * SLOT);
+            const uint32_t dst = saddr(ring + s * SLOT);
             const int nr = min(TR, jb.g.OUT - it.o0);
-            if (jb.fmt == FMT_Q4) {
-                const int cpr = it.kn / 32;  // 16-byte chunks of codes per row
-                const char* w = (const char*)jb.g.w + ((int64_t)it.o0 * jb.g.IN + it.k0) / 2;
-                for (int e = lane; e < nr * cpr; e += 32) {
-                    const int r = e / cpr, c = e - r * cpr;
-                    cp_async<16>(dst + r * WROWB + 16 * c, w + (int64_t)r * (jb.g.IN / 2) + 16 * c);
-                }
-                const int NG = jb.g.IN / 64, spr = it.kn / 128;  // 4-byte (two-group) chunks per row
-                for (int e = lane; e < nr * spr; e += 32) {
-                    const int r = e / spr, c = e - r * spr;
-                    const int64_t so = (int64_t)(it.o0 + r) * NG + it.k0 / 64 + 2 * c;
-                    cp_async<4>(dst + SB_OFF + r * 64 + 4 * c, jb.g.scales + so);
-                    cp_async<4>(dst + SB_OFF + TR * 64 + r * 64 + 4 * c, jb.g.biases + so);
-                }
-            } else {
-                const int cpr = it.kn / 8;  // 16-byte chunks of fp16 per row
-                const __half* w = (const __half*)jb.g.w + (int64_t)it.o0 * jb.g.IN + it.k0;
-                for (int e = lane; e < nr * cpr; e += 32) {
-                    const int r = e / cpr, c = e - r * cpr;
-                    cp_async<16>(dst + r * WROWB + 16 * c, w + (int64_t)r * jb.g.IN + 8 * c);
-                }
-            }
-            cp_async_arrive(full + s);
+            const bool q4 = jb.fmt == FMT_Q4;
+            const uint32_t rowb = q4 ? it.kn / 2 : it.kn * 2;
+            tc::mbar_expect_tx(full + s, nr * rowb + (q4 ? SBB : 0));
+            const char* w = q4 ? (const char*)jb.g.w + ((int64_t)it.o0 * jb.g.IN + it.k0) / 2
+                               : (const char*)jb.g.w + ((int64_t)it.o0 * jb.g.IN + it.k0) * 2;
+            const int64_t pitch = q4 ? jb.g.IN / 2 : (int64_t)jb.g.IN * 2;
+            for (int r = 0; r < nr; r++) bulk_copy(dst + r * WROWB, w + r * pitch, rowb, full + s);
+            if (q4) bulk_copy(dst + SB_OFF, jb.sbp + ((size_t)(it.o0 / TR) * jb.np + it.k0 / KPQ) * (SBB / 2), SBB, full + s);
         }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    // every copy issued here lands before the CTA may exit
+    for (int q = max(0, seq - NS); q < seq; q++)
+        if (!tc::mbar_wait_own(full + (q % NS), (q / NS) & 1, err)) ok = false;
+}
+
+// (scale, bias) of a 4-bit group-64 matrix [OUT, IN/64] into one SBB-byte
+// block per (16-row tile, 2048-column piece), tile-major: [2][16][32] fp16
+// (scales, then biases; rows past OUT and groups past IN are zero).
+__global__ void x070_repack_sb_small_kernel(const __half* __restrict__ sc, const __half* __restrict__ bi,
+                                            __half* __restrict__ out, int OUT, int IN) {
+    constexpr int BH = SBB / 2;  // halves per block
+    const int np = (IN + KPQ - 1) / KPQ, nt = (OUT + TR - 1) / TR, NG = IN / 64;
+    const int64_t n = (int64_t)nt * np * BH;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t blk = e / BH;
+        const int within = (int)(e - blk * BH);
+        const int tile = (int)(blk / np), piece = (int)(blk - (int64_t)tile * np);
+        const int hb = within / (TR * 32), rr = (within / 32) % TR, gi = within % 32;
+        const int o = tile * TR + rr, gg = piece * (KPQ / 64) + gi;
+        __half v = __ushort_as_half(0);
+        if (o < OUT && gg < NG) v = (hb ? bi : sc)[(int64_t)o * NG + gg];
+        out[e] = v;
+    }
 }
 
 // ---- activations: rows 0..R-1 of the job's x, columns [k0, k0 + KW) (clipped
-// to IN), into the staged window xs[8][XROW] (fp16); rows R..7 and columns past
-// IN are zero.  All 256 workers; the caller brackets it with worker barriers.
+// to IN, zero past IN up to whole 64-column groups), into the staged window
+// xs[R][XROW] (fp16).  All 256 workers; the caller brackets it with worker
+// barriers.
 __device__ void stage_x(const GemvJob& g, int R, int k0, __half* xs, int wt) {
     const int kn = min(KW, g.IN - k0);
     const int kpad = (kn + 63) & ~63;  // whole 64-column groups are read
     const int cpr = kpad / 8;          // 16-byte chunks per row
-    for (int e = wt; e < RB * cpr; e += WT) {
+    for (int e = wt; e < R * cpr; e += WT) {
         const int n = e / cpr, c = e - n * cpr;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (n < R && 8 * c < kn) v = *reinterpret_cast<const uint4*>((const __half*)g.x + (int64_t)n * g.x_stride + k0 + 8 * c);
+        if (8 * c < kn) v = *reinterpret_cast<const uint4*>((const __half*)g.x + (int64_t)n * g.x_stride + k0 + 8 * c);
         *reinterpret_cast<uint4*>(xs + n * XROW + 8 * c) = v;
     }
 }
 
-
 // ---- one piece on the worker warps: warp w (0..7) accumulates its share of
 // the piece's K into acc (rows g, g+8 of the 16-row tile x activation rows 2t,
 // 2t+1: the m16n8k16 accumulator fragment).  slot: the piece's weights;
-// xs: the staged activations, whose column 0 is K column xk0.
-__device__ __forceinline__ void piece_q4(const unsigned char* slot, const __half* xs, int kx, int kn, int w,
+// xs: the staged activations (R rows; the MMA's columns R..7 read row R-1
+// and are discarded), whose column 0 is K column xk0.
+__device__ __forceinline__ void piece_q4(const unsigned char* slot, const __half* xs, int kx, int kn, int R, int w,
                                          int lane, float (&acc)[4]) {
     const int g = lane >> 2, t = lane & 3;
     const int ngr = kn / 64, ga = ngr * w / 8, gb = ngr * (w + 1) / 8;
     const __half* sc = reinterpret_cast<const __half*>(slot + SB_OFF);
     const __half* bi = sc + TR * 32;
+#pragma unroll 4
     for (int gi = ga; gi < gb; gi++) {
         // B fragments (nibble-pair order) and the group sums of activation rows 2t, 2t+1
-        const __half* xr = xs + g * XROW + kx + 64 * gi;
+        const __half* xr = xs + min(g, R - 1) * XROW + kx + 64 * gi;
         const uint4 lo = *reinterpret_cast<const uint4*>(xr + 16 * t);
         const uint4 hi = *reinterpret_cast<const uint4*>(xr + 16 * t + 8);
         const uint32_t h[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
@@ -228,13 +238,14 @@ __device__ __forceinline__ void piece_q4(const unsigned char* slot, const __half
     }
 }
 
-__device__ __forceinline__ void piece_f16(const unsigned char* slot, const __half* xs, int kx, int kn, int w,
+__device__ __forceinline__ void piece_f16(const unsigned char* slot, const __half* xs, int kx, int kn, int R, int w,
                                           int lane, float (&acc)[4]) {
     const int g = lane >> 2, t = lane & 3;
     const int nks = kn / 16, ka = nks * w / 8, kb = nks * (w + 1) / 8;
     const __half* w0 = reinterpret_cast<const __half*>(slot + g * WROWB) + 2 * t;
     const __half* w1 = reinterpret_cast<const __half*>(slot + (g + 8) * WROWB) + 2 * t;
-    const __half* xr = xs + g * XROW + kx + 2 * t;
+    const __half* xr = xs + min(g, R - 1) * XROW + kx + 2 * t;
+#pragma unroll 4
     for (int ks = ka; ks < kb; ks++) {
         const int c = 16 * ks;
         const uint32_t a[4] = {*reinterpret_cast<const uint32_t*>(w0 + c), *reinterpret_cast<const uint32_t*>(w1 + c),
@@ -263,32 +274,35 @@ __device__ __forceinline__ bool grid_sync(unsigned int* bar, unsigned int gen, i
 __device__ __forceinline__ void tile_out(const GemvJob& g, int o0, int R, float* red, const float (&acc)[4], int w,
                                          int lane, int wt, bool ok) {
     const int gq = lane >> 2, t = lane & 3;
-    float* mine = red + w * TR * RB;
-    mine[gq * RB + 2 * t] = acc[0];
-    mine[gq * RB + 2 * t + 1] = acc[1];
-    mine[(gq + 8) * RB + 2 * t] = acc[2];
-    mine[(gq + 8) * RB + 2 * t + 1] = acc[3];
+    float* mine = red + w * TR * 8;
+    mine[gq * 8 + 2 * t] = acc[0];
+    mine[gq * 8 + 2 * t + 1] = acc[1];
+    mine[(gq + 8) * 8 + 2 * t] = acc[2];
+    mine[(gq + 8) * 8 + 2 * t + 1] = acc[3];
     pk::wbar(1, WT);
-    if (ok && wt < TR * RB) {
-        const int r = wt / RB, n = wt - r * RB;
+    if (ok && wt < TR * 8) {
+        const int r = wt / 8, n = wt - r * 8;
         float v = 0.f;
 #pragma unroll
-        for (int q = 0; q < 8; q++) v += red[q * TR * RB + wt];
+        for (int q = 0; q < 8; q++) v += red[q * TR * 8 + wt];
         if (n < R && o0 + r < g.OUT) epilogue(g, o0 + r, n, v);
     }
     pk::wbar(1, WT);
 }
 
-template <int GV>
+template <int GV, int RB>
 __global__ void __launch_bounds__(THREADS, 1) x070_small_kernel(const __grid_constant__ Args S) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + B_OFF);
+    using C = Cfg<RB>;
+    constexpr int NS = C::NS;
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::B_OFF);
     uint64_t* empty = full + NS;
-    Phase* phs = reinterpret_cast<Phase*>(smem + P_OFF);
-    int* flag = reinterpret_cast<int*>(smem + T_OFF);
-    float* glue = reinterpret_cast<float*>(smem + G_OFF);
-    float* red = reinterpret_cast<float*>(smem + RED_OFF);
-    __half* xs = reinterpret_cast<__half*>(smem + X_OFF);
+    Phase* phs = reinterpret_cast<Phase*>(smem + C::P_OFF);
+    int* flag = reinterpret_cast<int*>(smem + C::T_OFF);
+    float* glue = reinterpret_cast<float*>(smem + C::G_OFF);
+    float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
+    __half* xs = reinterpret_cast<__half*>(smem + C::X_OFF);
+    unsigned char* ring = smem + C::W_OFF;
     const pk::Args& A = S.g;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -297,7 +311,7 @@ __global__ void __launch_bounds__(THREADS, 1) x070_small_kernel(const __grid_con
     for (int p = tid; p < S.nphases; p += THREADS) phs[p] = S.phases[p];
     if (tid == 0) {
         for (int s = 0; s < NS; s++) {
-            tc::mbar_init(full + s, 32);   // the producer lanes' cp.async arrivals
+            tc::mbar_init(full + s, 1);    // the producer's expect_tx arrival (+ the copies' bytes)
             tc::mbar_init(empty + s, 8);   // one arrival per worker warp
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -307,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1) x070_small_kernel(const __grid_con
     bool ok = flag[1] != 0;  // a wait of an earlier launch gave up: skip the program
 
     if (warp == 0) {
-        if (ok) produce(S, phs, smem, full, empty, err, ok);
+        if (ok && lane == 0) produce<NS>(S, phs, ring, full, empty, err, ok);
     } else if (warp >= 2) {
         const int wt = tid - 64, w = warp - 2;
         float* sh = glue + 2 * 12 * 64;  // reduction scratch of the glue phases
@@ -389,9 +403,9 @@ __global__ void __launch_bounds__(THREADS, 1) x070_small_kernel(const __grid_con
                     const int s = seq % NS;
                     if (ok && !tc::mbar_wait(full + s, (seq / NS) & 1, err)) ok = false;
                     if (ok) {
-                        const unsigned char* slot = smem + W_OFF + s * SLOT;
-                        if (jb.fmt == FMT_Q4) piece_q4(slot, xs, it.k0 - xk0, it.kn, w, lane, acc);
-                        else piece_f16(slot, xs, it.k0 - xk0, it.kn, w, lane, acc);
+                        const unsigned char* slot = ring + s * SLOT;
+                        if (jb.fmt == FMT_Q4) piece_q4(slot, xs, it.k0 - xk0, it.kn, R, w, lane, acc);
+                        else piece_f16(slot, xs, it.k0 - xk0, it.kn, R, w, lane, acc);
                     }
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(empty + s);
