@@ -616,8 +616,84 @@ def cpu_threads(cores):
     return {"openmp": cores, "blas": int(os.environ.get("OPENBLAS_NUM_THREADS", BLAS_THREADS))}
 
 
+class ProjBackward29B:
+    """The frozen-base projection backward dX = bf16(bf16(dY) W_bf16) (the
+    bf16 VJP of X070Backbone.baseMatmul, X070Backbone.swift:337-356) over one
+    layer of config 5's frozen bf16 2.9B base at 4096 tokens per GPU: the four
+    C x C projections (r, k, v, o), key (4C x C) and value (C x 4C), through
+    rwkv_gemm_dx.  Tensor-bound: the roofline is the measured bf16 peak."""
+    name = "dx"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    C, TOK = 2560, 4096
+
+    def __init__(self):
+        self.metric = ("projection backward TFLOP/s (config 5: frozen bf16 2.9B base, one layer's dX = dY W "
+                       "for r/k/v/o, key, value at 4096 tokens, tcgen05)")
+
+    def setup(self, torch, dev):
+        from swiftrwkv_b200 import _lib
+        self.torch, self._lib = torch, _lib
+        C, F, T = self.C, 4 * self.C, self.TOK
+        self.shapes = [(C, C)] * 4 + [(F, C), (C, F)]  # (OUT, IN) of the forward projection
+        g = torch.Generator(device="cpu").manual_seed(SEED)
+        self.mats = []
+        for OUT, IN in self.shapes:
+            W = (torch.randn((OUT, IN), generator=g) * 0.02).to(torch.bfloat16).to(dev)
+            dy = torch.randn((T, OUT), generator=g).to(torch.bfloat16).to(dev)
+            dx = torch.empty((T, IN), device=dev, dtype=torch.float32)
+            self.mats.append((OUT, IN, W, dy, dx))
+        fl = lambda OUT, IN: 2.0 * T * OUT * IN
+        self.flops = sum(fl(o, i) for o, i in self.shapes)
+        self.alg_bytes = sum(o * i * 2 + T * o * 2 + T * i * 4 for o, i in self.shapes)
+        self.units_per_step = self.flops / 1e12
+        self.launches_per_step = len(self.shapes)
+        self.dom_flops = fl(*self.shapes[4])  # the key matrix's backward
+        self.kernel = "gemm_dx_kernel<DX_BF16, 256> (tcgen05, A = W^T MN-major via TMA), 4096 x 10240 -> 2560"
+        self.h2d = sum(T * o * 2 for o, _ in self.shapes)
+        self.d2h = sum(T * i * 4 for _, i in self.shapes)
+        self.pin_dy = [torch.empty((T, o), dtype=torch.bfloat16).pin_memory() for o, _ in self.shapes]
+        self.pin_dx = [torch.empty((T, i), dtype=torch.float32).pin_memory() for _, i in self.shapes]
+
+    def _dx(self, OUT, IN, W, dy, dx):
+        _lib, P = self._lib, self._lib.P
+        st = P(self.torch.cuda.current_stream().cuda_stream)
+        _lib.call("rwkv_gemm_dx", 1, P(dy.data_ptr()), 1, P(W.data_ptr()), 0, P(dx.data_ptr()), self.TOK, OUT, IN, 0, st)
+
+    def step(self):
+        for m in self.mats:
+            self._dx(*m)
+
+    def dominant(self):
+        self._dx(*self.mats[4])
+
+    def step_e2e(self):
+        for m, pd in zip(self.mats, self.pin_dy):
+            m[3].copy_(pd, non_blocking=True)
+        self.step()
+        for m, px in zip(self.mats, self.pin_dx):
+            px.copy_(m[4], non_blocking=True)
+
+    def cpu(self, seconds):
+        """The oracle's restatement (numpy float64 matmul of the bf16 operands,
+        one BLAS thread) on 256-token slices of the C x C shape."""
+        from oracle import oracle as O
+        rng = np.random.default_rng(SEED)
+        C, T = self.C, 256
+        dy = rng.standard_normal((T, C)).astype(np.float32)
+        W = (rng.standard_normal((C, C)) * 0.02).astype(np.float32)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.base_matmul_vjp(dy, W)
+            n += 1
+        dt = time.perf_counter() - t0
+        self.cpu_cores = 1
+        return n * 2.0 * T * C * C / dt / 1e12, f"{n} backward products of {T} tokens x {C} x {C}"
+
+
 WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "wkv7train": WKV7Train, "gemv": GemvSuite,
-             "statetune": StateTune29B}
+             "statetune": StateTune29B, "dx": ProjBackward29B}
 
 
 # ----------------------------------------------------------------------- timing
@@ -690,8 +766,8 @@ def run_reference(args, rank):
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
            "higher_is_better": True, "dtype": "f32", "data": "synthetic",
            "config": config,
-           "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cores, "kind": "port",
-                            "threads": cpu_threads(cores), "sample": sample},
+           "cpu_baseline": {"value": value, "unit": wl.unit, "cores": getattr(wl, "cpu_cores", cores), "kind": "port",
+                            "threads": cpu_threads(getattr(wl, "cpu_cores", cores)), "sample": sample},
            "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
@@ -853,7 +929,10 @@ def main():
         # the dominant kernel timed on its own stream position, L2 flushed before each launch
         dt = timed(torch, wl.dominant, args.steps, args.warmup, flush_l2, False)
         dom_ms = sum(dt) / len(dt)
-        achieved = wl.dom_bytes / (dom_ms / 1e3) / 1e9
+        if getattr(wl, "bound", "hbm") == "tensor":
+            achieved = wl.dom_flops / (dom_ms / 1e3) / 1e12
+        else:
+            achieved = wl.dom_bytes / (dom_ms / 1e3) / 1e9
         kernel = wl.kernel
     else:
         dom_ms = local_ms / wl.launches_per_step
@@ -877,6 +956,16 @@ def main():
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clocks,
     }
+    if getattr(wl, "bound", "hbm") == "tensor":
+        # a contraction: FLOPs against the measured dense bf16 peak (burst: the kernel is timed alone)
+        step_tf = wl.flops / (local_ms / 1e3) / 1e12
+        result["roofline"].update({"bound": "tensor", "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                                   "frac": achieved / peaks["bf16_tflops"], "traffic": None})
+        result["step_roofline"] = {"flops": wl.flops, "achieved": step_tf, "frac": step_tf / peaks["bf16_tflops"],
+                                   "unit": "TFLOP/s"}
+        result["dtype"] = "bf16 x bf16 -> f32 (bf16-rounded)"
+        result["config"].update({"model": "x070 2.9B frozen bf16 base (C=2560, FFN 10240), one layer",
+                                 "tokens_per_gpu": wl.TOK})
     if wl.name == "statetune":
         result["config"].update({"model": "x070 2.9B WKV path (L=32 H=40 N=64)", "seq_len": wl.T,
                                  "rows_per_gpu": wl.B, "global_batch": wl.B * world,
@@ -898,8 +987,9 @@ def main():
         cores = os.cpu_count() or 1
         O.set_threads(cores)
         v, sample = wl.cpu(args.cpu_seconds)
-        result["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": cores, "kind": "port",
-                                  "threads": cpu_threads(cores), "sample": sample}
+        used = getattr(wl, "cpu_cores", cores)
+        result["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": used, "kind": "port",
+                                  "threads": cpu_threads(used), "sample": sample}
         if "prefill" in result:
             pw = result["prefill"].pop("_wl")
             pv, psample = pw.cpu(min(args.cpu_seconds, 5.0))

@@ -421,14 +421,16 @@ int rwkv_x070_inject_wait_error(rwkv_x070_t model, int host_record, rwkv_stream_
 int rwkv_x070_profile_step(rwkv_x070_t model, int rows, float* ms_host, int cap, char* names_host,
                            int names_cap, int* count, rwkv_stream_t stream);
 /* How a decode step runs.  path 0 (the default): the per-kernel sequence
- * captured in a CUDA graph.  path 1: for 9..64 rows with fp16 activations and
- * no LoRA adapters, the whole step is ONE cooperative launch of a persistent
- * kernel (one CTA per SM, phases separated by grid barriers, weight tiles
- * streamed ahead of their phase); other steps keep the graph.  The arithmetic
- * is the same (the tcgen05 path's fp16-dequantised weights above 8 rows);
- * split-K sums are grouped differently.  On the 1.5B step the persistent
- * kernel is the slower of the two (64 rows: 2.70 vs 2.11 ms), hence the
- * default.  rwkv_x070_decode_path returns 1 when a step on `rows` rows takes
+ * captured in a CUDA graph.  path 1: for 1..64 rows with fp16 activations on
+ * the 4-bit base and no LoRA adapters, the whole step is ONE cooperative
+ * launch of a persistent kernel (one CTA per SM, phases separated by grid
+ * barriers, weights streamed ahead of their phase): 1..8 rows on exact-code
+ * mma.sync GEMVs, 9..64 rows on the tcgen05 GEMM; other steps keep the graph.
+ * The arithmetic is the per-kernel path's for the row count (the exact
+ * dequantised weight up to 8 rows, the fp16-dequantised weight above); sums
+ * are grouped differently.  On the 1.5B step the persistent kernels are the
+ * slower (1 row 1.48 vs 1.37 ms, 8 rows 1.87 vs 1.52 ms, 64 rows 2.70 vs
+ * 2.11 ms), hence the default.  rwkv_x070_decode_path returns 1 when a step on `rows` rows takes
  * the persistent kernel.  No counterpart in the reference (MLX schedules the
  * reference's kernels). */
 int rwkv_x070_set_decode_path(rwkv_x070_t model, int path);
