@@ -356,6 +356,21 @@ int rwkv_x070_destroy(rwkv_x070_t model);
  * rank a multiple of 16, at most 256; stored fp16.  Changing an adapter drops
  * the captured step graphs. */
 int rwkv_x070_set_param(rwkv_x070_t model, const char* name, const float* host, int64_t n);
+/* A projection or head matrix (set_param's names "blocks.L.tmix.{r,k,v,o}_proj.weight",
+ * "blocks.L.cmix.{key,value}.weight", "head.weight") from .rwkvq buffers
+ * in the loader's layout, HOST memory, used as stored (no requantisation):
+ * kind 1 = sb6 (bits = xbits 0..2; b1 = qblk [OUT, IN/32 * (16 + 4 xbits)],
+ * b2 = qsqm [OUT, IN/32 * 2], b3 = ddm [OUT, IN/256] fp16 pairs); kind 2 =
+ * sym (bits 6 or 8; b1 = qblk, b2 = qs [OUT, IN/16] int8, b3 = d [OUT,
+ * IN/256] fp16); n1..n3 their byte counts; IN % 256 == 0.  The step then
+ * runs that matrix through rwkv_sb6_gemv / rwkv_sym_gemv's kernels (at most 4
+ * activation rows per launch) with the projection's epilogue, as the
+ * reference's decode takes rwkvqSb6GEMV / rwkvqSymGEMV for sidecar matrices
+ * (X070Backbone.swift:708-732).  set_param with fp32 values returns the
+ * matrix to the model's own base container.  Steps with such matrices take
+ * the per-kernel path. */
+int rwkv_x070_set_param_rwkvq(rwkv_x070_t model, const char* name, int kind, int bits, const void* b1, int64_t n1,
+                              const void* b2, int64_t n2, const void* b3, int64_t n3);
 /* Random init with the x070 recipe (Sources/RWKVGen/Training/X070Init.swift:79-206),
  * drawn on the device from `seed`. */
 int rwkv_x070_init_random(rwkv_x070_t model, uint64_t seed);

@@ -123,11 +123,14 @@ class X070Oracle:
     # dequantised weight (MLX's quantized matrix-vector product).
     GEMV_MAX_ROWS = 8
 
-    def __init__(self, cfg: Cfg, weights: dict, act="f16", quant_bits=4, group=64):
+    def __init__(self, cfg: Cfg, weights: dict, act="f16", quant_bits=4, group=64, exact=None):
         """quant_bits 4: the big matrices in the 4-bit container (used
         dequantised); quant_bits 0: a dense bf16 base.  The low-rank and
         adapter matrices are stored fp16, or bf16 with a bf16 model (the
-        runtime's storage)."""
+        runtime's storage).  exact: {name: fp32 [OUT, IN]} matrices used as
+        given at every row count -- the dequantised .rwkvq sb6 / sym matrices,
+        whose GEMVs (RwkvqSb6GEMV.swift:103-145, RwkvqSymGEMV.swift:100-199)
+        multiply the exact dequantised weight."""
         self.cfg, self.act = cfg, act
         self.w = {}
         self.w16 = {}
@@ -145,6 +148,9 @@ class X070Oracle:
             elif v.ndim == 2:          # dense low-rank branches: 16-bit storage
                 v = to_bf16(v) if lr_bf16 else v.astype(np.float16).astype(np.float32)
             self.w[k] = v.astype(np.float64)
+        for k, v in (exact or {}).items():
+            self.w[k] = np.asarray(v, np.float32).astype(np.float64)
+            self.w16.pop(k, None)
 
     def new_state(self, rows):
         c = self.cfg

@@ -54,6 +54,7 @@ _SIGS = {
     "rwkv_q_gemm_status": [P],
     "rwkv_q_gemm_inject_wait_error": [I, P],
     "rwkv_gemm_dx": [I, P, I, P, I, P, I, I, I, I, P],
+    "rwkv_x070_set_param_rwkvq": [P, ctypes.c_char_p, I, I, P, I64, P, I64, P, I64],
     "rwkv_q_gemm_dx": [I, P, P, P, P, I, I, P, I, I, I, I, I, I, P],
     "rwkv_q_dequant": [P, P, P, I, I, P, I, I, I, I, P],
     "rwkv_q_rows": [P, I, P, P, P, I, I, P, I, I, I, I, P],

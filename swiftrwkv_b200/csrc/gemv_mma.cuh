@@ -59,7 +59,13 @@ struct GemvJob {
     int y_stride;
     const float* bias;    // per-output-row bias for ACT_DECAY / ACT_SIGMOID_BIAS
     float alpha;          // ACT_SCALE factor
+    // weight container: WFMT_AFFINE (w / scales / biases above), or a .rwkvq
+    // matrix: WFMT_SB6 (w = qblk, scales = qsqm, biases = ddm; wbits = xbits)
+    // or WFMT_SYM (w = qblk, scales = qs, biases = d; wbits = 6 or 8)
+    int wfmt;
+    int wbits;
 };
+enum WFmt : int { WFMT_AFFINE = 0, WFMT_SB6 = 1, WFMT_SYM = 2 };
 
 enum Act : int {
     ACT_NONE = 0,

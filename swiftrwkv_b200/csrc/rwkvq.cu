@@ -14,6 +14,7 @@
 // accumulation of s*sum(q*x) + m*sum(x) per block (sb6) or
 // s*(sum(q*x) - 32*sum(x)) per 16-block (sym 6-bit), warp shuffle reduction.
 #include "common.cuh"
+#include "gemv_mma.cuh"
 
 namespace rwkv {
 
@@ -69,11 +70,11 @@ __global__ void sb6_dequant_kernel(const uint8_t* __restrict__ qblk, const uint8
     for (int c = 0; c < 32; c++) o[c] = from_f<TO>((float)nib[c] * s + m);
 }
 
-template <typename TX, int R>
+template <typename TX, int R, bool EP = false>
 __global__ void __launch_bounds__(256)
 sb6_gemv_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
                 const uint8_t* __restrict__ qsqm, const __half* __restrict__ ddm,
-                float* __restrict__ y, int OUT, int IN, int xbits) {
+                float* __restrict__ y, int OUT, int IN, int xbits, const GemvJob jb, int n0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= OUT) return;
@@ -102,7 +103,10 @@ sb6_gemv_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
 #pragma unroll
     for (int n = 0; n < R; n++) {
         const float v = warp_sum(acc[n]);
-        if (lane == 0) y[(int64_t)n * OUT + row] = v;
+        if (lane == 0) {
+            if constexpr (EP) epilogue(jb, row, n0 + n, v);
+            else y[(int64_t)n * OUT + row] = v;
+        }
     }
 }
 
@@ -186,11 +190,11 @@ __global__ void sym_dequant_kernel(const uint8_t* __restrict__ qblk, const int8_
     for (int c = 0; c < 16; c++) o[c] = from_f<TO>((float)code[c] * s);
 }
 
-template <typename TX, int R>
+template <typename TX, int R, bool EP = false>
 __global__ void __launch_bounds__(256)
 sym_gemv_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
                 const int8_t* __restrict__ qs, const __half* __restrict__ d, float* __restrict__ y,
-                int OUT, int IN, int bits, int out_per) {
+                int OUT, int IN, int bits, int out_per, const GemvJob jb, int n0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= OUT) return;
@@ -240,7 +244,10 @@ sym_gemv_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
 #pragma unroll
     for (int n = 0; n < R; n++) {
         const float v = warp_sum(acc[n]);
-        if (lane == 0) y[(int64_t)n * OUT + row] = v;
+        if (lane == 0) {
+            if constexpr (EP) epilogue(jb, row, n0 + n, v);
+            else y[(int64_t)n * OUT + row] = v;
+        }
     }
 }
 
@@ -286,7 +293,7 @@ int launch_sb6_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
 #define SB6C(RR)                                                                         \
     case RR:                                                                             \
         sb6_gemv_kernel<TX, RR><<<blocks, 256, 0, st>>>(xp, qblk, qsqm, (const __half*)ddm, \
-                                                        yp, OUT, IN, xbits);             \
+                                                        yp, OUT, IN, xbits, GemvJob{}, 0); \
         break;
                 SB6C(1) SB6C(2) SB6C(3) SB6C(4)
 #undef SB6C
@@ -335,12 +342,52 @@ int launch_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
     case RR:                                                                                 \
         sym_gemv_kernel<TX, RR><<<blocks, 256, 0, st>>>(xp, qblk, (const int8_t*)qs,        \
                                                         (const __half*)d, yp, OUT, IN, bits, \
-                                                        out_per);                            \
+                                                        out_per, GemvJob{}, 0);              \
         break;
                 SYMC(1) SYMC(2) SYMC(3) SYMC(4)
 #undef SYMC
             }
             int rc = check_launch("sym_gemv_kernel");
+            if (rc) return rc;
+        }
+        return ok();
+    });
+}
+
+// A decode-runtime job on a .rwkvq matrix (GemvJob.wfmt WFMT_SB6 / WFMT_SYM):
+// y = x W^T through the sb6 / sym GEMV, at most 4 activation rows per launch
+// (the reference's sym kernel takes up to 4, its sb6 kernel 1), with the job's
+// epilogue (activation, fp16 / fp32 / += output).  x rows are contiguous
+// (x_stride == IN); xdtype is the activation type.
+int launch_rwkvq_job(int xdtype, const GemvJob& j, int R, cudaStream_t st) {
+    const size_t xe = xdtype == RWKV_F32 ? 4 : 2;
+    return dispatch_dtype(xdtype, [&]<typename TX>() {
+        const int blocks = ceil_div(j.OUT, 8);
+        for (int n0 = 0; n0 < R; n0 += 4) {
+            const int r = min(4, R - n0);
+            const TX* xp = (const TX*)((const char*)j.x + (size_t)n0 * j.IN * xe);
+            if (j.wfmt == WFMT_SB6) {
+                const uint8_t* qb = (const uint8_t*)j.w;
+                const uint8_t* qsqm = (const uint8_t*)j.scales;
+                const __half* ddm = (const __half*)j.biases;
+                switch (r) {
+#define SB6J(RR) \
+    case RR: sb6_gemv_kernel<TX, RR, true><<<blocks, 256, 0, st>>>(xp, qb, qsqm, ddm, nullptr, j.OUT, j.IN, j.wbits, j, n0); break;
+                    SB6J(1) SB6J(2) SB6J(3) SB6J(4)
+#undef SB6J
+                }
+            } else {
+                const uint8_t* qb = (const uint8_t*)j.w;
+                const int8_t* qs = (const int8_t*)j.scales;
+                const __half* d = (const __half*)j.biases;
+                switch (r) {
+#define SYMJ(RR) \
+    case RR: sym_gemv_kernel<TX, RR, true><<<blocks, 256, 0, st>>>(xp, qb, qs, d, nullptr, j.OUT, j.IN, j.wbits, j.OUT, j, n0); break;
+                    SYMJ(1) SYMJ(2) SYMJ(3) SYMJ(4)
+#undef SYMJ
+                }
+            }
+            int rc = check_launch("rwkvq_gemv_kernel");
             if (rc) return rc;
         }
         return ok();

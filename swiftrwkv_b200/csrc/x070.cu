@@ -23,6 +23,10 @@
 #include "x070_small.cuh"
 
 namespace rwkv {
+int launch_rwkvq_job(int xdtype, const GemvJob& j, int R, cudaStream_t st);
+}
+
+namespace rwkv {
 
 int launch_q_quantize(int, const void*, uint32_t*, void*, void*, int, int, int, int, cudaStream_t);
 int64_t wkv7_chunk_workspace(int, int, int);
@@ -79,6 +83,12 @@ struct QMat {
     __nv_bfloat16* dense = nullptr;
     __half2* sbr = nullptr;  // (scale, bias) repacked per 128-row block and 256-code stage (persistent step)
     __half* sbs = nullptr;   // (scale, bias) blocks per 16-row tile and 2048-code piece (1..8-row persistent step)
+    // set: the matrix is a .rwkvq sb6 / sym matrix (WFMT_SB6 / WFMT_SYM, qbits
+    // = xbits / bits) used as stored: qblk, q2 = qsqm / qs, qd = ddm / d
+    int fmt = WFMT_AFFINE, qbits = 0;
+    uint8_t* qblk = nullptr;
+    uint8_t* q2 = nullptr;
+    __half* qd = nullptr;
     int OUT = 0, IN = 0;
 };
 
@@ -287,6 +297,15 @@ struct X070 {
         for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
         for (void* p : pk_allocs) cudaFree(p);
+        auto free_q = [](QMat& q) {
+            if (q.qblk) cudaFree(q.qblk);
+            if (q.q2) cudaFree(q.q2);
+            if (q.qd) cudaFree(q.qd);
+        };
+        free_q(head);
+        for (LayerW& w : lw) {
+            free_q(w.r); free_q(w.k); free_q(w.v); free_q(w.o); free_q(w.key); free_q(w.value);
+        }
         pf_free();
         if (pf_prompt) cudaFree(pf_prompt);
         gflag.release();
@@ -303,6 +322,10 @@ struct X070 {
     int upload_q(QMat& q, const float* host, int64_t n) {
         RWKV_REQUIRE(n == (int64_t)q.OUT * q.IN, RWKV_E_SHAPE, "matrix size %lld, expected %d x %d",
                      (long long)n, q.OUT, q.IN);
+        if (q.fmt != WFMT_AFFINE) {  // back to the model's own container: the launch sequence changes
+            q.fmt = WFMT_AFFINE;
+            drop_graphs();
+        }
         if (dense) {
             float* t32 = nullptr;
             if (cudaMalloc(&t32, n * 4) != cudaSuccess) return fail(RWKV_E_CUDA, "set_param: staging allocation failed");
@@ -377,6 +400,68 @@ struct X070 {
         RWKV_REQUIRE(!alloc_failed && dst && lora_z && (!key || key_tmp), RWKV_E_CUDA, "set_param: adapter allocation failed");
         drop_graphs();
         return upload_h(dst, n, host, n);
+    }
+
+    // The base matrix `name` (set_param's names of the projection / head
+    // matrices) from .rwkvq buffers used as stored: kind WFMT_SB6 (bits =
+    // xbits 0..2; b1 = qblk, b2 = qsqm, b3 = ddm) or WFMT_SYM (bits 6 or 8;
+    // b1 = qblk, b2 = qs, b3 = d).
+    int set_param_rwkvq(const std::string& name, int kind, int bits, const void* b1, int64_t n1, const void* b2,
+                        int64_t n2, const void* b3, int64_t n3) {
+        QMat* q = nullptr;
+        if (name == "head.weight") q = &head;
+        else if (name.compare(0, 7, "blocks.") == 0) {
+            const size_t dot = name.find('.', 7);
+            const int l = dot == std::string::npos ? -1 : atoi(name.c_str() + 7);
+            if (l >= 0 && l < L) {
+                const std::string sfx = name.substr(dot + 1);
+                LayerW& w = lw[l];
+                if (sfx == "tmix.r_proj.weight") q = &w.r;
+                else if (sfx == "tmix.k_proj.weight") q = &w.k;
+                else if (sfx == "tmix.v_proj.weight") q = &w.v;
+                else if (sfx == "tmix.o_proj.weight") q = &w.o;
+                else if (sfx == "cmix.key.weight") q = &w.key;
+                else if (sfx == "cmix.value.weight") q = &w.value;
+            }
+        }
+        RWKV_REQUIRE(q, RWKV_E_SHAPE, "set_param_rwkvq: '%s' is not a projection or head matrix", name.c_str());
+        const int64_t OUT = q->OUT, IN = q->IN;
+        RWKV_REQUIRE(IN % 256 == 0, RWKV_E_UNSUPPORTED, "set_param_rwkvq: IN=%lld not a multiple of 256", (long long)IN);
+        int64_t e1, e2, e3;
+        if (kind == WFMT_SB6) {
+            RWKV_REQUIRE(bits >= 0 && bits <= 2, RWKV_E_UNSUPPORTED, "set_param_rwkvq: sb6 xbits %d", bits);
+            e1 = OUT * (IN / 32) * (16 + 4 * bits);
+            e2 = OUT * (IN / 32) * 2;
+            e3 = OUT * (IN / 256) * 4;
+        } else if (kind == WFMT_SYM) {
+            RWKV_REQUIRE(bits == 6 || bits == 8, RWKV_E_UNSUPPORTED, "set_param_rwkvq: sym bits %d", bits);
+            e1 = bits == 8 ? OUT * IN : OUT * (IN / 32) * 24;
+            e2 = OUT * (IN / 16);
+            e3 = OUT * (IN / 256) * 2;
+        } else {
+            return fail(RWKV_E_UNSUPPORTED, "set_param_rwkvq: kind %d (1 sb6, 2 sym)", kind);
+        }
+        RWKV_REQUIRE(b1 && b2 && b3, RWKV_E_NULL, "set_param_rwkvq: NULL buffer");
+        RWKV_REQUIRE(n1 == e1 && n2 == e2 && n3 == e3, RWKV_E_SHAPE,
+                     "set_param_rwkvq: '%s' buffers %lld / %lld / %lld bytes, expected %lld / %lld / %lld",
+                     name.c_str(), (long long)n1, (long long)n2, (long long)n3, (long long)e1, (long long)e2,
+                     (long long)e3);
+        if (q->qblk) cudaFree(q->qblk);
+        if (q->q2) cudaFree(q->q2);
+        if (q->qd) cudaFree(q->qd);
+        q->qblk = q->q2 = nullptr;
+        q->qd = nullptr;
+        if (cudaMalloc(&q->qblk, n1) != cudaSuccess || cudaMalloc(&q->q2, n2) != cudaSuccess ||
+            cudaMalloc(&q->qd, n3) != cudaSuccess)
+            return fail(RWKV_E_CUDA, "set_param_rwkvq: allocation failed");
+        cudaMemcpy(q->qblk, b1, n1, cudaMemcpyHostToDevice);
+        cudaMemcpy(q->q2, b2, n2, cudaMemcpyHostToDevice);
+        cudaMemcpy(q->qd, b3, n3, cudaMemcpyHostToDevice);
+        q->fmt = kind;
+        q->qbits = bits;
+        wver++;
+        drop_graphs();
+        return check_launch("set_param_rwkvq");
     }
 
     int set_param(const std::string& name, const float* host, int64_t n) {
@@ -535,6 +620,24 @@ struct X070 {
     // fmt 0: the base matrices (4-bit, or dense bf16); 1: the low-rank / adapter matrices
     int gemv(int fmt, GemvJobs& jobs, int nj, int R, cudaStream_t st) {
         const int wf = fmt == 0 ? base_wf : lr_wf;
+        if (fmt == 0) {
+            // .rwkvq matrices go to their own GEMV kernels, the rest below
+            GemvJobs rest{};
+            int nr = 0;
+            for (int i = 0; i < nj; i++) {
+                if (jobs.j[i].wfmt != WFMT_AFFINE) {
+                    const int xdt = bf16act ? RWKV_BF16 : f16act ? RWKV_F16 : RWKV_F32;
+                    if (int rc = launch_rwkvq_job(xdt, jobs.j[i], R, st)) return rc;
+                } else {
+                    rest.j[nr++] = jobs.j[i];
+                }
+            }
+            if (nr == 0) return RWKV_OK;
+            if (nr < nj) {
+                jobs = rest;
+                nj = nr;
+            }
+        }
         if (f16act) {
             const int tfmt = wf == WF_Q4 ? TC_Q4 : wf == WF_F16 ? TC_F16 : TC_BF16;
             const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
@@ -568,6 +671,8 @@ struct X070 {
     // whether gemv() takes the tensor-core path for these jobs
     bool tc_path(int fmt, const GemvJobs& jobs, int nj, int R) const {
         const int wf = fmt == 0 ? base_wf : lr_wf;
+        for (int i = 0; i < nj; i++)
+            if (jobs.j[i].wfmt != WFMT_AFFINE) return false;
         return f16act && plan_tc(wf == WF_Q4 ? TC_Q4 : wf == WF_F16 ? TC_F16 : TC_BF16, jobs, nj, R, sm_count).ok;
     }
     // output type of an activation-typed GEMM result
@@ -579,6 +684,13 @@ struct X070 {
         if (q.dense) j.w = q.dense;
         else j.w = q.wq;
         j.scales = q.sc; j.biases = q.bi; j.x = x; j.x_stride = xs;
+        if (q.fmt != WFMT_AFFINE) {
+            j.w = q.qblk;
+            j.scales = (const __half*)q.q2;
+            j.biases = q.qd;
+            j.wfmt = q.fmt;
+            j.wbits = q.qbits;
+        }
         j.OUT = q.OUT; j.IN = q.IN; j.act = act; j.out = out; j.y = y; j.y_stride = ys; j.bias = bias;
         return j;
     }
@@ -790,6 +902,12 @@ struct X070 {
     int64_t pk_wver = -1;
     int pk_occ = -1;  // CTAs of the persistent kernel per SM (cached)
 
+    bool any_rwkvq() const {
+        if (head.fmt != WFMT_AFFINE) return true;
+        for (const LayerW& w : lw)
+            if (w.r.fmt || w.k.fmt || w.v.fmt || w.o.fmt || w.key.fmt || w.value.fmt) return true;
+        return false;
+    }
     bool any_adapter() const {
         if (head_ad.on()) return true;
         for (const LayerW& w : lw)
@@ -800,7 +918,7 @@ struct X070 {
     // Whether a step on R rows takes the persistent kernel.
     bool pk_eligible(int R) const {
         return decode_path == 1 && f16act && !bf16act && !dense && R > 8 && R <= 64 && C % 256 == 0 && C <= 4 * pk::WT * 2 &&
-               F % 256 == 0 && V % 128 == 0 && !any_adapter();
+               F % 256 == 0 && V % 128 == 0 && !any_adapter() && !any_rwkvq();
     }
     template <typename T>
     T* pk_alloc(size_t n) {
@@ -1059,7 +1177,7 @@ struct X070 {
 
     bool sp_eligible(int R) const {
         return decode_path == 1 && f16act && !bf16act && !dense && R >= 1 && R <= 8 && C % 128 == 0 &&
-               C <= 4 * pk::WT * 2 && F % 128 == 0 && !any_adapter();
+               C <= 4 * pk::WT * 2 && F % 128 == 0 && !any_adapter() && !any_rwkvq();
     }
     struct SpProgram {
         int nphases = 0;
@@ -1855,6 +1973,12 @@ int rwkv_x070_profile_step(rwkv_x070_t h, int rows, float* ms_host, int cap, cha
     X070& m = *reinterpret_cast<X070*>(h);
     RWKV_REQUIRE(rows >= 1 && rows <= m.Rmax, RWKV_E_SHAPE, "rows %d not in 1..%d", rows, m.Rmax);
     return m.profile_step(rows, (cudaStream_t)stream, ms_host, cap, names_host, names_cap, count);
+}
+
+int rwkv_x070_set_param_rwkvq(rwkv_x070_t h, const char* name, int kind, int bits, const void* b1, int64_t n1,
+                              const void* b2, int64_t n2, const void* b3, int64_t n3) {
+    RWKV_REQUIRE(h && name, RWKV_E_NULL, "rwkv_x070_set_param_rwkvq: NULL argument");
+    return reinterpret_cast<X070*>(h)->set_param_rwkvq(name, kind, bits, b1, n1, b2, n2, b3, n3);
 }
 
 int rwkv_x070_set_decode_path(rwkv_x070_t h, int path) {

@@ -17,6 +17,16 @@ from . import _lib
 from ._lib import BF16, F16, F32, call
 
 
+def _native_matrix(key: str) -> bool:
+    """Base matrices a .rwkvq sb6 / sym tensor can stay native for."""
+    if key == "head.weight":
+        return True
+    parts = key.split(".")
+    return len(parts) >= 4 and parts[0] == "blocks" and ".".join(parts[2:]) in (
+        "tmix.r_proj.weight", "tmix.k_proj.weight", "tmix.v_proj.weight", "tmix.o_proj.weight",
+        "cmix.key.weight", "cmix.value.weight")
+
+
 def lora_ranks(D: int):
     """x070 low-rank sizes, rwkvMetal formula (X070Init.swift:46-52)."""
     def f(c, p):
@@ -91,28 +101,44 @@ class X070Backbone:
                  a.size)
         return self
 
-    def load_rwkvq(self, path: str, weights: dict | None = None):
+    def load_rwkvq(self, path: str, weights: dict | None = None, native: bool = True):
         """The projection matrices, embedding and head found in a `.rwkvq`
-        file (swiftrwkv_b200.rwkvq; world names mapped as RwkvqNaming does),
-        dequantised on the GPU -- sb6 and sym by the reference's dequant
-        kernels' arithmetic (RwkvqDequant.swift) -- into this model's base:
-        rounded once into bf16 for the dense base (the reference's
-        dequantise-then-matmul path), re-quantised into the 4-bit container
-        otherwise (lossy: sb6 / sym are not 4-bit group 64).  Tensors without
-        an x070 name are skipped; `weights` (reference names) supplies the
-        rest of the model.  Returns the x070 names loaded."""
+        file (swiftrwkv_b200.rwkvq; world names mapped as RwkvqNaming does).
+        With `native`, sb6 and sym projection / head matrices are kept as
+        stored (rwkv_x070_set_param_rwkvq: the step runs them through the
+        sb6 / sym GEMV kernels, as the reference's decode does); the others --
+        and every matrix without `native` -- are dequantised on the GPU by the
+        reference's dequant arithmetic (RwkvqDequant.swift) into this model's
+        base: rounded once into bf16 for the dense base, re-quantised into
+        the 4-bit container otherwise (lossy: sb6 / sym are not 4-bit group
+        64).  `weights` (reference names) is loaded first and supplies the
+        rest of the model; the file's tensors take precedence.  Returns the
+        x070 names loaded."""
         from .rwkvq import RwkvqFile, x070_key
         f = RwkvqFile(path)
+        if weights:
+            self.load(weights)
         done = []
         for wk in f.keys():
             key = x070_key(wk) if f.naming == "world" else wk
             if key is None:
                 continue
-            w = f.dequantize(wk, torch.float32).cpu().numpy()
-            call("rwkv_x070_set_param", self.h, key.encode(), w.ctypes.data_as(ctypes.c_void_p), w.size)
+            kind = f.info(wk)["kind"]
+            if native and kind in ("sb6", "sym") and _native_matrix(key) and f.info(wk)["shape"][1] % 256 == 0:
+                t = f.tensor(wk)
+                if kind == "sb6":
+                    bufs, fmt, bits = (t["qblk"], t["qsqm"], t["ddm"]), 1, int(t["xbits"])
+                else:
+                    bufs, fmt, bits = (t["qblk"], t["qs"], t["d"]), 2, int(t["bits"])
+                bufs = [np.ascontiguousarray(b) for b in bufs]
+                args = []
+                for b in bufs:
+                    args += [b.ctypes.data_as(ctypes.c_void_p), b.nbytes]
+                call("rwkv_x070_set_param_rwkvq", self.h, key.encode(), fmt, bits, *args)
+            else:
+                w = f.dequantize(wk, torch.float32).cpu().numpy()
+                call("rwkv_x070_set_param", self.h, key.encode(), w.ctypes.data_as(ctypes.c_void_p), w.size)
             done.append(key)
-        if weights:
-            self.load(weights)
         return done
 
     def init_random(self, seed: int = 0):
@@ -130,8 +156,9 @@ class X070Backbone:
 
     def set_decode_path(self, path: int):
         """0: one captured graph of per-op launches per step (default);
-        1: the persistent one-launch step where it applies (9..64 rows, fp16
-        activations, 4-bit base), the per-op graph elsewhere."""
+        1: the persistent one-launch step where it applies (1..64 rows, fp16
+        activations, 4-bit base, no adapters or .rwkvq matrices), the per-op
+        graph elsewhere."""
         call("rwkv_x070_set_decode_path", self.h, int(path))
         return self
 
