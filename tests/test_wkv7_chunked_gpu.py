@@ -23,7 +23,9 @@ def host(t):
 
 
 @pytest.mark.parametrize("B,T,H", [(1, 1, 2), (1, 5, 3), (1, 16, 2), (1, 17, 4), (2, 53, 3),
-                                   (1, 512, 12), (3, 32, 1), (2, 100, 5)])
+                                   (1, 512, 12), (3, 32, 1), (2, 100, 5),
+                                   # 24+ chunks: the grouped three-level scan (ragged last chunk and group)
+                                   (1, 1000, 3), (2, 390, 2)])
 @pytest.mark.parametrize("with_h0", [False, True])
 def test_chunked_matches_oracle(cuda, oracle, rng, B, T, H, with_h0):
     from swiftrwkv_b200 import kernel as K

@@ -35,7 +35,9 @@ def _case(rng, B, T, H, with_h0=True, with_dh=True):
     return ins, h0, dy, dh
 
 
-@pytest.mark.parametrize("B,T,H", [(1, 16, 1), (1, 64, 2), (2, 48, 3), (1, 256, 4), (3, 32, 2)])
+@pytest.mark.parametrize("B,T,H", [(1, 16, 1), (1, 64, 2), (2, 48, 3), (1, 256, 4), (3, 32, 2),
+                                   # 24+ chunks: the grouped three-level scans, forward and reverse
+                                   (1, 400, 2), (2, 528, 2)])
 @pytest.mark.parametrize("with_h0,with_dh", [(True, True), (False, False), (True, False)])
 def test_chunked_backward_matches_oracle(cuda, oracle, rng, B, T, H, with_h0, with_dh):
     from swiftrwkv_b200 import kernel as K
@@ -51,10 +53,12 @@ def test_chunked_backward_matches_oracle(cuda, oracle, rng, B, T, H, with_h0, wi
         assert rel_err(g, wv) < GRAD_TOL, (name, rel_err(g, wv))
 
 
-def test_chunked_train_forward_matches_sequential(cuda, rng):
-    """y, h_out, sa and every 16-token checkpoint against the sequential train forward."""
+@pytest.mark.parametrize("T", [96, 784])
+def test_chunked_train_forward_matches_sequential(cuda, rng, T):
+    """y, h_out, sa and every 16-token checkpoint against the sequential train
+    forward (T = 784: 49 chunks, the grouped scan with 7 groups of 7)."""
     from swiftrwkv_b200 import kernel as K
-    ins, h0, _, _ = _case(rng, 2, 96, 3)
+    ins, h0, _, _ = _case(rng, 2, T, 3)
     d = [dev(x) for x in ins]
     a = K._train_forward(*d, dev(h0))
     b = K.wkv7TrainForwardChunked(*d, dev(h0))
