@@ -616,6 +616,106 @@ def cpu_threads(cores):
     return {"openmp": cores, "blas": int(os.environ.get("OPENBLAS_NUM_THREADS", BLAS_THREADS))}
 
 
+class RwkvqGemvSuite:
+    """Config 2's .rwkvq variant: the sb6 (5-bit: 4 + 1 bit-plane) and sym (6-
+    and 8-bit) GEMVs at the 1.5B projection shapes (2048x2048, 8192x2048,
+    2048x8192, 65536x2048), fp16 activations, through rwkv_sb6_gemv /
+    rwkv_sym_gemv (RwkvqSb6GEMV.swift:69-208, RwkvqSymGEMV.swift:89-263).
+    Synthetic codes and scales (values do not change the timing)."""
+    name = "gemv_rwkvq"
+    unit = "GB/s"
+    MATS = [(2048, 2048), (8192, 2048), (2048, 8192), (65536, 2048)]
+    FMTS = [("sb6", 1), ("sym", 6), ("sym", 8)]
+
+    def __init__(self, rows=1):
+        self.rows = rows
+        self.metric = (f".rwkvq GEMV GB/s (config 2: sb6 5-bit, sym 6 / 8-bit at the 1.5B projection shapes, "
+                       f"rows {rows}, fp16 x)")
+
+    @staticmethod
+    def wbytes(kind, bits, OUT, IN):
+        if kind == "sb6":
+            return OUT * IN * (16 + 4 * bits + 2) // 32 + OUT * IN // 256 * 4
+        code = OUT * IN if bits == 8 else OUT * IN * 24 // 32
+        return code + OUT * IN // 16 + OUT * IN // 256 * 2
+
+    def setup(self, torch, dev):
+        from swiftrwkv_b200 import _lib
+        self.torch, self._lib = torch, _lib
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        R = self.rows
+        u8 = lambda n: torch.randint(0, 256, (n,), generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
+        self.jobs = []
+        for kind, bits in self.FMTS:
+            for OUT, IN in self.MATS:
+                if kind == "sb6":
+                    NB = IN // 32
+                    qblk = u8(OUT * NB * (16 + 4 * bits))
+                    q2 = u8(OUT * NB * 2) & 0x3F          # qs < 64, qm small and positive (valid int8)
+                    d = (torch.rand(OUT * (NB // 8) * 2, generator=g, device=dev) * 1e-3).half()
+                else:
+                    qblk = u8(OUT * IN if bits == 8 else OUT * IN // 32 * 24)
+                    q2 = u8(OUT * IN // 16) & 0x7F
+                    d = (torch.rand(OUT * (IN // 256), generator=g, device=dev) * 1e-4).half()
+                x = torch.randn((R, IN), generator=g, device=dev).half()
+                y = torch.empty((R, OUT), device=dev, dtype=torch.float32)
+                self.jobs.append((kind, bits, OUT, IN, qblk, q2, d, x, y))
+        mb = lambda kind, bits, OUT, IN: self.wbytes(kind, bits, OUT, IN) + R * IN * 2 + R * OUT * 4
+        self.alg_bytes = sum(mb(j[0], j[1], j[2], j[3]) for j in self.jobs)
+        self.units_per_step = self.alg_bytes / 1e9
+        self.launches_per_step = len(self.jobs) * ((R + 3) // 4)
+        self.dom = self.jobs[-1]  # sym 8-bit head
+        self.dom_bytes = mb(*self.dom[:4])
+        self.kernel = "sym_gemv_kernel (8-bit), 65536x2048"
+        self.h2d = sum(R * j[3] * 2 for j in self.jobs)
+        self.d2h = sum(R * j[2] * 4 for j in self.jobs)
+        self.pin_x = [torch.empty((R, j[3]), dtype=torch.float16).pin_memory() for j in self.jobs]
+        self.pin_y = [torch.empty((R, j[2]), dtype=torch.float32).pin_memory() for j in self.jobs]
+
+    def _gemv(self, kind, bits, OUT, IN, qblk, q2, d, x, y):
+        _lib, P = self._lib, self._lib.P
+        st = P(self.torch.cuda.current_stream().cuda_stream)
+        if kind == "sb6":
+            _lib.call("rwkv_sb6_gemv", 2, P(x.data_ptr()), P(qblk.data_ptr()), P(q2.data_ptr()), P(d.data_ptr()),
+                      P(y.data_ptr()), self.rows, OUT, IN, bits, st)
+        else:
+            _lib.call("rwkv_sym_gemv", 2, P(x.data_ptr()), P(qblk.data_ptr()), P(q2.data_ptr()), P(d.data_ptr()),
+                      P(y.data_ptr()), self.rows, OUT, IN, bits, OUT, st)
+
+    def step(self):
+        for j in self.jobs:
+            self._gemv(*j)
+
+    def dominant(self):
+        self._gemv(*self.dom)
+
+    def step_e2e(self):
+        for j, px in zip(self.jobs, self.pin_x):
+            j[7].copy_(px, non_blocking=True)
+        self.step()
+        for j, py in zip(self.jobs, self.pin_y):
+            py.copy_(j[8], non_blocking=True)
+
+    def cpu(self, seconds):
+        """The oracle's sb6 GEMV (RwkvqSb6GEMV.swift:103-145 order) on one
+        2048 x 2048 matrix, one row."""
+        from oracle import oracle as O
+        rng = np.random.default_rng(SEED)
+        OUT, IN, xb = 2048, 2048, 1
+        NB = IN // 32
+        qblk = rng.integers(0, 256, (OUT, NB * (16 + 4 * xb)), dtype=np.uint8)
+        qsqm = (rng.integers(0, 64, (OUT, NB * 2))).astype(np.uint8)
+        ddm = (np.abs(rng.standard_normal((OUT, NB // 8 * 2))) * 1e-3).astype(np.float16).view(np.uint16)
+        x = rng.standard_normal((IN,)).astype(np.float32)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.sb6_gemv(x, qblk, qsqm, ddm, OUT, IN, xb)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * self.wbytes("sb6", xb, OUT, IN) / dt / 1e9, f"{n} sb6 GEMVs of 2048x2048 (5-bit), 1 row"
+
+
 class ProjBackward29B:
     """The frozen-base projection backward dX = bf16(bf16(dY) W_bf16) (the
     bf16 VJP of X070Backbone.baseMatmul, X070Backbone.swift:337-356) over one
@@ -693,7 +793,8 @@ class ProjBackward29B:
 
 
 WORKLOADS = {"decode": Decode15B, "wkv7": WKV7Prefill, "wkv7train": WKV7Train, "gemv": GemvSuite,
-             "statetune": StateTune29B, "dx": ProjBackward29B}
+             "statetune": StateTune29B, "dx": ProjBackward29B,
+             "gemv_rwkvq": RwkvqGemvSuite}
 
 
 # ----------------------------------------------------------------------- timing
@@ -859,6 +960,8 @@ def make_workload(args):
         return Decode15B(args.rows or 64, args.prompt, args.decode_path)
     if args.workload == "gemv":
         return GemvSuite(args.rows or 1)
+    if args.workload == "gemv_rwkvq":
+        return RwkvqGemvSuite(args.rows or 1)
     if args.workload == "statetune":
         return StateTune29B(args.rows or 1)
     return WORKLOADS[args.workload]()
@@ -942,7 +1045,9 @@ def main():
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32" if wl.name in ("wkv7", "wkv7train", "statetune") else "u4 x f16 -> f32", "data": "synthetic",
+        "dtype": ("f32" if wl.name in ("wkv7", "wkv7train", "statetune") else
+                  "sb6 u5 / sym u6, i8 x f16 -> f32" if wl.name == "gemv_rwkvq" else "u4 x f16 -> f32"),
+        "data": "synthetic",
         "config": {"workload": wl.name, "l2": l2_note, "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],

@@ -70,40 +70,258 @@ __global__ void sb6_dequant_kernel(const uint8_t* __restrict__ qblk, const uint8
     for (int c = 0; c < 32; c++) o[c] = from_f<TO>((float)nib[c] * s + m);
 }
 
-template <typename TX, int R, bool EP = false>
-__global__ void __launch_bounds__(256)
-sb6_gemv_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
-                const uint8_t* __restrict__ qsqm, const __half* __restrict__ ddm,
-                float* __restrict__ y, int OUT, int IN, int xbits, const GemvJob jb, int n0) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + warp;
-    if (row >= OUT) return;
-    const int NB = IN / 32, NSB = NB / 8, BB = 16 + 4 * xbits;
+// Four codes packed in the bytes of a word -> exact floats: byte k placed
+// under the exponent of 2^23 (one PRMT), less 2^23 (one FADD).
+__device__ __forceinline__ float code_f(uint32_t packed, int k) {
+    return __int_as_float(__byte_perm(packed, 0x4B000000u, (uint32_t)k | 0x7540u)) - 8388608.f;
+}
+// Bits 0..3 of b, one per byte (bit i -> bit 0 of byte i).
+__device__ __forceinline__ uint32_t spread4(uint32_t b) { return ((b & 0xFu) * 0x00204081u) & 0x01010101u; }
+
+// ---- tiled GEMVs (the launchers' path): CTA = 256 threads; TPR = min(16,
+// IN / 128) threads per output row (RPC = 256 / TPR rows per CTA); thread
+// (row, u) owns unit u of every K window -- a unit is 128 codes (4 sb6 blocks
+// or 8 sym 16-blocks), loaded as 16-byte vectors with its scales in one load.
+// Each window (TPR units per row) of the activations, and the per-block sums
+// of x, are staged in shared memory for all rows of the CTA.  Per block the
+// arithmetic is the row-per-warp kernels' (codes summed sequentially, fp32
+// s * sum(q x) + m * sum(x)); the TPR partials of a row are summed by a fixed
+// shuffle tree.
+constexpr int TG_T = 256;
+constexpr int TG_UNIT = 128;
+
+// threads per row: the largest power of two <= 16 that divides IN / 128
+__host__ __device__ __forceinline__ int tg_tpr(int IN) {
+    const int u = IN / TG_UNIT;
+    int t = 16;
+    while (t > 1 && u % t) t >>= 1;
+    return t;
+}
+
+// Staged window layout: a 32-column sub-block takes 36 floats and a 128-column
+// unit 148 (4 x 36 + 4), so the threads of a row -- one unit each -- read
+// distinct banks (16-byte vectors stay aligned).  xidx: the offset of column c
+// of a row inside the window; TG_RS: the floats of one row (16 units).
+constexpr int TG_SUB = 36, TG_USTR = 148, TG_RS = 16 * TG_USTR;
+__device__ __forceinline__ int xidx(int c) { return (c >> 7) * TG_USTR + ((c >> 5) & 3) * TG_SUB + (c & 31); }
+
+// x rows of the window [k0, k0 + W) into xs (fp32, the layout above), block
+// sums (blocks of BS codes, summed in column order) into bs[n][W / BS].
+template <typename TX, int R, int BS>
+__device__ __forceinline__ void tg_stage(const TX* __restrict__ x, int64_t xstride, int k0, int W, int rows,
+                                         float* xs, float* bs) {
+    for (int e = threadIdx.x; e < R * W; e += TG_T) {
+        const int n = e / W, c = e - n * W;
+        xs[n * TG_RS + xidx(c)] = n < rows ? to_f(x[(int64_t)n * xstride + k0 + c]) : 0.f;
+    }
+    __syncthreads();
+    const int nb = W / BS;
+    for (int e = threadIdx.x; e < R * nb; e += TG_T) {
+        const int n = e / nb, b = e - n * nb;
+        const float* p = xs + n * TG_RS + xidx(b * BS);
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < BS; c++) t += p[c];
+        bs[e] = t;
+    }
+    __syncthreads();
+}
+
+template <typename TX, int R, bool EP, int XB>
+__global__ void __launch_bounds__(TG_T)
+sb6_gemv_tile_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk, const uint8_t* __restrict__ qsqm,
+                     const __half* __restrict__ ddm, float* __restrict__ y, int OUT, int IN, int rows,
+                     const GemvJob jb, int n0) {
+    constexpr int xbits = XB;
+    __shared__ __align__(16) float xs[R * TG_RS];
+    __shared__ float bs[R * 16 * TG_UNIT / 32];
+    const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT;
+    const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
+    const int row = blockIdx.x * RPC + lr;
+    const int NB = IN / 32, NSB = NB / 8;
+    constexpr int BB = 16 + 4 * xbits, NV = BB / 4;  // block bytes; 16-byte vectors per unit = words per block
+    const int64_t rowc = min(row, OUT - 1);
     float acc[R];
 #pragma unroll
     for (int n = 0; n < R; n++) acc[n] = 0.f;
-    for (int p = lane; p < NB; p += 32) {
-        uint8_t nib[32];
-        sb6_block_codes(qblk + ((int64_t)row * NB + p) * BB, xbits, nib);
-        float s, m;
-        sb6_block_scales(qsqm, ddm, row, NB, NSB, p, s, m);
+    for (int k0 = 0; k0 < IN; k0 += W) {
+        tg_stage<TX, R, 32>(x, IN, k0, W, rows, xs, bs);
+        const int blk0 = (k0 + u * TG_UNIT) / 32;  // first of the unit's 4 blocks
+        const uint4* src = reinterpret_cast<const uint4*>(qblk + (rowc * NB + blk0) * BB);
+        uint32_t wd[24];
 #pragma unroll
-        for (int n = 0; n < R; n++) {
-            const TX* xp = x + (int64_t)n * IN + p * 32;
-            float dv = 0.f, xs = 0.f;
-#pragma unroll
-            for (int c = 0; c < 32; c++) {
-                const float xv = to_f(xp[c]);
-                dv = fmaf(xv, (float)nib[c], dv);
-                xs += xv;
+        for (int v = 0; v < 6; v++) {
+            if (v < NV) {
+                const uint4 q = __ldg(src + v);
+                wd[4 * v] = q.x; wd[4 * v + 1] = q.y; wd[4 * v + 2] = q.z; wd[4 * v + 3] = q.w;
             }
-            acc[n] = fmaf(s, dv, fmaf(m, xs, acc[n]));
         }
+        const uint2 sq = __ldg(reinterpret_cast<const uint2*>(qsqm + 2 * (rowc * NB + blk0)));
+        const __half2 dd = __ldg(reinterpret_cast<const __half2*>(ddm) + rowc * NSB + blk0 / 8);
+        const float d = __low2float(dd), dm = __high2float(dd);
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const uint32_t pair = (b < 2 ? sq.x : sq.y) >> (16 * (b & 1));
+            const float s = rnd_half((float)(pair & 0xFF) * d);
+            const float m = rnd_half((float)(int8_t)(pair >> 8) * dm);
+            const int wb = b * NV;  // the block's first word: NV words per block
+            const uint32_t qh = xbits >= 1 ? wd[wb + 4] : 0u, qh2 = xbits >= 2 ? wd[wb + 5] : 0u;
+            const int cb = u * TG_UNIT + 32 * b;  // column of the block inside the window
+            // the block's 32 codes as floats, column order (bytes j: low nibble col j, high col j + 16)
+            float q[32];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t nw = wd[wb + i];
+                uint32_t lo = nw & 0x0F0F0F0Fu, hi = (nw >> 4) & 0x0F0F0F0Fu;
+                if (xbits >= 1) {
+                    lo |= spread4(qh >> (4 * i)) << 4;
+                    hi |= spread4(qh >> (16 + 4 * i)) << 4;
+                }
+                if (xbits >= 2) {
+                    lo |= spread4(qh2 >> (4 * i)) << 5;
+                    hi |= spread4(qh2 >> (16 + 4 * i)) << 5;
+                }
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    q[4 * i + k] = code_f(lo, k);
+                    q[16 + 4 * i + k] = code_f(hi, k);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < R; n++) {
+                const float* xb = xs + n * TG_RS + xidx(cb);  // the block: 32 contiguous floats
+                float dv = 0.f;
+#pragma unroll
+                for (int c4 = 0; c4 < 8; c4++) {
+                    const float4 xv = reinterpret_cast<const float4*>(xb)[c4];
+                    dv = fmaf(xv.x, q[4 * c4], dv);
+                    dv = fmaf(xv.y, q[4 * c4 + 1], dv);
+                    dv = fmaf(xv.z, q[4 * c4 + 2], dv);
+                    dv = fmaf(xv.w, q[4 * c4 + 3], dv);
+                }
+                acc[n] = fmaf(s, dv, fmaf(m, bs[n * (W / 32) + cb / 32], acc[n]));
+            }
+        }
+        __syncthreads();  // the window may be overwritten
     }
 #pragma unroll
     for (int n = 0; n < R; n++) {
-        const float v = warp_sum(acc[n]);
-        if (lane == 0) {
+        float v = acc[n];
+        for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (u == 0 && row < OUT && n < rows) {
+            if constexpr (EP) epilogue(jb, row, n0 + n, v);
+            else y[(int64_t)n * OUT + row] = v;
+        }
+    }
+}
+
+// sym: a unit is 8 16-blocks (8-bit: 8 vectors) or 4 32-code pairs (6-bit: 6
+// vectors); x of matrix xi = row / out_per (every row of a CTA in one matrix).
+template <typename TX, int R, bool EP>
+__global__ void __launch_bounds__(TG_T)
+sym_gemv_tile_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk, const int8_t* __restrict__ qs,
+                     const __half* __restrict__ d, float* __restrict__ y, int OUT, int IN, int bits, int out_per,
+                     int rows, const GemvJob jb, int n0) {
+    __shared__ __align__(16) float xs[R * TG_RS];
+    __shared__ float bs[R * 16 * TG_UNIT / 16];
+    const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT;
+    const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
+    const int row = blockIdx.x * RPC + lr;
+    const int NB = IN / 16, NSB = IN / 256, NK = OUT / out_per, xi = (blockIdx.x * RPC) / out_per;
+    const int64_t rowc = min(row, OUT - 1);
+    const TX* xm = x + (int64_t)xi * IN;
+    float acc[R];
+#pragma unroll
+    for (int n = 0; n < R; n++) acc[n] = 0.f;
+    for (int k0 = 0; k0 < IN; k0 += W) {
+        tg_stage<TX, R, 16>(xm, (int64_t)NK * IN, k0, W, rows, xs, bs);
+        const int blk0 = (k0 + u * TG_UNIT) / 16;  // first of the unit's 8 16-blocks
+        const int cu = u * TG_UNIT;                 // the unit's column inside the window
+        const uint2 q8 = __ldg(reinterpret_cast<const uint2*>(qs + rowc * NB + blk0));
+        const float dsb = __half2float(__ldg(d + rowc * NSB + blk0 / 16));
+        float sc[8];
+#pragma unroll
+        for (int b = 0; b < 8; b++)
+            sc[b] = rnd_half((float)(int8_t)((b < 4 ? q8.x : q8.y) >> (8 * (b & 3))) * dsb);
+        if (bits == 8) {
+            const uint4* src = reinterpret_cast<const uint4*>(qblk + rowc * IN + (int64_t)blk0 * 16);
+#pragma unroll
+            for (int b = 0; b < 8; b++) {
+                const uint4 qv = __ldg(src + b);
+                const uint32_t wd[4] = {qv.x, qv.y, qv.z, qv.w};
+                // int8 codes: bytes ^ 0x80 -> 0..255 under 2^23, less 2^23 + 128
+                float q[16];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const uint32_t u8 = wd[i] ^ 0x80808080u;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) q[4 * i + k] = code_f(u8, k) - 128.f;
+                }
+#pragma unroll
+                for (int n = 0; n < R; n++) {
+                    const float* xb = xs + n * TG_RS + xidx(cu + 16 * b);  // 16 contiguous floats
+                    float dv = 0.f;
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; c4++) {
+                        const float4 xv = reinterpret_cast<const float4*>(xb)[c4];
+                        dv = fmaf(xv.x, q[4 * c4], dv);
+                        dv = fmaf(xv.y, q[4 * c4 + 1], dv);
+                        dv = fmaf(xv.z, q[4 * c4 + 2], dv);
+                        dv = fmaf(xv.w, q[4 * c4 + 3], dv);
+                    }
+                    acc[n] = fmaf(sc[b], dv, acc[n]);
+                }
+            }
+        } else {
+            const uint4* src = reinterpret_cast<const uint4*>(qblk + (rowc * (IN / 32) + blk0 / 2) * 24);
+            uint32_t wd[24];
+#pragma unroll
+            for (int v = 0; v < 6; v++) {
+                const uint4 q = __ldg(src + v);
+                wd[4 * v] = q.x; wd[4 * v + 1] = q.y; wd[4 * v + 2] = q.z; wd[4 * v + 3] = q.w;
+            }
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                const uint32_t* pw = wd + 6 * p;
+                const uint32_t hb = pw[4], hb2 = pw[5];
+                // the pair's 32 codes (+32) as floats, column order: block q's bytes 0..7
+                // (words 2q, 2q+1) give columns j (low nibble) and j + 8 (high) of the block
+                float q[32];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int blk = i >> 1, half = i & 1;  // word i: block blk, bytes 4 half .. 4 half + 3
+                    const uint32_t nw = pw[i];
+                    const int cl = 16 * blk + 4 * half, ch = cl + 8;  // columns of the low / high nibbles
+                    const uint32_t lo = (nw & 0x0F0F0F0Fu) | (spread4(hb >> cl) << 4) | (spread4(hb2 >> cl) << 5);
+                    const uint32_t hi = ((nw >> 4) & 0x0F0F0F0Fu) | (spread4(hb >> ch) << 4) | (spread4(hb2 >> ch) << 5);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        q[cl + k] = code_f(lo, k);
+                        q[ch + k] = code_f(hi, k);
+                    }
+                }
+#pragma unroll
+                for (int n = 0; n < R; n++) {
+                    const float* xp = xs + n * TG_RS + xidx(cu + 32 * p);  // the pair: 32 contiguous floats
+                    float dv0 = 0.f, dv1 = 0.f;
+#pragma unroll
+                    for (int c = 0; c < 16; c++) {
+                        dv0 = fmaf(xp[c], q[c], dv0);
+                        dv1 = fmaf(xp[16 + c], q[16 + c], dv1);
+                    }
+                    const int bi = (cu + 32 * p) / 16;
+                    acc[n] = fmaf(sc[2 * p], dv0 - 32.0f * bs[n * (W / 16) + bi],
+                                  fmaf(sc[2 * p + 1], dv1 - 32.0f * bs[n * (W / 16) + bi + 1], acc[n]));
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int n = 0; n < R; n++) {
+        float v = acc[n];
+        for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (u == 0 && row < OUT && n < rows) {
             if constexpr (EP) epilogue(jb, row, n0 + n, v);
             else y[(int64_t)n * OUT + row] = v;
         }
@@ -279,26 +497,33 @@ int launch_sb6_dequant(const uint8_t* qblk, const uint8_t* qsqm, const uint16_t*
     });
 }
 
+// sb6 tile kernel for xbits 0..2 and 1 or up to 4 activation rows
+template <typename TX, bool EP>
+static void sb6_tile_launch(int xbits, int r, int blocks, cudaStream_t st, const TX* x, const uint8_t* qblk,
+                            const uint8_t* qsqm, const __half* ddm, float* y, int OUT, int IN, const GemvJob& jb,
+                            int n0) {
+#define SB6T(RR, XBB) sb6_gemv_tile_kernel<TX, RR, EP, XBB><<<blocks, TG_T, 0, st>>>(x, qblk, qsqm, ddm, y, OUT, IN, r, jb, n0)
+    if (r == 1) {
+        if (xbits == 0) SB6T(1, 0); else if (xbits == 1) SB6T(1, 1); else SB6T(1, 2);
+    } else {
+        if (xbits == 0) SB6T(4, 0); else if (xbits == 1) SB6T(4, 1); else SB6T(4, 2);
+    }
+#undef SB6T
+}
+
 int launch_sb6_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_t* qsqm,
                     const uint16_t* ddm, float* y, int rows, int OUT, int IN, int xbits,
                     cudaStream_t st) {
     const size_t xe = xdtype == RWKV_F32 ? 4 : 2;
+    const int blocks = ceil_div(OUT, TG_T / tg_tpr(IN));
     return dispatch_dtype(xdtype, [&]<typename TX>() {
         for (int n0 = 0; n0 < rows; n0 += 4) {
             const int r = min(4, rows - n0);
             const TX* xp = (const TX*)((const char*)x + (size_t)n0 * IN * xe);
             float* yp = y + (size_t)n0 * OUT;
-            const int blocks = ceil_div(OUT, 8);
-            switch (r) {
-#define SB6C(RR)                                                                         \
-    case RR:                                                                             \
-        sb6_gemv_kernel<TX, RR><<<blocks, 256, 0, st>>>(xp, qblk, qsqm, (const __half*)ddm, \
-                                                        yp, OUT, IN, xbits, GemvJob{}, 0); \
-        break;
-                SB6C(1) SB6C(2) SB6C(3) SB6C(4)
-#undef SB6C
-            }
-            int rc = check_launch("sb6_gemv_kernel");
+            sb6_tile_launch<TX, false>(xbits, r, blocks, st, xp, qblk, qsqm, (const __half*)ddm, yp, OUT, IN,
+                                       GemvJob{}, 0);
+            int rc = check_launch("sb6_gemv_tile_kernel");
             if (rc) return rc;
         }
         return ok();
@@ -330,22 +555,33 @@ int launch_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
                     const uint16_t* d, float* y, int nn, int OUT, int IN, int bits, int out_per,
                     cudaStream_t st) {
     const size_t xe = xdtype == RWKV_F32 ? 4 : 2;
-    const int NK = OUT / out_per;
+    const int NK = OUT / out_per, rpc = TG_T / tg_tpr(IN);
+    const bool tiled = out_per % rpc == 0;  // every CTA's rows inside one fused matrix
     return dispatch_dtype(xdtype, [&]<typename TX>() {
         for (int n0 = 0; n0 < nn; n0 += 4) {
             const int r = min(4, nn - n0);
             const TX* xp = (const TX*)((const char*)x + (size_t)n0 * NK * IN * xe);
             float* yp = y + (size_t)n0 * OUT;
-            const int blocks = ceil_div(OUT, 8);
-            switch (r) {
+            if (tiled) {
+                const int blocks = ceil_div(OUT, rpc);
+                if (r == 1)
+                    sym_gemv_tile_kernel<TX, 1, false><<<blocks, TG_T, 0, st>>>(
+                        xp, qblk, (const int8_t*)qs, (const __half*)d, yp, OUT, IN, bits, out_per, r, GemvJob{}, 0);
+                else
+                    sym_gemv_tile_kernel<TX, 4, false><<<blocks, TG_T, 0, st>>>(
+                        xp, qblk, (const int8_t*)qs, (const __half*)d, yp, OUT, IN, bits, out_per, r, GemvJob{}, 0);
+            } else {
+                const int blocks = ceil_div(OUT, 8);
+                switch (r) {
 #define SYMC(RR)                                                                             \
     case RR:                                                                                 \
         sym_gemv_kernel<TX, RR><<<blocks, 256, 0, st>>>(xp, qblk, (const int8_t*)qs,        \
                                                         (const __half*)d, yp, OUT, IN, bits, \
                                                         out_per, GemvJob{}, 0);              \
         break;
-                SYMC(1) SYMC(2) SYMC(3) SYMC(4)
+                    SYMC(1) SYMC(2) SYMC(3) SYMC(4)
 #undef SYMC
+                }
             }
             int rc = check_launch("sym_gemv_kernel");
             if (rc) return rc;
@@ -362,32 +598,26 @@ int launch_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
 int launch_rwkvq_job(int xdtype, const GemvJob& j, int R, cudaStream_t st) {
     const size_t xe = xdtype == RWKV_F32 ? 4 : 2;
     return dispatch_dtype(xdtype, [&]<typename TX>() {
-        const int blocks = ceil_div(j.OUT, 8);
+        const int blocks = ceil_div(j.OUT, TG_T / tg_tpr(j.IN));
         for (int n0 = 0; n0 < R; n0 += 4) {
             const int r = min(4, R - n0);
             const TX* xp = (const TX*)((const char*)j.x + (size_t)n0 * j.IN * xe);
+            const uint8_t* qb = (const uint8_t*)j.w;
             if (j.wfmt == WFMT_SB6) {
-                const uint8_t* qb = (const uint8_t*)j.w;
                 const uint8_t* qsqm = (const uint8_t*)j.scales;
                 const __half* ddm = (const __half*)j.biases;
-                switch (r) {
-#define SB6J(RR) \
-    case RR: sb6_gemv_kernel<TX, RR, true><<<blocks, 256, 0, st>>>(xp, qb, qsqm, ddm, nullptr, j.OUT, j.IN, j.wbits, j, n0); break;
-                    SB6J(1) SB6J(2) SB6J(3) SB6J(4)
-#undef SB6J
-                }
+                sb6_tile_launch<TX, true>(j.wbits, r, blocks, st, xp, qb, qsqm, ddm, nullptr, j.OUT, j.IN, j, n0);
             } else {
-                const uint8_t* qb = (const uint8_t*)j.w;
                 const int8_t* qs = (const int8_t*)j.scales;
                 const __half* d = (const __half*)j.biases;
-                switch (r) {
-#define SYMJ(RR) \
-    case RR: sym_gemv_kernel<TX, RR, true><<<blocks, 256, 0, st>>>(xp, qb, qs, d, nullptr, j.OUT, j.IN, j.wbits, j.OUT, j, n0); break;
-                    SYMJ(1) SYMJ(2) SYMJ(3) SYMJ(4)
-#undef SYMJ
-                }
+                if (r == 1)
+                    sym_gemv_tile_kernel<TX, 1, true><<<blocks, TG_T, 0, st>>>(xp, qb, qs, d, nullptr, j.OUT, j.IN,
+                                                                             j.wbits, j.OUT, r, j, n0);
+                else
+                    sym_gemv_tile_kernel<TX, 4, true><<<blocks, TG_T, 0, st>>>(xp, qb, qs, d, nullptr, j.OUT, j.IN,
+                                                                             j.wbits, j.OUT, r, j, n0);
             }
-            int rc = check_launch("rwkvq_gemv_kernel");
+            int rc = check_launch("rwkvq_gemv_tile_kernel");
             if (rc) return rc;
         }
         return ok();
