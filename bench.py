@@ -303,7 +303,9 @@ class GemvSuite:
         self.launches_per_step = len(self.MATS)
         # the dominant launch: the 65536 x 2048 head matrix
         self.dom_bytes = mat_bytes(*self.MATS[-1])
-        self.kernel = ("gemm_w4_kernel (mma.sync GEMV mode, exact per-group scaling), 65536x2048"
+        self.kernel = ("q4_gemv_stream_kernel (streaming CUDA-core GEMV, x staged once per CTA), 65536x2048"
+                       if R <= 2 else
+                       "gemm_w4_kernel (mma.sync GEMV mode, exact per-group scaling), 65536x2048"
                        if R <= 8 else "gemm_tc_kernel (tcgen05, TMA + TMEM), 65536x2048")
         self.h2d = sum(R * IN * 2 for _, IN in self.MATS)
         self.d2h = sum(R * OUT * 4 for OUT, _ in self.MATS)
@@ -415,6 +417,7 @@ class Decode15B:
         self.dom_bytes = (L * sum(v for k, v in self.family.items() if k != "gemm_head")
                           + self.family["gemm_head"]) / self.family_launches
         kern = ("gemm_tc_kernel<TC_Q4> (tcgen05 4-bit GEMM, TMA + TMEM)" if R > 8 else
+                "q4_gemv_stream_kernel (streaming CUDA-core 4-bit GEMV)" if R <= 2 else
                 "gemm_w4_kernel (mma.sync 4-bit GEMV mode)")
         self.kernel = (f"{kern}: r/k/v, o, key, value x {L} layers + head = {self.family_launches} "
                        "launches per step; per-launch time from the runtime's step profiler "

@@ -18,6 +18,7 @@
 #include <unordered_map>
 
 #include "gemm_dx.cuh"
+#include "gemv_stream.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_w4_wide.cuh"
 
@@ -344,6 +345,12 @@ int launch_q_gemm(int xdtype, const void* x, const uint32_t* wq, const void* sca
         if (sc->flag.take(st))
             return fail(RWKV_E_TIMEOUT, "rwkv_q_gemm: a tensor-core GEMM wait of an earlier call gave up; "
                                         "its outputs are not valid (flag cleared, nothing launched)");
+        // 1..2 rows: the streaming CUDA-core GEMV (gemv_stream.cuh)
+        if (q4_stream_eligible(jobs, 1, rows)) {
+            cudaError_t e = launch_q4_gemv_stream(jobs, 1, rows, sc->sm_count, false, st);
+            if (e != cudaSuccess) return fail(RWKV_E_CUDA, "q4_gemv_stream_kernel: %s", cudaGetErrorString(e));
+            return ok();
+        }
         // more than 8 rows: tcgen05 (TMA + TMEM) when the shapes allow it
         const TcPlan tp = plan_tc(TC_Q4, jobs, 1, rows, sc->sm_count);
         if (tp.ok) {

@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_w4_wide.cuh"
+#include "gemv_stream.cuh"
 #include "x070_kernels.cuh"
 #include "x070_persist.cuh"
 #include "x070_small.cuh"
@@ -639,6 +640,11 @@ struct X070 {
             }
         }
         if (f16act) {
+            // 1..2 rows of fp16 activations on the 4-bit base: the streaming CUDA-core GEMV
+            if (fmt == 0 && wf == WF_Q4 && !bf16act && q4_stream_eligible(jobs, nj, R)) {
+                cudaError_t e = launch_q4_gemv_stream(jobs, nj, R, sm_count, /*pdl=*/true, st);
+                return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "q4_gemv_stream: %s", cudaGetErrorString(e));
+            }
             const int tfmt = wf == WF_Q4 ? TC_Q4 : wf == WF_F16 ? TC_F16 : TC_BF16;
             const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
             if (tp.ok) {

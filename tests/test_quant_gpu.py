@@ -76,10 +76,12 @@ def test_dequant_bit_exact(cuda, oracle, rng, bits):
     assert torch.equal(gotbf, torch.from_numpy(want).to(torch.bfloat16).cuda())
 
 
-@pytest.mark.parametrize("OUT,IN", MATS)
-@pytest.mark.parametrize("rows", [1, 8])
+@pytest.mark.parametrize("OUT,IN", MATS + [(100, 768), (16, 128)])
+@pytest.mark.parametrize("rows", [1, 2, 8])
 def test_gemv_matches_exact_product(cuda, oracle, rng, OUT, IN, rows):
-    """fp16 activations, W ~ N(0, 0.02) quantised 4-bit g64."""
+    """fp16 activations, W ~ N(0, 0.02) quantised 4-bit g64.
+    1 and 2 rows take the streaming CUDA-core GEMV (row blocks off the grid,
+    fewer than 16 units per row, one window), 8 rows the mma.sync GEMV."""
     from swiftrwkv_b200 import quant as Q
     W, wq, sc, bi = make_affine(oracle, rng, OUT, IN)
     x = f16(rng.standard_normal((rows, IN)))

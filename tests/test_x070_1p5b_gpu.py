@@ -53,7 +53,7 @@ def model16(cuda, weights):
     m.close()
 
 
-@pytest.mark.parametrize("rows", [1, 8, 64, 256])
+@pytest.mark.parametrize("rows", [1, 2, 8, 64, 256])
 def test_1p5b_width_logits_match_oracle(model16, oracle16, rows):
     from oracle import x070_oracle as XO
     ids = XO.splitmix_ids(rows, 3, vocab=V, seed=rows)

@@ -22,10 +22,12 @@ def tiny(act, rows=4, n_layer=2, n_embd=128, vocab=64, seed=42):
 
 
 @pytest.mark.parametrize("act,tol", [("f32", 1e-4), ("f16", 2e-3)])
-def test_step_logits_match_oracle(cuda, act, tol):
+@pytest.mark.parametrize("rows", [1, 2, 4])
+def test_step_logits_match_oracle(cuda, act, tol, rows):
+    """1 and 2 rows of fp16 activations run the 4-bit projections on the
+    streaming CUDA-core GEMV, 4 rows on the mma.sync GEMV."""
     from oracle import x070_oracle as XO
-    m, ref = tiny(act)
-    rows = 4
+    m, ref = tiny(act, rows=rows)
     ids = XO.splitmix_ids(rows, 6)
     m.reset(rows)
     st = ref.new_state(rows)
