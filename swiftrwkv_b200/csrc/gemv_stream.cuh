@@ -8,9 +8,10 @@
 // job (jobs.j[blockIdx.y]).  All of x and its per-group sums are staged in
 // shared memory once per CTA; after that a thread only streams codes, one
 // 128-code unit per step (gemv_tile.cuh layout: TPR threads per output row,
-// RPC rows per block), the next step's unit loaded while this one is summed,
-// so loads stay in flight across row blocks; the TPR partials of a row meet
-// in a fixed shuffle tree.
+// RPC rows per block; TPR 64 for IN a multiple of 8192), the next step's
+// unit loaded while this one is summed, so loads stay in flight across row
+// blocks; the TPR partials of a row meet in a fixed shuffle tree (and, at
+// TPR 64, one add of the row's two warp sums).
 //
 // Codes become fp16 two at a time: the nibbles at bits 0-3 / 16-19 of a word
 // OR'd under the exponent of 1024 read 1024 + q, one HSUB2 takes 1024 off;
@@ -56,6 +57,12 @@ __device__ __forceinline__ void qs_codes8(uint32_t w, __half2 (&c)[4]) {
 // read two conflict-free wavefronts of 16-byte vectors).
 constexpr int QS_HU = 136;
 
+// Threads per output row: 64 when IN / 128 is a multiple of 64 (a row
+// spans two warps: one window, 4 rows per CTA, so the 2048 x 8192 shapes
+// launch 4x the CTAs and keep a whole matrix in flight), else gemv_tile.cuh's
+// choice (<= 16).
+__host__ __device__ __forceinline__ int qs_tpr(int IN) { return (IN / TG_UNIT) % 64 == 0 ? 64 : tg_tpr(IN); }
+
 // Shared memory for IN columns and R rows: x, then the group sums (fp32).
 __host__ __device__ __forceinline__ size_t qs_gs_off(int IN, int R) {
     return ((size_t)R * (IN / TG_UNIT) * QS_HU * 2 + 15) & ~(size_t)15;
@@ -69,8 +76,9 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
     extern __shared__ __align__(16) unsigned char smq[];
     const GemvJob& jb = jobs.j[blockIdx.y];
     const int OUT = jb.OUT, IN = jb.IN;
-    const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT, NW = IN / W;
+    const int TPR = qs_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT, NW = IN / W;
     const int NU = IN / TG_UNIT, RS = NU * QS_HU, NG = IN / 64;
+    __shared__ float red[2][TG_T / 32][R];  // TPR 64: the two warps' partials of a row
     __half* xh = reinterpret_cast<__half*>(smq);
     float* gs = reinterpret_cast<float*>(smq + qs_gs_off(IN, R));
     const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
@@ -166,12 +174,27 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
         }
         if (win == NW - 1) {  // the row block's last window: reduce the row, store, restart
             const int row = (blockIdx.x + (it / NW) * gridDim.x) * RPC + lr;
+            float v[R];
 #pragma unroll
             for (int n = 0; n < R; n++) {
-                float v = acc[n];
-                for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (u == 0 && row < OUT && n < rows) epilogue(jb, row, n, v);
+                v[n] = acc[n];
+                for (int o = min(TPR, 32) / 2; o > 0; o >>= 1) v[n] += __shfl_xor_sync(0xffffffffu, v[n], o);
                 acc[n] = 0.f;
+            }
+            if (TPR == 64) {  // two warps per row: meet in shared memory (double-buffered by row block)
+                float(&rb)[TG_T / 32][R] = red[(it / NW) & 1];
+                if ((tid & 31) == 0) {
+#pragma unroll
+                    for (int n = 0; n < R; n++) rb[tid >> 5][n] = v[n];
+                }
+                __syncthreads();
+#pragma unroll
+                for (int n = 0; n < R; n++) v[n] = rb[2 * lr][n] + rb[2 * lr + 1][n];
+            }
+            if (u == 0 && row < OUT) {
+#pragma unroll
+                for (int n = 0; n < R; n++)
+                    if (n < rows) epilogue(jb, row, n, v[n]);
             }
         }
     }
@@ -202,7 +225,7 @@ inline cudaError_t launch_q4_gemv_stream(const GemvJobs& jobs, int nj, int rows,
     int maxin = 0, maxrb = 0;
     for (int i = 0; i < nj; i++) {
         maxin = std::max(maxin, jobs.j[i].IN);
-        const int rpc = TG_T / tg_tpr(jobs.j[i].IN);
+        const int rpc = TG_T / qs_tpr(jobs.j[i].IN);
         maxrb = std::max(maxrb, (jobs.j[i].OUT + rpc - 1) / rpc);
     }
     const int R = rows <= 1 ? 1 : 2;
