@@ -248,4 +248,134 @@ inline cudaError_t launch_q4_gemv_stream(const GemvJobs& jobs, int nj, int rows,
     return R == 1 ? go(q4_gemv_stream_kernel<1>) : go(q4_gemv_stream_kernel<2>);
 }
 
+// ---- dense fp16 GEMV for 1..2 activation rows (the low-rank branches) ----
+//
+// y[n, o] = sum_k W[o, k] x[n, k], W fp16 [OUT, IN] (IN a multiple of 32),
+// x fp16, fp32 sums (products exact: fma.rn.f32.f16).  FS_TPR threads per
+// output row, each a 32-column chunk per step (four 16-byte loads), two
+// chunks in flight; the TPR partials of a row meet in a shuffle tree.  The
+// down projections (IN = C) put a warp on a row, the up projections (IN = the
+// rank, 32..128) 1-4 threads on a row, so every shape keeps its whole matrix
+// in flight in one round trip.  x is staged in shared memory once per CTA,
+// a 32-column chunk padded to 40 halves (80 bytes: the 32 lanes of a row read
+// conflict-free 16-byte vectors).
+constexpr int FS_CH = 40;
+
+// threads per row: the largest power of two <= 32 dividing IN / 32
+__host__ __device__ __forceinline__ int fs_tpr(int IN) {
+    const int nc = IN / 32;
+    int t = 32;
+    while (t > 1 && nc % t) t >>= 1;
+    return t;
+}
+__host__ __device__ __forceinline__ size_t f16_small_smem(int IN, int R) { return (size_t)R * (IN / 32) * FS_CH * 2; }
+
+template <int R>
+__global__ void __launch_bounds__(TG_T) f16_gemv_small_kernel(const GemvJobs jobs, int rows) {
+    extern __shared__ __align__(16) unsigned char smf[];
+    const GemvJob& jb = jobs.j[blockIdx.y];
+    const int OUT = jb.OUT, IN = jb.IN;
+    const int TPR = fs_tpr(IN), RPC = TG_T / TPR, NC = IN / 32, RS = NC * FS_CH;
+    __half* xh = reinterpret_cast<__half*>(smf);
+    const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
+    const int row0 = blockIdx.x * RPC;
+    if (tid == 0) pdl_trigger();
+    if (row0 >= OUT) {  // a smaller job of the launch: nothing here
+        pdl_wait();
+        return;
+    }
+    const __half* wr = (const __half*)jb.w + (int64_t)min(row0 + lr, OUT - 1) * IN;
+    uint4 wv[2][4];
+    auto ld = [&](int s, int c) {
+        const uint4* p = reinterpret_cast<const uint4*>(wr + c * 32);
+#pragma unroll
+        for (int v = 0; v < 4; v++) wv[s][v] = __ldg(p + v);
+    };
+    if (u < NC) ld(0, u);
+    if (u + TPR < NC) ld(1, u + TPR);
+    pdl_wait();
+    {  // stage x (16-byte vectors; the launcher checks the alignment)
+        const __half* x = (const __half*)jb.x;
+        const int nv = NC * 4;  // 16-byte vectors of a row
+        for (int e = tid; e < R * nv; e += TG_T) {
+            const int n = e / nv, q = e - n * nv;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (n < rows) v = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)n * jb.x_stride) + q);
+            *reinterpret_cast<uint4*>(xh + n * RS + (q >> 2) * FS_CH + (q & 3) * 8) = v;
+        }
+        __syncthreads();
+    }
+    float acc[R];
+#pragma unroll
+    for (int n = 0; n < R; n++) acc[n] = 0.f;
+    for (int c0 = u; c0 < NC; c0 += 2 * TPR) {
+#pragma unroll
+        for (int s = 0; s < 2; s++) {
+            const int c = c0 + s * TPR;
+            if (c < NC) {
+#pragma unroll
+                for (int v = 0; v < 4; v++) {
+                    const __half2 w01 = qs_u2h(wv[s][v].x), w23 = qs_u2h(wv[s][v].y);
+                    const __half2 w45 = qs_u2h(wv[s][v].z), w67 = qs_u2h(wv[s][v].w);
+#pragma unroll
+                    for (int n = 0; n < R; n++) {
+                        const uint4 xv = *reinterpret_cast<const uint4*>(xh + n * RS + c * FS_CH + v * 8);
+                        const __half2 x01 = qs_u2h(xv.x), x23 = qs_u2h(xv.y), x45 = qs_u2h(xv.z), x67 = qs_u2h(xv.w);
+                        float d = acc[n];
+                        d = fma_f16f32(__low2half(w01), __low2half(x01), d);
+                        d = fma_f16f32(__high2half(w01), __high2half(x01), d);
+                        d = fma_f16f32(__low2half(w23), __low2half(x23), d);
+                        d = fma_f16f32(__high2half(w23), __high2half(x23), d);
+                        d = fma_f16f32(__low2half(w45), __low2half(x45), d);
+                        d = fma_f16f32(__high2half(w45), __high2half(x45), d);
+                        d = fma_f16f32(__low2half(w67), __low2half(x67), d);
+                        d = fma_f16f32(__high2half(w67), __high2half(x67), d);
+                        acc[n] = d;
+                    }
+                }
+                if (c + 2 * TPR < NC) ld(s, c + 2 * TPR);  // this slot's next chunk
+            }
+        }
+    }
+    const int row = row0 + lr;
+#pragma unroll
+    for (int n = 0; n < R; n++) {
+        float v = acc[n];
+        for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (u == 0 && row < OUT && n < rows) epilogue(jb, row, n, v);
+    }
+}
+
+// Whether jobs[0..nj) (dense fp16 weights) can take f16_gemv_small_kernel at
+// `rows` activation rows: IN a multiple of 32, 16-byte aligned W rows and x.
+inline bool f16_small_eligible(const GemvJobs& jobs, int nj, int rows) {
+    if (rows < 1 || rows > QS_MAXR || nj < 1) return false;
+    for (int i = 0; i < nj; i++) {
+        const GemvJob& j = jobs.j[i];
+        if (j.IN % 32 || j.IN > 8192 || j.OUT < 1) return false;
+        if (((uintptr_t)j.w | (uintptr_t)j.x | (uintptr_t)(j.x_stride * 2)) & 15) return false;
+    }
+    return true;
+}
+
+inline cudaError_t launch_f16_gemv_small(const GemvJobs& jobs, int nj, int rows, bool pdl, cudaStream_t st) {
+    int maxin = 0, maxb = 0;
+    for (int i = 0; i < nj; i++) {
+        maxin = std::max(maxin, jobs.j[i].IN);
+        const int rpc = TG_T / fs_tpr(jobs.j[i].IN);
+        maxb = std::max(maxb, (jobs.j[i].OUT + rpc - 1) / rpc);
+    }
+    const int R = rows <= 1 ? 1 : 2;
+    const size_t smem = f16_small_smem(maxin, R);
+    const dim3 grid(maxb, nj);
+    auto go = [&](auto kern) {
+        if (!pdl) {
+            kern<<<grid, TG_T, smem, st>>>(jobs, rows);
+            return cudaGetLastError();
+        }
+        return launch_pdl(kern, grid, dim3(TG_T), smem, st, jobs, rows);
+    };
+    return R == 1 ? go(f16_gemv_small_kernel<1>) : go(f16_gemv_small_kernel<2>);
+}
+
 }  // namespace rwkv

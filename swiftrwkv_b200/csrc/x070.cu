@@ -645,6 +645,11 @@ struct X070 {
                 cudaError_t e = launch_q4_gemv_stream(jobs, nj, R, sm_count, /*pdl=*/true, st);
                 return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "q4_gemv_stream: %s", cudaGetErrorString(e));
             }
+            // and the dense fp16 low-rank branches: the small fp16 GEMV
+            if (fmt == 1 && wf == WF_F16 && !bf16act && f16_small_eligible(jobs, nj, R)) {
+                cudaError_t e = launch_f16_gemv_small(jobs, nj, R, /*pdl=*/true, st);
+                return e == cudaSuccess ? RWKV_OK : fail(RWKV_E_CUDA, "f16_gemv_small: %s", cudaGetErrorString(e));
+            }
             const int tfmt = wf == WF_Q4 ? TC_Q4 : wf == WF_F16 ? TC_F16 : TC_BF16;
             const TcPlan tp = plan_tc(tfmt, jobs, nj, R, sm_count);
             if (tp.ok) {
