@@ -90,21 +90,23 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
         return;
     }
     const int total = nblk * NW;
+    // the load stream: row block lrb, window lwin; soff indexes the unit's
+    // first (scale, bias) pair, 8 x soff its first code word
+    int lrb = blockIdx.x, lwin = 0, soff = 0;
+    auto set_row = [&]() { soff = min(lrb * RPC + lr, OUT - 1) * NG + 2 * u; };
     uint4 cw[4];
     __half2 s2, b2;
-    auto load = [&](int it) {
-        const int rb = blockIdx.x + (it / NW) * gridDim.x, win = it - (it / NW) * NW;
-        const int64_t row = min(rb * RPC + lr, OUT - 1);
-        const int c0 = win * W + u * TG_UNIT;
-        const uint4* src = reinterpret_cast<const uint4*>((const uint32_t*)jb.w + row * (IN / 8) + c0 / 8);
+    auto load = [&]() {
+        const uint4* src = reinterpret_cast<const uint4*>((const uint32_t*)jb.w + 8 * (int64_t)soff);
 #pragma unroll
         for (int v = 0; v < 4; v++) cw[v] = __ldg(src + v);
-        s2 = __ldg(reinterpret_cast<const __half2*>(jb.scales + row * NG + c0 / 64));
-        b2 = __ldg(reinterpret_cast<const __half2*>(jb.biases + row * NG + c0 / 64));
+        s2 = __ldg(reinterpret_cast<const __half2*>(jb.scales + soff));
+        b2 = __ldg(reinterpret_cast<const __half2*>(jb.biases + soff));
     };
-    load(0);
+    set_row();
+    load();
     pdl_wait();
-    {  // stage x (16-byte vectors when aligned), then the group sums
+    {  // stage x (16-byte vectors when aligned) permuted per 8 columns, then the group sums
         const __half* x = (const __half*)jb.x;
         const bool vec = (((uintptr_t)x | (uintptr_t)(jb.x_stride * 2)) & 15) == 0;
         const int nch = NU * 16;  // 16-byte chunks of a row
@@ -121,15 +123,19 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
                                    s16[4] | (uint32_t)s16[5] << 16, s16[6] | (uint32_t)s16[7] << 16);
                 }
             }
-            *reinterpret_cast<uint4*>(xh + n * RS + (ch >> 4) * QS_HU + (ch & 15) * 8) = v;
+            // (x0 x1)(x2 x3)(x4 x5)(x6 x7) -> (x0 x4)(x1 x5)(x2 x6)(x3 x7): pair j matches code pair j
+            const uint4 o = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632),
+                                       __byte_perm(v.y, v.w, 0x5410), __byte_perm(v.y, v.w, 0x7632));
+            *reinterpret_cast<uint4*>(xh + n * RS + (ch >> 4) * QS_HU + (ch & 15) * 8) = o;
         }
         __syncthreads();
         for (int e = tid; e < R * NG; e += TG_T) {
             const int n = e / NG, g = e - n * NG;
             const __half* p = xh + n * RS + (g >> 1) * QS_HU + (g & 1) * 64;
             float t = 0.f;
+            // column order: column c of a piece sits at slot 2 (c % 4) + c / 4
 #pragma unroll 16
-            for (int c = 0; c < 64; c++) t += __half2float(p[c]);
+            for (int c = 0; c < 64; c++) t += __half2float(p[(c & ~7) + 2 * (c & 3) + ((c >> 2) & 1)]);
             gs[e] = t;
         }
         __syncthreads();
@@ -137,12 +143,23 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
     float acc[R];
 #pragma unroll
     for (int n = 0; n < R; n++) acc[n] = 0.f;
+    int win = 0, crb = blockIdx.x;  // the compute stream's window and row block
     for (int it = 0; it < total; it++) {
         const uint32_t wd[16] = {cw[0].x, cw[0].y, cw[0].z, cw[0].w, cw[1].x, cw[1].y, cw[1].z, cw[1].w,
                                  cw[2].x, cw[2].y, cw[2].z, cw[2].w, cw[3].x, cw[3].y, cw[3].z, cw[3].w};
         const float sg[2] = {__low2float(s2), __high2float(s2)}, bg[2] = {__low2float(b2), __high2float(b2)};
-        if (it + 1 < total) load(it + 1);  // the next unit, in flight during this one
-        const int win = it % NW, unit = win * TPR + u;
+        if (it + 1 < total) {  // the next unit, in flight during this one
+            if (++lwin == NW) {
+                lwin = 0;
+                lrb += gridDim.x;
+                set_row();
+            } else {
+                soff += W / 64;
+            }
+            load();
+        }
+        const int unit = win * TPR + u;
+        const __half* xu = xh + unit * QS_HU;
 #pragma unroll
         for (int gq = 0; gq < 2; gq++) {
             float dv[R];
@@ -154,17 +171,13 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
                 qs_codes8(wd[8 * gq + i], c);
 #pragma unroll
                 for (int n = 0; n < R; n++) {
-                    const uint4 xv = *reinterpret_cast<const uint4*>(xh + n * RS + unit * QS_HU + gq * 64 + i * 8);
-                    const __half2 x01 = qs_u2h(xv.x), x23 = qs_u2h(xv.y), x45 = qs_u2h(xv.z), x67 = qs_u2h(xv.w);
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xu + n * RS + gq * 64 + i * 8);
+                    const __half2 xp[4] = {qs_u2h(xv.x), qs_u2h(xv.y), qs_u2h(xv.z), qs_u2h(xv.w)};
                     float d = dv[n];
-                    d = fma_f16f32(__low2half(c[0]), __low2half(x01), d);
-                    d = fma_f16f32(__low2half(c[1]), __high2half(x01), d);
-                    d = fma_f16f32(__low2half(c[2]), __low2half(x23), d);
-                    d = fma_f16f32(__low2half(c[3]), __high2half(x23), d);
-                    d = fma_f16f32(__high2half(c[0]), __low2half(x45), d);
-                    d = fma_f16f32(__high2half(c[1]), __high2half(x45), d);
-                    d = fma_f16f32(__high2half(c[2]), __low2half(x67), d);
-                    d = fma_f16f32(__high2half(c[3]), __high2half(x67), d);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) d = fma_f16f32(__low2half(c[j]), __low2half(xp[j]), d);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) d = fma_f16f32(__high2half(c[j]), __high2half(xp[j]), d);
                     dv[n] = d;
                 }
             }
@@ -173,7 +186,7 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
             for (int n = 0; n < R; n++) acc[n] = fmaf(sg[gq], dv[n], fmaf(bg[gq], gs[n * NG + g], acc[n]));
         }
         if (win == NW - 1) {  // the row block's last window: reduce the row, store, restart
-            const int row = (blockIdx.x + (it / NW) * gridDim.x) * RPC + lr;
+            const int row = crb * RPC + lr;
             float v[R];
 #pragma unroll
             for (int n = 0; n < R; n++) {
@@ -182,7 +195,7 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
                 acc[n] = 0.f;
             }
             if (TPR == 64) {  // two warps per row: meet in shared memory (double-buffered by row block)
-                float(&rb)[TG_T / 32][R] = red[(it / NW) & 1];
+                float(&rb)[TG_T / 32][R] = red[((crb - (int)blockIdx.x) / (int)gridDim.x) & 1];
                 if ((tid & 31) == 0) {
 #pragma unroll
                     for (int n = 0; n < R; n++) rb[tid >> 5][n] = v[n];
@@ -196,6 +209,10 @@ __global__ void __launch_bounds__(TG_T, R == 1 ? 4 : 3) q4_gemv_stream_kernel(co
                 for (int n = 0; n < R; n++)
                     if (n < rows) epilogue(jb, row, n, v[n]);
             }
+            win = 0;
+            crb += gridDim.x;
+        } else {
+            win++;
         }
     }
 }
@@ -212,6 +229,7 @@ inline bool q4_stream_eligible(const GemvJobs& jobs, int nj, int rows) {
     for (int i = 0; i < nj; i++) {
         const GemvJob& j = jobs.j[i];
         if (j.wfmt != WFMT_AFFINE || j.IN % TG_UNIT || j.OUT < 1) return false;
+        if ((int64_t)j.OUT * (j.IN / 64) >= (int64_t)1 << 31) return false;  // 32-bit (scale, bias) index
         if (((uintptr_t)j.w & 15) || (((uintptr_t)j.scales | (uintptr_t)j.biases) & 3)) return false;
         if (q4_stream_smem(j.IN, rows) > (size_t)QS_SMEM_MAX) return false;
     }
@@ -231,11 +249,14 @@ inline cudaError_t launch_q4_gemv_stream(const GemvJobs& jobs, int nj, int rows,
     const int R = rows <= 1 ? 1 : 2;
     const size_t smem = q4_stream_smem(maxin, R);
     auto go = [&](auto kern) {
-        static const cudaError_t attr =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QS_SMEM_MAX);
-        if (attr != cudaSuccess) return attr;
+        // both instances share one function-pointer type, so the opt-in is
+        // set per call (a host-side attribute, no device work)
+        cudaError_t e = smem > 48 * 1024
+                            ? cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QS_SMEM_MAX)
+                            : cudaSuccess;
+        if (e != cudaSuccess) return e;
         int occ = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, TG_T, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, TG_T, smem);
         if (e != cudaSuccess) return e;
         const int G = std::max(1, std::min(maxrb, std::max(1, occ) * sm_count / nj));
         const dim3 grid(G, nj);

@@ -76,7 +76,7 @@ def test_dequant_bit_exact(cuda, oracle, rng, bits):
     assert torch.equal(gotbf, torch.from_numpy(want).to(torch.bfloat16).cuda())
 
 
-@pytest.mark.parametrize("OUT,IN", MATS + [(100, 768), (16, 128)])
+@pytest.mark.parametrize("OUT,IN", MATS + [(100, 768), (16, 128), (300, 16384)])
 @pytest.mark.parametrize("rows", [1, 2, 8])
 def test_gemv_matches_exact_product(cuda, oracle, rng, OUT, IN, rows):
     """fp16 activations, W ~ N(0, 0.02) quantised 4-bit g64.
