@@ -354,18 +354,71 @@ class Decode15B:
     unit = "tok/s"
     L, C, V, PROMPT = 24, 2048, 65536, 128
 
-    def __init__(self, rows=64, prompt=128, decode_path="launches"):
+    # --base: the projection / head matrices' container.  q4: MLX affine 4-bit
+    # group 64 (config 4's QLoRA base); sb6 / sym6 / sym8: .rwkvq matrices kept
+    # native (rwkv_x070_set_param_rwkvq), the formats of the reference's
+    # published decode timings (docs/Inference.md:550-557: "compression" = sb6,
+    # "reduction" = sym); synthetic codes and scales.
+    BASES = {"q4": ("MLX affine 4-bit g64", None, 0),
+             "sb6": (".rwkvq sb6 5-bit (4 + 1 bit-plane, group 32; compression)", "sb6", 1),
+             "sym6": (".rwkvq sym 6-bit (reduction)", "sym", 6),
+             "sym8": (".rwkvq sym 8-bit (reduction)", "sym", 8)}
+
+    def __init__(self, rows=64, prompt=128, decode_path="launches", base="q4"):
         self.rows = rows
         self.PROMPT = prompt
         self.decode_path = decode_path
-        self.metric = (f"x070 1.5B 4-bit decode tok/s (generateBatch greedy, {rows} rows/GPU, "
+        self.base = base
+        self.base_label, self.rq_kind, self.rq_bits = self.BASES[base]
+        what = "4-bit" if base == "q4" else self.base_label
+        self.metric = (f"x070 1.5B {what} decode tok/s (generateBatch greedy, {rows} rows/GPU, "
                        "fp16 activations)")
+
+    def _matrices(self):
+        C, F, V = self.C, 4 * self.C, self.V
+        for l in range(self.L):
+            for n in ("tmix.r_proj", "tmix.k_proj", "tmix.v_proj", "tmix.o_proj"):
+                yield f"blocks.{l}.{n}.weight", C, C
+            yield f"blocks.{l}.cmix.key.weight", F, C
+            yield f"blocks.{l}.cmix.value.weight", C, F
+        yield "head.weight", V, C
+
+    def _set_rwkvq(self):
+        """Every projection and the head as native .rwkvq matrices (synthetic
+        codes, small positive scales); returns the bytes they replace and add."""
+        import ctypes
+        from swiftrwkv_b200 import _lib
+        rng = np.random.default_rng(SEED)
+        kind, bits = self.rq_kind, self.rq_bits
+        old = new = 0
+        for key, OUT, IN in self._matrices():
+            if kind == "sb6":
+                NB = IN // 32
+                b1 = rng.integers(0, 256, OUT * NB * (16 + 4 * bits), dtype=np.uint8)
+                b2 = rng.integers(0, 64, OUT * NB * 2, dtype=np.uint8)
+                b3 = (rng.random(OUT * (IN // 256) * 2) * 1e-3).astype(np.float16)
+                fmt = 1
+            else:
+                b1 = rng.integers(0, 256, OUT * IN if bits == 8 else OUT * IN // 32 * 24, dtype=np.uint8)
+                b2 = rng.integers(0, 128, OUT * IN // 16, dtype=np.uint8)
+                b3 = (rng.random(OUT * (IN // 256)) * 1e-4).astype(np.float16)
+                fmt = 2
+            args = []
+            for b in (b1, b2, b3):
+                args += [b.ctypes.data_as(ctypes.c_void_p), b.nbytes]
+            _lib.call("rwkv_x070_set_param_rwkvq", self.m.h, key.encode(), fmt, bits, *args)
+            old += OUT * IN * (0.5 + 4 / 64)
+            new += RwkvqGemvSuite.wbytes(kind, bits, OUT, IN)
+        return old, new
 
     def setup(self, torch, dev):
         from swiftrwkv_b200.x070 import X070Backbone, X070Config
         self.torch = torch
         cfg = X070Config(self.L, self.C, self.V)
         self.m = X070Backbone(cfg, max_rows=self.rows, act="f16").init_random(seed=SEED)
+        self.rq_bytes = (0, 0)
+        if self.rq_kind:
+            self.rq_bytes = self._set_rwkvq()
         self.m.set_decode_path(1 if self.decode_path == "persistent" else 0)
         self.stream = torch.cuda.Stream(device=dev)
         torch.cuda.set_stream(self.stream)
@@ -378,7 +431,7 @@ class Decode15B:
         H = self.C // 64
         self.state_bytes = self.rows * self.L * H * 64 * 64 * 4 * 2   # read + write
         shift_bytes = self.rows * self.L * self.C * 4 * 2 * 2
-        self.alg_bytes = self.m.weight_bytes + self.state_bytes + shift_bytes
+        self.alg_bytes = self.m.weight_bytes - self.rq_bytes[0] + self.rq_bytes[1] + self.state_bytes + shift_bytes
         self.units_per_step = self.rows
         self.launches_per_step = self.m.launches_per_step
         # e2e: the previous step's tokens go host -> device, this step's
@@ -406,6 +459,8 @@ class Decode15B:
         (r/k/v, o, key, value in every layer, and the head)."""
         R, C, F, V, L = self.rows, self.C, 4 * self.C, self.V, self.L
         q = lambda OUT, IN: OUT * IN * (0.5 + 4 / 64)
+        if self.rq_kind:
+            q = lambda OUT, IN: RwkvqGemvSuite.wbytes(self.rq_kind, self.rq_bits, OUT, IN)
         self.family = {
             "gemm_rkv": 3 * (q(C, C) + R * C * 2 + R * C * 4),
             "gemm_o": q(C, C) + R * C * 2 + R * C * 8,          # y += : read + write
@@ -419,6 +474,8 @@ class Decode15B:
         kern = ("gemm_tc_kernel<TC_Q4> (tcgen05 4-bit GEMM, TMA + TMEM)" if R > 8 else
                 "q4_gemv_stream_kernel (streaming CUDA-core 4-bit GEMV)" if R <= 2 else
                 "gemm_w4_kernel (mma.sync 4-bit GEMV mode)")
+        if self.rq_kind:
+            kern = f"{self.rq_kind}_gemv_tile_kernel (.rwkvq {self.base} GEMV, launches of up to 4 rows)"
         self.kernel = (f"{kern}: r/k/v, o, key, value x {L} layers + head = {self.family_launches} "
                        "launches per step; per-launch time from the runtime's step profiler "
                        "(rwkv_x070_profile_step: an event after every launch of a captured step)")
@@ -462,7 +519,7 @@ class Decode15B:
         return tot / n
 
     def cpu(self, seconds, rows=None):
-        return cpu_decode_tokps(self.L, self.C, self.V, seconds, rows or self.rows)
+        return cpu_decode_tokps(self.L, self.C, self.V, seconds, rows or self.rows, self.base)
 
 
 class StateTune29B:
@@ -554,20 +611,31 @@ class StateTune29B:
 _CPU_CACHE = {}
 
 
-def cpu_decode_tokps(L, C, V, seconds, rows=1):
-    """CPU oracle decode of `rows` rows at 1.5B shapes: one layer (its 4-bit
-    GEMVs on packed weights, the low-rank branches, WKV step + tail, all over
+def cpu_decode_tokps(L, C, V, seconds, rows=1, base="q4"):
+    """CPU oracle decode of `rows` rows at 1.5B shapes: one layer (its
+    projection GEMVs on packed weights -- 4-bit affine, or the .rwkvq sb6 / sym
+    GEMVs for those bases --, the low-rank branches, WKV step + tail, all over
     the rows) and the head GEMV are timed, and the step is extrapolated as L
     layers + head."""
     from oracle import oracle as O
     from oracle.x070_oracle import lora_ranks
-    key = (L, C, V)
+    key = (L, C, V, base)
     if key not in _CPU_CACHE:
         rng = np.random.default_rng(SEED)
         H, F = C // 64, 4 * C
         rk = lora_ranks(C)
+        _, kind, bits = Decode15B.BASES[base]
 
         def q(OUT, IN):
+            if kind == "sb6":
+                NB = IN // 32
+                return ("sb6", rng.integers(0, 256, (OUT, NB * (16 + 4 * bits)), dtype=np.uint8),
+                        rng.integers(0, 64, (OUT, NB * 2), dtype=np.uint8),
+                        (rng.random((OUT, NB // 8 * 2)) * 1e-3).astype(np.float16).view(np.uint16), OUT, IN, bits)
+            if kind == "sym":
+                return ("sym", rng.integers(0, 256, OUT * IN if bits == 8 else OUT * IN // 32 * 24, dtype=np.uint8),
+                        rng.integers(0, 128, OUT * IN // 16, dtype=np.uint8),
+                        (rng.random(OUT * (IN // 256)) * 1e-4).astype(np.float16).view(np.uint16), OUT, IN, bits)
             W = (rng.standard_normal((OUT, IN)) * 0.02).astype(np.float16).astype(np.float32)
             return O.affine_quantize(W)
 
@@ -583,22 +651,34 @@ def cpu_decode_tokps(L, C, V, seconds, rows=1):
     return _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head, rows)
 
 
+def _cpu_gemv(x, m):
+    """One projection on the oracle: 4-bit affine (wq, scales, biases) or a
+    .rwkvq ("sb6" | "sym", codes, scales, d, OUT, IN, bits) matrix."""
+    from oracle import oracle as O
+    if m[0] == "sb6":
+        return np.stack([O.sb6_gemv(xr, *m[1:]) for xr in np.atleast_2d(x)])
+    if m[0] == "sym":
+        return O.sym_gemv(np.atleast_2d(x), *m[1:])
+    return O.affine_gemv(x, *m)
+
+
 def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head, rows):
     from oracle import oracle as O
     ones, zeros = np.ones(C, np.float32), np.zeros(C, np.float32)
 
     def layer():
-        rr = O.affine_gemv(x, *mats["r"])
-        kk = O.affine_gemv(x, *mats["k"])
-        vv = O.affine_gemv(x, *mats["v"])
+        rr = _cpu_gemv(x, mats["r"])
+        kk = _cpu_gemv(x, mats["k"])
+        vv = _cpu_gemv(x, mats["v"])
         hs = {n: (x @ lora[n][0].T) @ lora[n][1].T for n in "wavg"}
         wd = np.exp(-0.606531 / (1 + np.exp(-hs["w"]))).astype(np.float32)
         y, _ = O.wkv7_step(*(t.reshape(rows, H, 64) for t in (rr, wd, kk, vv, -kk, kk)), state)
         t = O.wkv_tail(y.reshape(rows, C), rr, kk, vv, ones, ones, zeros, hs["g"].astype(np.float32), H, 64)
-        o = O.affine_gemv(t, *mats["o"])
-        hk = np.maximum(O.affine_gemv(x + o, *mats["key"]), 0)
-        return O.affine_gemv(hk * hk, *mats["value"])
+        o = _cpu_gemv(t, mats["o"])
+        hk = np.maximum(_cpu_gemv(x + o, mats["key"]), 0)
+        return _cpu_gemv(hk * hk, mats["value"])
 
+    layer()  # untimed: first-touch of the packed matrices, thread-pool start
     t0 = time.perf_counter()
     n = 0
     while time.perf_counter() - t0 < seconds / 2 or n == 0:
@@ -608,7 +688,7 @@ def _cpu_decode_time(L, seconds, C, H, mats, lora, state, x, head, rows):
     t0 = time.perf_counter()
     m = 0
     while time.perf_counter() - t0 < seconds / 4 or m == 0:
-        O.affine_gemv(x, *head)
+        _cpu_gemv(x, head)
         m += 1
     t_head = (time.perf_counter() - t0) / m
     return rows / (L * t_layer + t_head), (f"{rows} rows; {n} timed x070 1.5B layers + {m} head GEMVs "
@@ -864,7 +944,7 @@ def run_reference(args, rank):
             per.append(v)
     if wl.name == "decode":
         config.update({"model": "x070 1.5B (L=24 C=2048 H=32 V=65536 FFN=8192)", "rows_per_gpu": wl.rows,
-                       "global_batch": wl.rows * world, "base": "MLX affine 4-bit g64"})
+                       "global_batch": wl.rows * world, "base": wl.base_label})
     value = statistics.median(per)
     out = {"impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -960,7 +1040,7 @@ def config3_line(torch, dev, args, peaks):
 
 def make_workload(args):
     if args.workload == "decode":
-        return Decode15B(args.rows or 64, args.prompt, args.decode_path)
+        return Decode15B(args.rows or 64, args.prompt, args.decode_path, args.base)
     if args.workload == "gemv":
         return GemvSuite(args.rows or 1)
     if args.workload == "gemv_rwkvq":
@@ -982,6 +1062,9 @@ def main():
     ap.add_argument("--decode-path", default="launches", choices=["launches", "persistent"],
                     help="decode: one graph of per-op launches (default) or the persistent one-launch step "
                          "(9..64 rows, fp16 activations, 4-bit base)")
+    ap.add_argument("--base", default="q4", choices=sorted(Decode15B.BASES),
+                    help="decode: the projection / head container (q4: MLX affine 4-bit g64, default; "
+                         "sb6 / sym6 / sym8: native .rwkvq matrices)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -1085,7 +1168,7 @@ def main():
         result["config"]["decode_path"] = "persistent" if wl.persistent else "launches"
         result["config"].update({"model": "x070 1.5B (L=24 C=2048 H=32 V=65536 FFN=8192)",
                                  "rows_per_gpu": wl.rows, "global_batch": wl.rows * world,
-                                 "prompt": wl.PROMPT, "base": "MLX affine 4-bit g64"})
+                                 "prompt": wl.PROMPT, "base": wl.base_label})
     if wl.name == "decode" and world == 1:
         result["prefill"] = wkv_prefill_line(torch, dev, args, peaks, flush_l2)
         result["config3"] = config3_line(torch, dev, args, peaks)
