@@ -655,9 +655,10 @@ def _cpu_gemv(x, m):
     """One projection on the oracle: 4-bit affine (wq, scales, biases) or a
     .rwkvq ("sb6" | "sym", codes, scales, d, OUT, IN, bits) matrix."""
     from oracle import oracle as O
-    if m[0] == "sb6":
+    kind = m[0] if isinstance(m[0], str) else "q4"
+    if kind == "sb6":
         return np.stack([O.sb6_gemv(xr, *m[1:]) for xr in np.atleast_2d(x)])
-    if m[0] == "sym":
+    if kind == "sym":
         return O.sym_gemv(np.atleast_2d(x), *m[1:])
     return O.affine_gemv(x, *m)
 
