@@ -73,13 +73,23 @@ __global__ void sb6_dequant_kernel(const uint8_t* __restrict__ qblk, const uint8
 
 template <typename TX, int R, bool EP, int XB>
 __global__ void __launch_bounds__(TG_T)
-sb6_gemv_tile_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk, const uint8_t* __restrict__ qsqm,
-                     const __half* __restrict__ ddm, float* __restrict__ y, int OUT, int IN, int rows,
-                     const GemvJob jb, int n0) {
+sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk_, const uint8_t* __restrict__ qsqm_,
+                     const __half* __restrict__ ddm_, float* __restrict__ y, int OUT_, int IN_, int rows,
+                     const GemvJobs jobs, int n0) {
     constexpr int xbits = XB;
     __shared__ __align__(16) float xs[R * TG_RS];
     __shared__ float bs[R * 16 * TG_UNIT / 32];
+    // EP: the matrix, activations and epilogue of job blockIdx.y (a runtime
+    // projection); else the arguments
+    const GemvJob& jb = jobs.j[blockIdx.y];
+    const int OUT = EP ? jb.OUT : OUT_, IN = EP ? jb.IN : IN_;
+    const int64_t xstride = EP ? (int64_t)jb.x_stride : (int64_t)IN;
+    const TX* __restrict__ x = EP ? (const TX*)jb.x + n0 * xstride : x_;
+    const uint8_t* __restrict__ qblk = EP ? (const uint8_t*)jb.w : qblk_;
+    const uint8_t* __restrict__ qsqm = EP ? (const uint8_t*)jb.scales : qsqm_;
+    const __half* __restrict__ ddm = EP ? jb.biases : ddm_;
     const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT;
+    if ((int)blockIdx.x * RPC >= OUT) return;  // a smaller job of the launch
     const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
     const int row = blockIdx.x * RPC + lr;
     const int NB = IN / 32, NSB = NB / 8;
@@ -89,7 +99,7 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
 #pragma unroll
     for (int n = 0; n < R; n++) acc[n] = 0.f;
     for (int k0 = 0; k0 < IN; k0 += W) {
-        tg_stage<TX, R, 32>(x, IN, k0, W, rows, xs, bs);
+        tg_stage<TX, R, 32>(x, xstride, k0, W, rows, xs, bs);
         const int blk0 = (k0 + u * TG_UNIT) / 32;  // first of the unit's 4 blocks
         const uint4* src = reinterpret_cast<const uint4*>(qblk + (rowc * NB + blk0) * BB);
         uint32_t wd[24];
@@ -163,22 +173,33 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk,
 // vectors); x of matrix xi = row / out_per (every row of a CTA in one matrix).
 template <typename TX, int R, bool EP>
 __global__ void __launch_bounds__(TG_T)
-sym_gemv_tile_kernel(const TX* __restrict__ x, const uint8_t* __restrict__ qblk, const int8_t* __restrict__ qs,
-                     const __half* __restrict__ d, float* __restrict__ y, int OUT, int IN, int bits, int out_per,
-                     int rows, const GemvJob jb, int n0) {
+sym_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk_, const int8_t* __restrict__ qs_,
+                     const __half* __restrict__ d_, float* __restrict__ y, int OUT_, int IN_, int bits_, int out_per_,
+                     int rows, const GemvJobs jobs, int n0) {
     __shared__ __align__(16) float xs[R * TG_RS];
     __shared__ float bs[R * 16 * TG_UNIT / 16];
+    // EP: the matrix, activations and epilogue of job blockIdx.y (a runtime
+    // projection, one matrix per job); else the arguments
+    const GemvJob& jb = jobs.j[blockIdx.y];
+    const int OUT = EP ? jb.OUT : OUT_, IN = EP ? jb.IN : IN_, bits = EP ? jb.wbits : bits_;
+    const int out_per = EP ? jb.OUT : out_per_;
+    const TX* __restrict__ x = EP ? (const TX*)jb.x + n0 * (int64_t)jb.x_stride : x_;
+    const uint8_t* __restrict__ qblk = EP ? (const uint8_t*)jb.w : qblk_;
+    const int8_t* __restrict__ qs = EP ? (const int8_t*)jb.scales : qs_;
+    const __half* __restrict__ d = EP ? jb.biases : d_;
     const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT;
+    if ((int)blockIdx.x * RPC >= OUT) return;  // a smaller job of the launch
     const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
     const int row = blockIdx.x * RPC + lr;
     const int NB = IN / 16, NSB = IN / 256, NK = OUT / out_per, xi = (blockIdx.x * RPC) / out_per;
     const int64_t rowc = min(row, OUT - 1);
     const TX* xm = x + (int64_t)xi * IN;
+    const int64_t xstride = EP ? (int64_t)jb.x_stride : (int64_t)NK * IN;
     float acc[R];
 #pragma unroll
     for (int n = 0; n < R; n++) acc[n] = 0.f;
     for (int k0 = 0; k0 < IN; k0 += W) {
-        tg_stage<TX, R, 16>(xm, (int64_t)NK * IN, k0, W, rows, xs, bs);
+        tg_stage<TX, R, 16>(xm, xstride, k0, W, rows, xs, bs);
         const int blk0 = (k0 + u * TG_UNIT) / 16;  // first of the unit's 8 16-blocks
         const int cu = u * TG_UNIT;                 // the unit's column inside the window
         const uint2 q8 = __ldg(reinterpret_cast<const uint2*>(qs + rowc * NB + blk0));
@@ -442,17 +463,23 @@ int launch_sb6_dequant(const uint8_t* qblk, const uint8_t* qsqm, const uint16_t*
 }
 
 // sb6 tile kernel for xbits 0..2 and 1 or up to 4 activation rows
+// (EP: grid.y jobs of one format)
 template <typename TX, bool EP>
-static void sb6_tile_launch(int xbits, int r, int blocks, cudaStream_t st, const TX* x, const uint8_t* qblk,
-                            const uint8_t* qsqm, const __half* ddm, float* y, int OUT, int IN, const GemvJob& jb,
-                            int n0) {
-#define SB6T(RR, XBB) sb6_gemv_tile_kernel<TX, RR, EP, XBB><<<blocks, TG_T, 0, st>>>(x, qblk, qsqm, ddm, y, OUT, IN, r, jb, n0)
+static cudaError_t sb6_tile_launch(int xbits, int r, dim3 grid, cudaStream_t st, const TX* x, const uint8_t* qblk,
+                                   const uint8_t* qsqm, const __half* ddm, float* y, int OUT, int IN,
+                                   const GemvJobs& jobs, int n0) {
+    auto go = [&](auto kern) {
+        kern<<<grid, TG_T, 0, st>>>(x, qblk, qsqm, ddm, y, OUT, IN, r, jobs, n0);
+        return cudaGetLastError();
+    };
     if (r == 1) {
-        if (xbits == 0) SB6T(1, 0); else if (xbits == 1) SB6T(1, 1); else SB6T(1, 2);
-    } else {
-        if (xbits == 0) SB6T(4, 0); else if (xbits == 1) SB6T(4, 1); else SB6T(4, 2);
+        if (xbits == 0) return go(sb6_gemv_tile_kernel<TX, 1, EP, 0>);
+        if (xbits == 1) return go(sb6_gemv_tile_kernel<TX, 1, EP, 1>);
+        return go(sb6_gemv_tile_kernel<TX, 1, EP, 2>);
     }
-#undef SB6T
+    if (xbits == 0) return go(sb6_gemv_tile_kernel<TX, 4, EP, 0>);
+    if (xbits == 1) return go(sb6_gemv_tile_kernel<TX, 4, EP, 1>);
+    return go(sb6_gemv_tile_kernel<TX, 4, EP, 2>);
 }
 
 int launch_sb6_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_t* qsqm,
@@ -465,8 +492,8 @@ int launch_sb6_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
             const int r = min(4, rows - n0);
             const TX* xp = (const TX*)((const char*)x + (size_t)n0 * IN * xe);
             float* yp = y + (size_t)n0 * OUT;
-            sb6_tile_launch<TX, false>(xbits, r, blocks, st, xp, qblk, qsqm, (const __half*)ddm, yp, OUT, IN,
-                                       GemvJob{}, 0);
+            sb6_tile_launch<TX, false>(xbits, r, dim3(blocks), st, xp, qblk, qsqm, (const __half*)ddm, yp, OUT, IN,
+                                       GemvJobs{}, 0);
             int rc = check_launch("sb6_gemv_tile_kernel");
             if (rc) return rc;
         }
@@ -510,10 +537,10 @@ int launch_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
                 const int blocks = ceil_div(OUT, rpc);
                 if (r == 1)
                     sym_gemv_tile_kernel<TX, 1, false><<<blocks, TG_T, 0, st>>>(
-                        xp, qblk, (const int8_t*)qs, (const __half*)d, yp, OUT, IN, bits, out_per, r, GemvJob{}, 0);
+                        xp, qblk, (const int8_t*)qs, (const __half*)d, yp, OUT, IN, bits, out_per, r, GemvJobs{}, 0);
                 else
                     sym_gemv_tile_kernel<TX, 4, false><<<blocks, TG_T, 0, st>>>(
-                        xp, qblk, (const int8_t*)qs, (const __half*)d, yp, OUT, IN, bits, out_per, r, GemvJob{}, 0);
+                        xp, qblk, (const int8_t*)qs, (const __half*)d, yp, OUT, IN, bits, out_per, r, GemvJobs{}, 0);
             } else {
                 const int blocks = ceil_div(OUT, 8);
                 switch (r) {
@@ -539,30 +566,33 @@ int launch_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
 // (the reference's sym kernel takes up to 4, its sb6 kernel 1), with the job's
 // epilogue (activation, fp16 / fp32 / += output).  x rows are contiguous
 // (x_stride == IN); xdtype is the activation type.
-int launch_rwkvq_job(int xdtype, const GemvJob& j, int R, cudaStream_t st) {
-    const size_t xe = xdtype == RWKV_F32 ? 4 : 2;
+// Runtime projections on .rwkvq matrices: jobs of one format (WFMT_SB6 with
+// one xbits, or WFMT_SYM with one bit width), fp16 / bf16 / fp32 activations
+// with the jobs' row strides, up to 4 rows per launch, grid.y = the jobs.
+// (Plain launches: as programmatic dependents the early CTAs, parked at the
+// wait, took the previous kernel's SM slots -- sym 6-bit decode at 1 row
+// 1.17 -> 1.47 ms.)
+int launch_rwkvq_jobs(int xdtype, const GemvJobs& jobs, int nj, int R, cudaStream_t st) {
+    int blocks = 0;
+    for (int i = 0; i < nj; i++) blocks = std::max(blocks, ceil_div(jobs.j[i].OUT, TG_T / tg_tpr(jobs.j[i].IN)));
+    const dim3 grid(blocks, nj);
+    const GemvJob& j0 = jobs.j[0];
     return dispatch_dtype(xdtype, [&]<typename TX>() {
-        const int blocks = ceil_div(j.OUT, TG_T / tg_tpr(j.IN));
         for (int n0 = 0; n0 < R; n0 += 4) {
             const int r = min(4, R - n0);
-            const TX* xp = (const TX*)((const char*)j.x + (size_t)n0 * j.IN * xe);
-            const uint8_t* qb = (const uint8_t*)j.w;
-            if (j.wfmt == WFMT_SB6) {
-                const uint8_t* qsqm = (const uint8_t*)j.scales;
-                const __half* ddm = (const __half*)j.biases;
-                sb6_tile_launch<TX, true>(j.wbits, r, blocks, st, xp, qb, qsqm, ddm, nullptr, j.OUT, j.IN, j, n0);
+            cudaError_t e;
+            if (j0.wfmt == WFMT_SB6) {
+                e = sb6_tile_launch<TX, true>(j0.wbits, r, grid, st, nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0,
+                                              jobs, n0);
             } else {
-                const int8_t* qs = (const int8_t*)j.scales;
-                const __half* d = (const __half*)j.biases;
-                if (r == 1)
-                    sym_gemv_tile_kernel<TX, 1, true><<<blocks, TG_T, 0, st>>>(xp, qb, qs, d, nullptr, j.OUT, j.IN,
-                                                                             j.wbits, j.OUT, r, j, n0);
-                else
-                    sym_gemv_tile_kernel<TX, 4, true><<<blocks, TG_T, 0, st>>>(xp, qb, qs, d, nullptr, j.OUT, j.IN,
-                                                                             j.wbits, j.OUT, r, j, n0);
+                auto go = [&](auto kern) {
+                    kern<<<grid, TG_T, 0, st>>>((const TX*)nullptr, (const uint8_t*)nullptr, (const int8_t*)nullptr,
+                                                (const __half*)nullptr, (float*)nullptr, 0, 0, 0, 1, r, jobs, n0);
+                    return cudaGetLastError();
+                };
+                e = r == 1 ? go(sym_gemv_tile_kernel<TX, 1, true>) : go(sym_gemv_tile_kernel<TX, 4, true>);
             }
-            int rc = check_launch("rwkvq_gemv_tile_kernel");
-            if (rc) return rc;
+            if (e != cudaSuccess) return fail(RWKV_E_CUDA, "rwkvq_gemv_tile_kernel: %s", cudaGetErrorString(e));
         }
         return ok();
     });
