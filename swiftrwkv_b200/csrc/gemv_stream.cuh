@@ -275,9 +275,8 @@ inline cudaError_t launch_q4_gemv_stream(const GemvJobs& jobs, int nj, int rows,
 // x fp16, fp32 sums (products exact: fma.rn.f32.f16).  FS_TPR threads per
 // output row, each a 32-column chunk per step (four 16-byte loads), two
 // chunks in flight; the TPR partials of a row meet in a shuffle tree.  The
-// down projections (IN = C) put a warp on a row, the up projections (IN = the
-// rank, 32..128) 1-4 threads on a row, so every shape keeps its whole matrix
-// in flight in one round trip.  x is staged in shared memory once per CTA,
+// down projections (IN = C) put a warp on a row, so the whole matrix is in
+// flight in one round trip.  x is staged in shared memory once per CTA,
 // a 32-column chunk padded to 40 halves (80 bytes: the 32 lanes of a row read
 // conflict-free 16-byte vectors).
 constexpr int FS_CH = 40;
@@ -368,12 +367,14 @@ __global__ void __launch_bounds__(TG_T) f16_gemv_small_kernel(const GemvJobs job
 }
 
 // Whether jobs[0..nj) (dense fp16 weights) can take f16_gemv_small_kernel at
-// `rows` activation rows: IN a multiple of 32, 16-byte aligned W rows and x.
+// `rows` activation rows: IN a multiple of 32 and at least 256, 16-byte
+// aligned W rows and x.  (The up projections, whose IN is the rank, stay on
+// the mma.sync GEMV: 1-row decode 0.93 ms with them here, 0.89 without.)
 inline bool f16_small_eligible(const GemvJobs& jobs, int nj, int rows) {
     if (rows < 1 || rows > QS_MAXR || nj < 1) return false;
     for (int i = 0; i < nj; i++) {
         const GemvJob& j = jobs.j[i];
-        if (j.IN % 32 || j.IN > 8192 || j.OUT < 1) return false;
+        if (j.IN % 32 || j.IN < 256 || j.IN > 8192 || j.OUT < 1) return false;
         if (((uintptr_t)j.w | (uintptr_t)j.x | (uintptr_t)(j.x_stride * 2)) & 15) return false;
     }
     return true;
