@@ -196,6 +196,11 @@ int rwkv_wkv7_step_tail(const float* r, const float* w, const float* k, const fl
 
 /* y[n, o] = sum_i x[n, i] * W[o, i]   (quantizedMM with transpose: true).
  * x: [rows, IN] in xdtype; y: [rows, OUT] in ydtype; accumulation in fp32.
+ * fp16 x on the 4-bit group-64 container: 1-2 rows on the streaming CUDA-core
+ * GEMV (IN % 128 == 0), 3-8 rows on the mma.sync GEMV -- both MLX's
+ * matrix-vector numerics, scale * sum(q x) + bias * sum(x) per group --, more
+ * rows on the tcgen05 GEMM over the weight dequantised into fp16 (MLX's
+ * quantized-matmul numerics).
  * Replaces the quantizedMM call of X070Backbone.baseProj
  * (Sources/RWKVGen/X070Backbone.swift:678-681) and RwkvqNativeWeight
  * (Sources/RWKVQuant/RwkvqNative.swift:48-51). */
