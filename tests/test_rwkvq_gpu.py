@@ -99,6 +99,10 @@ def test_native_rwkvq_matrices_match_oracle(cuda, oracle, rng, tmp_path, rows, a
     tensors, deq = {}, {}
     plan = {  # x070 name: (world name, kind, bits, OUT, IN)
         "blocks.0.tmix.r_proj.weight": ("blocks.0.att.receptance.weight", "sb6", 0, C, C),
+        # r and k of layer 0, k and v of layer 1 share a format: one launch at 1 row
+        "blocks.0.tmix.k_proj.weight": ("blocks.0.att.key.weight", "sb6", 0, C, C),
+        "blocks.1.tmix.r_proj.weight": ("blocks.1.att.receptance.weight", "sym", 6, C, C),
+        "blocks.1.tmix.k_proj.weight": ("blocks.1.att.key.weight", "sb6", 1, C, C),
         "blocks.0.tmix.o_proj.weight": ("blocks.0.att.output.weight", "sym", 8, C, C),
         "blocks.0.cmix.key.weight": ("blocks.0.ffn.key.weight", "sym", 6, 4 * C, C),
         "blocks.1.cmix.value.weight": ("blocks.1.ffn.value.weight", "sb6", 2, C, 4 * C),
