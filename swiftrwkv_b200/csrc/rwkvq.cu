@@ -71,6 +71,61 @@ __global__ void sb6_dequant_kernel(const uint8_t* __restrict__ qblk, const uint8
     for (int c = 0; c < 32; c++) o[c] = from_f<TO>((float)nib[c] * s + m);
 }
 
+// One 128-code sb6 unit (4 blocks of 32, NV words each: 16 bytes of nibbles
+// + xbits bit-planes of 4 bytes) of an output row against R staged rows:
+// per block s = half(qs * d), m = half(qm * dm), acc += s * sum(q x) + m *
+// sum(x), codes summed in column order.  xs: staged rows (xidx layout, RS
+// floats per row); bs: block sums (BSR per row); cu: the unit's first column.
+template <int R, int XB>
+__device__ __forceinline__ void sb6_unit(const uint32_t (&wd)[24], uint2 sq, __half2 dd, const float* xs, int RS,
+                                         const float* bs, int BSR, int cu, float (&acc)[R]) {
+    constexpr int xbits = XB, NV = (16 + 4 * XB) / 4;
+    const float d = __low2float(dd), dm = __high2float(dd);
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        const uint32_t pair = (b < 2 ? sq.x : sq.y) >> (16 * (b & 1));
+        const float s = rnd_half((float)(pair & 0xFF) * d);
+        const float m = rnd_half((float)(int8_t)(pair >> 8) * dm);
+        const int wb = b * NV;  // the block's first word: NV words per block
+        const uint32_t qh = xbits >= 1 ? wd[wb + 4] : 0u, qh2 = xbits >= 2 ? wd[wb + 5] : 0u;
+        const int cb = cu + 32 * b;  // column of the block in the staged rows
+        // the block's 32 codes as floats, column order (bytes j: low nibble col j, high col j + 16)
+        float q[32];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t nw = wd[wb + i];
+            uint32_t lo = nw & 0x0F0F0F0Fu, hi = (nw >> 4) & 0x0F0F0F0Fu;
+            if (xbits >= 1) {
+                lo |= spread4(qh >> (4 * i)) << 4;
+                hi |= spread4(qh >> (16 + 4 * i)) << 4;
+            }
+            if (xbits >= 2) {
+                lo |= spread4(qh2 >> (4 * i)) << 5;
+                hi |= spread4(qh2 >> (16 + 4 * i)) << 5;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                q[4 * i + k] = code_f(lo, k);
+                q[16 + 4 * i + k] = code_f(hi, k);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < R; n++) {
+            const float* xb = xs + n * RS + xidx(cb);  // the block: 32 contiguous floats
+            float dv = 0.f;
+#pragma unroll
+            for (int c4 = 0; c4 < 8; c4++) {
+                const float4 xv = reinterpret_cast<const float4*>(xb)[c4];
+                dv = fmaf(xv.x, q[4 * c4], dv);
+                dv = fmaf(xv.y, q[4 * c4 + 1], dv);
+                dv = fmaf(xv.z, q[4 * c4 + 2], dv);
+                dv = fmaf(xv.w, q[4 * c4 + 3], dv);
+            }
+            acc[n] = fmaf(s, dv, fmaf(m, bs[n * BSR + cb / 32], acc[n]));
+        }
+    }
+}
+
 template <typename TX, int R, bool EP, int XB>
 __global__ void __launch_bounds__(TG_T)
 sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk_, const uint8_t* __restrict__ qsqm_,
@@ -112,50 +167,7 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
         }
         const uint2 sq = __ldg(reinterpret_cast<const uint2*>(qsqm + 2 * (rowc * NB + blk0)));
         const __half2 dd = __ldg(reinterpret_cast<const __half2*>(ddm) + rowc * NSB + blk0 / 8);
-        const float d = __low2float(dd), dm = __high2float(dd);
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-            const uint32_t pair = (b < 2 ? sq.x : sq.y) >> (16 * (b & 1));
-            const float s = rnd_half((float)(pair & 0xFF) * d);
-            const float m = rnd_half((float)(int8_t)(pair >> 8) * dm);
-            const int wb = b * NV;  // the block's first word: NV words per block
-            const uint32_t qh = xbits >= 1 ? wd[wb + 4] : 0u, qh2 = xbits >= 2 ? wd[wb + 5] : 0u;
-            const int cb = u * TG_UNIT + 32 * b;  // column of the block inside the window
-            // the block's 32 codes as floats, column order (bytes j: low nibble col j, high col j + 16)
-            float q[32];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t nw = wd[wb + i];
-                uint32_t lo = nw & 0x0F0F0F0Fu, hi = (nw >> 4) & 0x0F0F0F0Fu;
-                if (xbits >= 1) {
-                    lo |= spread4(qh >> (4 * i)) << 4;
-                    hi |= spread4(qh >> (16 + 4 * i)) << 4;
-                }
-                if (xbits >= 2) {
-                    lo |= spread4(qh2 >> (4 * i)) << 5;
-                    hi |= spread4(qh2 >> (16 + 4 * i)) << 5;
-                }
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    q[4 * i + k] = code_f(lo, k);
-                    q[16 + 4 * i + k] = code_f(hi, k);
-                }
-            }
-#pragma unroll
-            for (int n = 0; n < R; n++) {
-                const float* xb = xs + n * TG_RS + xidx(cb);  // the block: 32 contiguous floats
-                float dv = 0.f;
-#pragma unroll
-                for (int c4 = 0; c4 < 8; c4++) {
-                    const float4 xv = reinterpret_cast<const float4*>(xb)[c4];
-                    dv = fmaf(xv.x, q[4 * c4], dv);
-                    dv = fmaf(xv.y, q[4 * c4 + 1], dv);
-                    dv = fmaf(xv.z, q[4 * c4 + 2], dv);
-                    dv = fmaf(xv.w, q[4 * c4 + 3], dv);
-                }
-                acc[n] = fmaf(s, dv, fmaf(m, bs[n * (W / 32) + cb / 32], acc[n]));
-            }
-        }
+        sb6_unit<R, XB>(wd, sq, dd, xs, TG_RS, bs, W / 32, u * TG_UNIT, acc);
         __syncthreads();  // the window may be overwritten
     }
 #pragma unroll
