@@ -449,9 +449,9 @@ int rwkv_x070_profile_step(rwkv_x070_t model, int rows, float* ms_host, int cap,
  * The arithmetic is the per-kernel path's for the row count (the exact
  * dequantised weight up to 8 rows, the fp16-dequantised weight above); sums
  * are grouped differently.  On the 1.5B step the persistent kernels are the
- * slower (1 row 1.48 vs 1.37 ms, 8 rows 1.87 vs 1.52 ms, 64 rows 2.70 vs
- * 2.11 ms), hence the default.  rwkv_x070_decode_path returns 1 when a step on `rows` rows takes
- * the persistent kernel.  No counterpart in the reference (MLX schedules the
+ * slower (1 row 1.48 vs 0.89 ms, 8 rows 1.87 vs 1.52 ms, 64 rows 2.70 vs
+ * 2.11 ms), hence the default.  rwkv_x070_decode_path returns 1 when a step
+ * on `rows` rows takes the persistent kernel.  No counterpart in the reference (MLX schedules the
  * reference's kernels). */
 int rwkv_x070_set_decode_path(rwkv_x070_t model, int path);
 /* The raw %globaltimer trace of the last rwkv_x070_profile_step that ran the
