@@ -71,8 +71,8 @@ def measured_traffic(wl):
     ncu capture summarised in profiles/traffic.json for this workload and row
     count; None when no capture covers it."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
-    if not os.path.exists(p):
-        return None
+    if not os.path.exists(p) or getattr(wl, "rq_kind", None) or getattr(wl, "persistent", False):
+        return None  # the captures cover the 4-bit per-op kernels only
     with open(p) as f:
         d = json.load(f)
     e = d.get(wl.name, {}).get(str(getattr(wl, "rows", "")))
