@@ -750,7 +750,7 @@ class RwkvqGemvSuite:
         self.launches_per_step = len(self.jobs) * ((R + 3) // 4)
         self.dom = self.jobs[-1]  # sym 8-bit head
         self.dom_bytes = mb(*self.dom[:4])
-        self.kernel = "sym_gemv_kernel (8-bit), 65536x2048"
+        self.kernel = "sym_gemv_tile_kernel (8-bit), 65536x2048"
         self.h2d = sum(R * j[3] * 2 for j in self.jobs)
         self.d2h = sum(R * j[2] * 4 for j in self.jobs)
         self.pin_x = [torch.empty((R, j[3]), dtype=torch.float16).pin_memory() for j in self.jobs]
