@@ -126,14 +126,17 @@ __device__ __forceinline__ void sb6_unit(const uint32_t (&wd)[24], uint2 sq, __h
     }
 }
 
-template <typename TX, int R, bool EP, int XB>
+// TM: the most threads (128-code units) per output row and window: 16, or 32
+// for the runtime's one-row launches (8192-column rows then take two windows
+// and twice the CTAs).
+template <typename TX, int R, bool EP, int XB, int TM = 16>
 __global__ void __launch_bounds__(TG_T)
 sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk_, const uint8_t* __restrict__ qsqm_,
                      const __half* __restrict__ ddm_, float* __restrict__ y, int OUT_, int IN_, int rows,
                      const GemvJobs jobs, int n0) {
     constexpr int xbits = XB;
-    __shared__ __align__(16) float xs[R * TG_RS];
-    __shared__ float bs[R * 16 * TG_UNIT / 32];
+    __shared__ __align__(16) float xs[R * TM * TG_USTR];
+    __shared__ float bs[R * TM * TG_UNIT / 32];
     // EP: the matrix, activations and epilogue of job blockIdx.y (a runtime
     // projection); else the arguments
     const GemvJob& jb = jobs.j[blockIdx.y];
@@ -143,7 +146,7 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
     const uint8_t* __restrict__ qblk = EP ? (const uint8_t*)jb.w : qblk_;
     const uint8_t* __restrict__ qsqm = EP ? (const uint8_t*)jb.scales : qsqm_;
     const __half* __restrict__ ddm = EP ? jb.biases : ddm_;
-    const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT;
+    const int TPR = tg_tpr(IN, TM), RPC = TG_T / TPR, W = TPR * TG_UNIT;
     if ((int)blockIdx.x * RPC >= OUT) return;  // a smaller job of the launch
     const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
     const int row = blockIdx.x * RPC + lr;
@@ -154,7 +157,7 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
 #pragma unroll
     for (int n = 0; n < R; n++) acc[n] = 0.f;
     for (int k0 = 0; k0 < IN; k0 += W) {
-        tg_stage<TX, R, 32>(x, xstride, k0, W, rows, xs, bs);
+        tg_stage<TX, R, 32>(x, xstride, k0, W, rows, xs, bs, TM * TG_USTR);
         const int blk0 = (k0 + u * TG_UNIT) / 32;  // first of the unit's 4 blocks
         const uint4* src = reinterpret_cast<const uint4*>(qblk + (rowc * NB + blk0) * BB);
         uint32_t wd[24];
@@ -167,7 +170,7 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
         }
         const uint2 sq = __ldg(reinterpret_cast<const uint2*>(qsqm + 2 * (rowc * NB + blk0)));
         const __half2 dd = __ldg(reinterpret_cast<const __half2*>(ddm) + rowc * NSB + blk0 / 8);
-        sb6_unit<R, XB>(wd, sq, dd, xs, TG_RS, bs, W / 32, u * TG_UNIT, acc);
+        sb6_unit<R, XB>(wd, sq, dd, xs, TM * TG_USTR, bs, W / 32, u * TG_UNIT, acc);
         __syncthreads();  // the window may be overwritten
     }
 #pragma unroll
@@ -183,13 +186,13 @@ sb6_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
 
 // sym: a unit is 8 16-blocks (8-bit: 8 vectors) or 4 32-code pairs (6-bit: 6
 // vectors); x of matrix xi = row / out_per (every row of a CTA in one matrix).
-template <typename TX, int R, bool EP>
+template <typename TX, int R, bool EP, int TM = 16>
 __global__ void __launch_bounds__(TG_T)
 sym_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk_, const int8_t* __restrict__ qs_,
                      const __half* __restrict__ d_, float* __restrict__ y, int OUT_, int IN_, int bits_, int out_per_,
                      int rows, const GemvJobs jobs, int n0) {
-    __shared__ __align__(16) float xs[R * TG_RS];
-    __shared__ float bs[R * 16 * TG_UNIT / 16];
+    __shared__ __align__(16) float xs[R * TM * TG_USTR];
+    __shared__ float bs[R * TM * TG_UNIT / 16];
     // EP: the matrix, activations and epilogue of job blockIdx.y (a runtime
     // projection, one matrix per job); else the arguments
     const GemvJob& jb = jobs.j[blockIdx.y];
@@ -199,7 +202,7 @@ sym_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
     const uint8_t* __restrict__ qblk = EP ? (const uint8_t*)jb.w : qblk_;
     const int8_t* __restrict__ qs = EP ? (const int8_t*)jb.scales : qs_;
     const __half* __restrict__ d = EP ? jb.biases : d_;
-    const int TPR = tg_tpr(IN), RPC = TG_T / TPR, W = TPR * TG_UNIT;
+    const int TPR = tg_tpr(IN, TM), RPC = TG_T / TPR, W = TPR * TG_UNIT;
     if ((int)blockIdx.x * RPC >= OUT) return;  // a smaller job of the launch
     const int tid = threadIdx.x, lr = tid / TPR, u = tid - lr * TPR;
     const int row = blockIdx.x * RPC + lr;
@@ -211,7 +214,7 @@ sym_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
 #pragma unroll
     for (int n = 0; n < R; n++) acc[n] = 0.f;
     for (int k0 = 0; k0 < IN; k0 += W) {
-        tg_stage<TX, R, 16>(xm, xstride, k0, W, rows, xs, bs);
+        tg_stage<TX, R, 16>(xm, xstride, k0, W, rows, xs, bs, TM * TG_USTR);
         const int blk0 = (k0 + u * TG_UNIT) / 16;  // first of the unit's 8 16-blocks
         const int cu = u * TG_UNIT;                 // the unit's column inside the window
         const uint2 q8 = __ldg(reinterpret_cast<const uint2*>(qs + rowc * NB + blk0));
@@ -236,7 +239,7 @@ sym_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
                 }
 #pragma unroll
                 for (int n = 0; n < R; n++) {
-                    const float* xb = xs + n * TG_RS + xidx(cu + 16 * b);  // 16 contiguous floats
+                    const float* xb = xs + n * (TM * TG_USTR) + xidx(cu + 16 * b);  // 16 contiguous floats
                     float dv = 0.f;
 #pragma unroll
                     for (int c4 = 0; c4 < 4; c4++) {
@@ -279,7 +282,7 @@ sym_gemv_tile_kernel(const TX* __restrict__ x_, const uint8_t* __restrict__ qblk
                 }
 #pragma unroll
                 for (int n = 0; n < R; n++) {
-                    const float* xp = xs + n * TG_RS + xidx(cu + 32 * p);  // the pair: 32 contiguous floats
+                    const float* xp = xs + n * (TM * TG_USTR) + xidx(cu + 32 * p);  // the pair: 32 contiguous floats
                     float dv0 = 0.f, dv1 = 0.f;
 #pragma unroll
                     for (int c = 0; c < 16; c++) {
@@ -476,7 +479,7 @@ int launch_sb6_dequant(const uint8_t* qblk, const uint8_t* qsqm, const uint16_t*
 
 // sb6 tile kernel for xbits 0..2 and 1 or up to 4 activation rows
 // (EP: grid.y jobs of one format)
-template <typename TX, bool EP>
+template <typename TX, bool EP, int TM = 16>
 static cudaError_t sb6_tile_launch(int xbits, int r, dim3 grid, cudaStream_t st, const TX* x, const uint8_t* qblk,
                                    const uint8_t* qsqm, const __half* ddm, float* y, int OUT, int IN,
                                    const GemvJobs& jobs, int n0) {
@@ -485,9 +488,9 @@ static cudaError_t sb6_tile_launch(int xbits, int r, dim3 grid, cudaStream_t st,
         return cudaGetLastError();
     };
     if (r == 1) {
-        if (xbits == 0) return go(sb6_gemv_tile_kernel<TX, 1, EP, 0>);
-        if (xbits == 1) return go(sb6_gemv_tile_kernel<TX, 1, EP, 1>);
-        return go(sb6_gemv_tile_kernel<TX, 1, EP, 2>);
+        if (xbits == 0) return go(sb6_gemv_tile_kernel<TX, 1, EP, 0, TM>);
+        if (xbits == 1) return go(sb6_gemv_tile_kernel<TX, 1, EP, 1, TM>);
+        return go(sb6_gemv_tile_kernel<TX, 1, EP, 2, TM>);
     }
     if (xbits == 0) return go(sb6_gemv_tile_kernel<TX, 4, EP, 0>);
     if (xbits == 1) return go(sb6_gemv_tile_kernel<TX, 4, EP, 1>);
@@ -585,8 +588,12 @@ int launch_sym_gemv(int xdtype, const void* x, const uint8_t* qblk, const uint8_
 // wait, took the previous kernel's SM slots -- sym 6-bit decode at 1 row
 // 1.17 -> 1.47 ms.)
 int launch_rwkvq_jobs(int xdtype, const GemvJobs& jobs, int nj, int R, cudaStream_t st) {
+    // one row: up to 32 threads per output row (two windows and twice the CTAs
+    // for 8192-column rows); more rows: up to 16 (the window staged per row)
+    const int tm = R == 1 ? 32 : 16;
     int blocks = 0;
-    for (int i = 0; i < nj; i++) blocks = std::max(blocks, ceil_div(jobs.j[i].OUT, TG_T / tg_tpr(jobs.j[i].IN)));
+    for (int i = 0; i < nj; i++)
+        blocks = std::max(blocks, ceil_div(jobs.j[i].OUT, TG_T / tg_tpr(jobs.j[i].IN, tm)));
     const dim3 grid(blocks, nj);
     const GemvJob& j0 = jobs.j[0];
     return dispatch_dtype(xdtype, [&]<typename TX>() {
@@ -594,15 +601,18 @@ int launch_rwkvq_jobs(int xdtype, const GemvJobs& jobs, int nj, int R, cudaStrea
             const int r = min(4, R - n0);
             cudaError_t e;
             if (j0.wfmt == WFMT_SB6) {
-                e = sb6_tile_launch<TX, true>(j0.wbits, r, grid, st, nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0,
-                                              jobs, n0);
+                e = R == 1 ? sb6_tile_launch<TX, true, 32>(j0.wbits, r, grid, st, nullptr, nullptr, nullptr, nullptr,
+                                                           nullptr, 0, 0, jobs, n0)
+                           : sb6_tile_launch<TX, true>(j0.wbits, r, grid, st, nullptr, nullptr, nullptr, nullptr,
+                                                       nullptr, 0, 0, jobs, n0);
             } else {
                 auto go = [&](auto kern) {
                     kern<<<grid, TG_T, 0, st>>>((const TX*)nullptr, (const uint8_t*)nullptr, (const int8_t*)nullptr,
                                                 (const __half*)nullptr, (float*)nullptr, 0, 0, 0, 1, r, jobs, n0);
                     return cudaGetLastError();
                 };
-                e = r == 1 ? go(sym_gemv_tile_kernel<TX, 1, true>) : go(sym_gemv_tile_kernel<TX, 4, true>);
+                e = R == 1 ? go(sym_gemv_tile_kernel<TX, 1, true, 32>) : r == 1 ? go(sym_gemv_tile_kernel<TX, 1, true>)
+                                                                           : go(sym_gemv_tile_kernel<TX, 4, true>);
             }
             if (e != cudaSuccess) return fail(RWKV_E_CUDA, "rwkvq_gemv_tile_kernel: %s", cudaGetErrorString(e));
         }
